@@ -1,0 +1,153 @@
+// Internal host-side structures shared by the translation units of libammon_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <functional>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "ammon_b200.h"
+
+namespace ab {
+
+// ---- errors -----------------------------------------------------------------------
+// Every C entry point catches ab::Error and turns it into a status + thread-local text.
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] inline void fail(int code, const std::string& msg) { throw Error(code, msg); }
+[[noreturn]] inline void invalid(const std::string& msg) { fail(AB_ERR_VALIDATION, msg); }
+
+void set_last_error(const std::string& msg);
+
+inline void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        fail(AB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Runs fn, mapping exceptions to a status code.
+template <class F>
+int guard(F&& fn) {
+    try {
+        fn();
+        return AB_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("host allocation failed");
+        return AB_ERR_ARGUMENT;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return AB_ERR_ARGUMENT;
+    }
+}
+
+// ---- tensors -------------------------------------------------------------------------
+inline size_t dtype_size(int32_t dt) {
+    switch (dt) {
+        case AB_F32: return 4;
+        case AB_BF16: return 2;
+        case AB_U32: return 4;
+        default: fail(AB_ERR_ARGUMENT, "unknown dtype " + std::to_string(dt));
+    }
+}
+
+inline const char* dtype_name(int32_t dt) {
+    switch (dt) {
+        case AB_F32: return "f32";
+        case AB_BF16: return "bf16";
+        case AB_U32: return "u32";
+        default: return "?";
+    }
+}
+
+inline uint64_t numel(const ab_tensor& t) {
+    uint64_t n = 1;
+    for (int i = 0; i < t.rank; i++) n *= t.dims[i];
+    return n;
+}
+
+inline uint64_t nbytes(const ab_tensor& t) { return numel(t) * dtype_size(t.dtype); }
+
+std::string shape_str(const ab_tensor& t);
+
+// Contract checks with the reference's message vocabulary ("parameter `x`",
+// "expected rank N", symbolic dim names in backticks).
+void expect_rank(const char* param, const ab_tensor& t, int rank);
+void expect_rank_in(const char* param, const ab_tensor& t, int lo, int hi);
+void expect_dtype(const char* param, const ab_tensor& t, int32_t dt);
+void expect_float(const char* param, const ab_tensor& t);
+void expect_dim(const char* param, const ab_tensor& t, int axis, const char* sym, uint64_t want);
+void expect_data(const char* param, const ab_tensor& t);
+// Step parcel [n, 2] u32 with n >= need.
+uint32_t expect_step(const ab_tensor& step, uint32_t need);
+
+// ---- runtime -----------------------------------------------------------------------
+struct Runtime {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t* flags = nullptr;  // device word: bit flags raised by kernels
+    void activate() const;      // cudaSetDevice(device)
+    void check_flags();         // reads + clears the flag word, throws AB_ERR_DEVICE
+};
+
+enum DeviceFlag : uint32_t {
+    kFlagTokenRange = 1u,
+    kFlagPositionRange = 2u,
+    kFlagWaitTimeout = 4u,
+};
+
+// ---- schemes -------------------------------------------------------------------------
+using LaunchFn = std::function<cudaError_t(cudaStream_t)>;
+
+struct Node {
+    std::string label;
+    LaunchFn launch;
+};
+
+struct Scheme {
+    Runtime* rt = nullptr;
+    std::vector<Node> nodes;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool dirty = true;
+    bool use_graph = true;
+    uint32_t records = 0;
+    uint32_t replays = 0;
+    void add(const char* label, LaunchFn fn) {
+        nodes.push_back(Node{label, std::move(fn)});
+        dirty = true;
+    }
+    void release_graph();
+};
+
+// Launch with optional programmatic dependent launch (PDL): the kernel may begin while
+// its predecessor drains; kernels call griddepcontrol.wait before reading predecessor
+// outputs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl,
+                   void (*kernel)(KArgs...), Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? attr : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+}  // namespace ab
+
+struct ab_runtime : ab::Runtime {};
+struct ab_scheme : ab::Scheme {};

@@ -1,0 +1,96 @@
+// Host-side interfaces of the fused decode kernels (gemv.cu, attention.cu).
+#pragma once
+
+#include "internal.h"
+
+namespace ab {
+
+struct Step;
+
+// Prologue applied to the activations a GEMV reads.
+enum GemvPro : int {
+    kProNone = 0,  // x is used as given (f32 or bf16, converted to the weight type)
+    kProNorm = 1,  // x (f32) is RMS-normalised with a gain vector first
+};
+
+// Epilogue applied to each pair of output rows (2u, 2u + 1).
+enum GemvEpi : int {
+    kEpiStore = 0,     // out[b, r] = y
+    kEpiQkv = 1,       // rows of [wq; wk; wv]: RoPE on q and k, K/V appended to the cache
+    kEpiSwiglu = 2,    // rows (w1[u], w3[u]): out[b, u] = silu(y1) * y3
+    kEpiResidual = 3,  // out[b, r] += y (f32 residual stream)
+};
+
+// Parameters of one fused GEMV launch (plain old data; passed by value to the kernel).
+struct GemvParams {
+    // Virtual weight matrix: up to three row-major [rows, K] segments stacked, or two
+    // segments interleaved row by row (kEpiSwiglu).
+    const void* seg[3];
+    uint32_t seg_rows[3];
+    uint32_t n_rows;  // total virtual rows
+    uint32_t units;   // output pairs = ceil(n_rows / 2) (or rows of w1 for SwiGLU)
+    uint32_t K;
+    uint32_t nchunks;  // ceil(K / (32 * elements per 16 bytes))
+    uint32_t nb;       // live batch rows in this launch
+    // activations [nb, K]
+    const void* x;
+    int32_t x_dtype;
+    uint32_t x_stride;
+    const void* norm_w;
+    int32_t norm_dtype;
+    float eps;
+    // outputs
+    void* out;
+    int32_t out_dtype;
+    uint32_t out_stride;
+    // kEpiQkv
+    float* q;
+    uint32_t qd, kvd, head, seq;
+    float theta;
+    void* kcache;
+    void* vcache;
+    int32_t kv_dtype;
+    uint64_t cache_stride;  // elements between consecutive batch rows of the cache
+    const Step* step;
+    uint32_t* flags;
+};
+
+// Records one fused GEMV (weights of dtype wdtype) over batch rows [0, batch).
+void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, uint32_t batch,
+                 int pro, int epi);
+
+// Whether the fused GEMV can run on these shapes (K vector-aligned, rows 16-byte aligned).
+bool gemv_fusable(int32_t wdtype, uint32_t K, const void* const* segs, int nseg);
+
+// Parameters of the fused flash-decoding attention launch.
+struct AttnParams {
+    const float* q;      // [B, H, hd] (rotated)
+    const void* kcache;  // [B, S, KV, hd]
+    const void* vcache;
+    int32_t kv_dtype;
+    uint64_t cache_stride;  // elements between batch rows of the cache
+    void* out;              // [B, H * hd]
+    int32_t out_dtype;
+    uint32_t heads, kv_heads, head, seq, batch;
+    uint32_t nsplit;
+    float* part_o;   // [B, KV, nsplit, g, hd]
+    float* part_ml;  // [B, KV, nsplit, g, 2]
+    uint32_t* counters;  // [B, KV], zero between launches
+    const Step* step;
+    uint32_t* flags;
+};
+
+// Scratch (floats for part_o + part_ml, counters) the fused attention needs.
+void attention_scratch_size(uint32_t batch, uint32_t heads, uint32_t head, uint32_t nsplit,
+                            uint64_t* floats, uint64_t* counters);
+uint32_t attention_choose_splits(uint32_t batch, uint32_t kv_heads, uint32_t seq, int sm_count,
+                                 uint32_t max_splits);
+bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t kv_dtype);
+void record_attention(ab_scheme* s, const char* label, AttnParams p);
+
+// Rejects batched shapes the single-row reference kernels cannot take.
+void record_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x);
+void record_rmsnorm_ref(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor o, float eps);
+void record_linear(ab_scheme* s, const char* label, ab_tensor weight, ab_tensor x, ab_tensor out);
+
+}  // namespace ab

@@ -1,0 +1,257 @@
+/*
+ * ammon_b200 — C ABI of the B200-native Ammon decode layer path.
+ *
+ * The entry points mirror the public API of the Ammon crate (src/lib.rs re-exports):
+ * a runtime (src/gpu.rs), record-then-replay schemes (Goldy's Scheme, used by every
+ * module's record()), the DecodeStep control parcel (src/kernels.rs:10-33), the
+ * kernels of src/kernels.rs, the modules of src/modules.rs, and the host decode
+ * loop (src/generate.rs, src/tokenizer.rs:179-189). Each declaration names the
+ * reference item it replaces.
+ *
+ * Conventions
+ *  - Every function returns an int status (AB_OK = 0). On failure ab_last_error()
+ *    returns a message for the calling thread. No C++ exception crosses the ABI.
+ *  - Record functions validate first. A rejected call adds no node to the scheme
+ *    (the reference's "IR node count unchanged" contract, tests/kernels.rs:125-146).
+ *  - Tensors are plain descriptors of contiguous row-major device memory. The caller
+ *    owns weights, activations and caches; modules own their scratch.
+ *  - Nothing runs at record time. ab_scheme_submit() replays the recorded work on the
+ *    runtime's stream as one CUDA graph; per-step data changes through
+ *    ab_step_deposit() without re-recording.
+ */
+#ifndef AMMON_B200_H
+#define AMMON_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status ------------------------------------------------------------- */
+#define AB_OK 0
+#define AB_ERR_VALIDATION 1 /* shape / dtype contract violated (GoldyError::Validation) */
+#define AB_ERR_CUDA 2       /* a CUDA runtime call failed */
+#define AB_ERR_ARGUMENT 3   /* null handle, bad enum, size out of range */
+#define AB_ERR_DEVICE 4     /* a kernel flagged an out-of-range token or position */
+#define AB_ERR_NCCL 5       /* a collective failed */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ab_last_error(void);
+
+/* ---- data types ---------------------------------------------------------- */
+typedef enum { AB_F32 = 0, AB_BF16 = 1, AB_U32 = 2 } ab_dtype;
+
+/* Contiguous row-major device tensor view (goldy::TensorView). rank 1..4. */
+typedef struct {
+    void* data;
+    int32_t dtype;
+    int32_t rank;
+    uint32_t dims[4];
+} ab_tensor;
+
+/* DecodeStep { token, position } (src/kernels.rs:10-15). A parcel of n of them is an
+ * AB_U32 tensor of dims [n, 2]; entry b drives batch row (stream) b. */
+typedef struct {
+    uint32_t token;
+    uint32_t position;
+} ab_decode_step;
+
+typedef struct ab_runtime ab_runtime;
+typedef struct ab_scheme ab_scheme;
+typedef struct ab_kvcache ab_kvcache;
+typedef struct ab_attention_block ab_attention_block;
+typedef struct ab_swiglu_block ab_swiglu_block;
+typedef struct ab_llama ab_llama;
+
+/* ---- runtime (src/gpu.rs:5-13 create_runtime) ---------------------------- */
+int ab_runtime_create(int32_t device, ab_runtime** out);
+int ab_runtime_destroy(ab_runtime* rt);
+/* Waits for the runtime stream; reports AB_ERR_DEVICE if a kernel flagged a bad index. */
+int ab_runtime_synchronize(ab_runtime* rt);
+/* The runtime's cudaStream_t, for callers that interleave their own work. */
+void* ab_runtime_stream(ab_runtime* rt);
+/* Number of SMs of the runtime's device. */
+int ab_runtime_sm_count(ab_runtime* rt, int32_t* out);
+
+/* ---- tensors (goldy::Tensor::zeros / from_f32 / host take) ---------------- */
+int ab_tensor_zeros(ab_runtime* rt, int32_t dtype, int32_t rank, const uint32_t* dims,
+                    ab_tensor* out);
+int ab_tensor_free(ab_runtime* rt, ab_tensor* t);
+/* Synchronous host -> device copy of `bytes` (must equal the tensor's size). */
+int ab_tensor_write(ab_runtime* rt, ab_tensor t, const void* host, uint64_t bytes);
+/* Waits for the runtime stream, then device -> host copy. */
+int ab_tensor_read(ab_runtime* rt, ab_tensor t, void* host, uint64_t bytes);
+/* Seeded synthetic values: mean + std * z with z an Irwin-Hall(12) deviate of a
+ * splitmix64 hash of (seed, stream, index). Bit-identical to the CPU generator used by
+ * the test oracle. f32 and bf16 tensors. */
+int ab_tensor_fill_normal(ab_runtime* rt, ab_tensor t, uint64_t seed, uint64_t stream,
+                          float mean, float std);
+/* goldy::TensorView::narrow(0, start, len) and reshape: host-side view arithmetic. */
+int ab_tensor_narrow(ab_tensor t, uint32_t start, uint32_t len, ab_tensor* out);
+int ab_tensor_reshape(ab_tensor t, int32_t rank, const uint32_t* dims, ab_tensor* out);
+
+/* ---- DecodeStep parcel (src/kernels.rs:17-33 parcel / deposit_target) ------- */
+/* Device parcel of n zeroed DecodeSteps (AB_U32, dims [n, 2]). Free with ab_tensor_free. */
+int ab_step_parcel(ab_runtime* rt, uint32_t n, ab_tensor* out);
+/* Deposit: upload n steps, ordered on the runtime stream before later submits
+ * (MemoryExchange::bind_deposit + write_data, tests/kernels.rs:202-210). */
+int ab_step_deposit(ab_runtime* rt, ab_tensor parcel, const ab_decode_step* steps, uint32_t n);
+
+/* ---- schemes (goldy::Scheme: record, submit, ir_node_count, replay_stats) ---- */
+int ab_scheme_create(ab_runtime* rt, ab_scheme** out);
+int ab_scheme_destroy(ab_scheme* s);
+/* Replays every recorded node on the runtime stream. The first submit after a record
+ * captures and instantiates a CUDA graph; later submits relaunch it. */
+int ab_scheme_submit(ab_scheme* s);
+int ab_scheme_node_count(const ab_scheme* s, uint32_t* out);
+/* records = graph instantiations, replays = submits. */
+int ab_scheme_replay_stats(const ab_scheme* s, uint32_t* records, uint32_t* replays);
+/* enable = 0 launches nodes directly on each submit (debugging); default 1 (graph). */
+int ab_scheme_use_graph(ab_scheme* s, int32_t enable);
+
+/* ---- kernels (src/kernels.rs; each records one dispatch) ------------------- */
+/* embed (src/kernels.rs:35-47): x[b, :] = table[step[b].token, :]. */
+int ab_kernel_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x);
+/* gemv (src/kernels.rs:49-73): serial-order xout[pos, i] = sum_j w[i, j] x[j]. */
+int ab_kernel_gemv(ab_scheme* s, ab_tensor x, ab_tensor w, ab_tensor xout, ab_tensor step);
+/* rmsnorm / rmsnorm_inplace (src/kernels.rs:75-128): one row per block, eps 1e-5. */
+int ab_kernel_rmsnorm(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor o);
+int ab_kernel_rmsnorm_inplace(ab_scheme* s, ab_tensor x, ab_tensor weight);
+/* rope (src/kernels.rs:130-172): rotates q [heads, head] and row pos of k [seq, kv, head]. */
+int ab_kernel_rope(ab_scheme* s, ab_tensor q, ab_tensor k, ab_tensor step, float theta);
+/* rope_store (src/kernels.rs:174-210). */
+int ab_kernel_rope_store(ab_scheme* s, ab_tensor q, ab_tensor k_proj, ab_tensor k,
+                         ab_tensor step, float theta);
+/* cache_store (src/kernels.rs:212-226). */
+int ab_kernel_cache_store(ab_scheme* s, ab_tensor src, ab_tensor dst, ab_tensor step);
+/* attention_partial / attention_combine (src/kernels.rs:228-410): flash-decoding with the
+ * reference's 8-position splits and partial layout [q_heads, splits, head + 2]. */
+int ab_kernel_attention_partial(ab_scheme* s, ab_tensor q, ab_tensor key_cache,
+                                ab_tensor value_cache, ab_tensor partial, ab_tensor step);
+int ab_kernel_attention_combine(ab_scheme* s, ab_tensor partial, ab_tensor xb, ab_tensor step);
+/* attention (src/kernels.rs:412-460): serial scores into att [q_heads, seq]. */
+int ab_kernel_attention(ab_scheme* s, ab_tensor q, ab_tensor att, ab_tensor xb,
+                        ab_tensor key_cache, ab_tensor value_cache, ab_tensor step);
+/* swiglu (src/kernels.rs:462-476): hb = silu(hb) * hb2. */
+int ab_kernel_swiglu(ab_scheme* s, ab_tensor hb, ab_tensor hb2);
+/* TensorKernels::add_into / matmul_into (src/kernels.rs:506-528). matmul: a is the
+ * weight [d_out, d_in], b is x [d_in] or [batch, d_in], out [d_out] or [batch, d_out]. */
+int ab_tensor_add_into(ab_scheme* s, ab_tensor a, ab_tensor b, ab_tensor out);
+int ab_tensor_matmul_into(ab_scheme* s, ab_tensor a, ab_tensor b, ab_tensor out);
+
+/* ---- modules (src/modules.rs) --------------------------------------------- */
+/* Embedding::record (src/modules.rs:111-119). x is [dim] or [batch, dim]. */
+int ab_embedding_record(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x);
+/* RmsNorm::record / record_inplace (src/modules.rs:146-163). */
+int ab_rmsnorm_record(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor out);
+int ab_rmsnorm_record_inplace(ab_scheme* s, ab_tensor x, ab_tensor weight);
+/* Linear::record (src/modules.rs:178-186): out = weight @ x. */
+int ab_linear_record(ab_scheme* s, ab_tensor weight, ab_tensor x, ab_tensor out);
+
+/* KvCache::new / layer (src/modules.rs:38-64): [layers, batch, seq, kv_heads, head].
+ * layer() returns [seq, kv_heads, head] views when batch == 1, else
+ * [batch, seq, kv_heads, head]. dtype AB_F32 (the reference's) or AB_BF16. */
+int ab_kvcache_create(ab_runtime* rt, uint32_t layers, uint32_t seq_len, uint32_t kv_heads,
+                      uint32_t head_size, int32_t dtype, uint32_t batch, ab_kvcache** out);
+int ab_kvcache_layer(const ab_kvcache* c, uint32_t layer, ab_tensor* key, ab_tensor* value);
+int ab_kvcache_zero(ab_kvcache* c);
+int ab_kvcache_destroy(ab_kvcache* c);
+
+/* CausalAttentionBlockWeights (src/modules.rs:13-19). */
+typedef struct {
+    ab_tensor norm, query, key, value, output;
+} ab_attention_weights;
+
+/* CausalAttentionBlock::new (src/modules.rs:203-230). The reference signature is
+ * (hidden, query_heads, seq_len) with batch 1 and RoPE theta 10000
+ * (src/blocks.rs:234); max_batch and rope_theta extend it (pass 1 and 10000 for the
+ * reference behaviour). */
+int ab_attention_block_create(ab_runtime* rt, uint32_t hidden, uint32_t query_heads,
+                              uint32_t seq_len, uint32_t max_batch, float rope_theta,
+                              ab_attention_block** out);
+/* CausalAttentionBlock::record (src/modules.rs:232-260; op order src/blocks.rs:178-259):
+ * RMSNorm, Q/K/V, RoPE with the K/V append at step.position, split attention, output
+ * projection and residual add into x. */
+int ab_attention_block_record(ab_attention_block* b, ab_scheme* s, ab_tensor x,
+                              const ab_attention_weights* w, ab_tensor key, ab_tensor value,
+                              ab_tensor step);
+int ab_attention_block_destroy(ab_attention_block* b);
+
+/* SwiGluBlockWeights (src/modules.rs:23-28): gate = w1, up = w3, down = w2. */
+typedef struct {
+    ab_tensor norm, gate, up, down;
+} ab_swiglu_weights;
+
+/* SwiGluBlock::new (src/modules.rs:289-298), with max_batch (1 = reference). */
+int ab_swiglu_block_create(ab_runtime* rt, uint32_t hidden, uint32_t intermediate,
+                           uint32_t max_batch, ab_swiglu_block** out);
+/* SwiGluBlock::record (src/modules.rs:300-321; op order src/blocks.rs:262-278). */
+int ab_swiglu_block_record(ab_swiglu_block* b, ab_scheme* s, ab_tensor x,
+                           const ab_swiglu_weights* w);
+int ab_swiglu_block_destroy(ab_swiglu_block* b);
+
+/* ---- host decode loop (src/model.rs, src/generate.rs, src/tokenizer.rs) ------ */
+/* sample_argmax (src/tokenizer.rs:179-189): first index of the maximum. */
+int32_t ab_sample_argmax(const float* logits, uint32_t n);
+
+/* AutoregressiveModel (src/model.rs:7-11) as a C vtable. step() returns a host
+ * pointer to vocab_size logits that stays valid until the next step. */
+typedef struct {
+    void* self;
+    uint32_t (*vocab_size)(void* self);
+    uint32_t (*max_seq_len)(void* self);
+    int (*step)(void* self, uint32_t token, uint32_t pos, const float** logits);
+} ab_autoregressive_model;
+
+/* generate_tokens (src/generate.rs:43-91). Writes up to cap ids to out_tokens and the
+ * full count to *out_len; tokens_per_second as the reference computes it. */
+int ab_generate_tokens(const ab_autoregressive_model* m, const int32_t* prompt,
+                       uint32_t prompt_len, uint32_t max_new_tokens, int32_t has_stop,
+                       int32_t stop_on, int32_t* out_tokens, uint32_t cap, uint32_t* out_len,
+                       double* tokens_per_second);
+
+/* ---- Llama-shaped model assembly ----------------------------------------------
+ * The reference leaves model assembly to architecture crates (README.md:5,21). This
+ * is the llama2.c-layout composition the harness and benchmark use: Embedding,
+ * layers x [CausalAttentionBlock, SwiGluBlock], final RmsNorm, classifier Linear. */
+typedef struct {
+    uint32_t dim, layers, heads, kv_heads, head_dim, hidden, vocab, seq, batch;
+    float rope_theta, norm_eps;
+    int32_t dtype; /* AB_F32: fp32 everywhere; AB_BF16: bf16 weights and KV cache */
+} ab_llama_config;
+
+int ab_llama_create(ab_runtime* rt, const ab_llama_config* cfg, ab_llama** out);
+/* Seeded synthetic weights, the same streams the CPU oracle uses. */
+int ab_llama_init_synthetic(ab_llama* m, uint64_t seed, float std);
+/* Weight view: which = 0 embed, 1 wcls, 2 rms_final, 3 rms_att, 4 wq, 5 wk, 6 wv, 7 wo,
+ * 8 rms_ffn, 9 w1, 10 w2, 11 w3. */
+int ab_llama_weight(ab_llama* m, int32_t which, uint32_t layer, ab_tensor* out);
+/* KV cache of the model (for inspection). */
+int ab_llama_cache(ab_llama* m, ab_kvcache** out);
+/* One batched decode step: deposits n = batch steps and replays the step graph.
+ * logits_host (may be NULL) receives [batch, vocab] fp32; argmax_host (may be NULL)
+ * receives [batch] ids from the device argmax (same tie rule as sample_argmax). */
+int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* logits_host,
+                  int32_t* argmax_host);
+/* Device logits [batch, vocab] of the last step. */
+int ab_llama_logits(ab_llama* m, ab_tensor* out);
+/* Zero the KV cache (a new sequence). */
+int ab_llama_reset(ab_llama* m);
+/* AutoregressiveModel view of a batch-1 model (logits read back to the host). */
+int ab_llama_as_model(ab_llama* m, ab_autoregressive_model* out);
+int ab_llama_destroy(ab_llama* m);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AMMON_B200_H */
