@@ -285,6 +285,22 @@ class Scheme:
     def use_graph(self, enable: bool):
         _check(_abi.lib().ab_scheme_use_graph(self._h, 1 if enable else 0))
 
+    def node_labels(self) -> List[str]:
+        out = []
+        buf = C.create_string_buffer(128)
+        for i in range(self.ir_node_count()):
+            _check(_abi.lib().ab_scheme_node_label(self._h, i, buf, 128))
+            out.append(buf.value.decode())
+        return out
+
+    def time_nodes(self, iters: int = 10) -> List[float]:
+        """Mean milliseconds per launch of each node, each launched on its own between CUDA
+        events on the runtime stream."""
+        n = self.ir_node_count()
+        arr = (C.c_float * max(n, 1))()
+        _check(_abi.lib().ab_scheme_time_nodes(self._h, iters, arr, max(n, 1)))
+        return [float(arr[i]) for i in range(n)]
+
     def keep(self, *objs):
         self._keep.extend(objs)
 
@@ -551,6 +567,28 @@ class LlamaModel:
         """AutoregressiveModel::step (src/model.rs:10): host logits of one token."""
         logits, _ = self.step_batch([token], [pos])
         return logits[0]
+
+    def decode_device(self, tokens: Sequence[int], positions: Sequence[int], steps: int,
+                      want_tokens: bool = True):
+        """Greedy decode of `steps` tokens entirely on the device, starting from one
+        DecodeStep per batch row. Returns [steps, batch] ids (or None)."""
+        n = self.cfg.batch
+        arr = (_abi.DecodeStep_t * n)(*[(int(t), int(p)) for t, p in zip(tokens, positions)])
+        out = np.zeros((steps, n), np.int32) if want_tokens else None
+        _check(_abi.lib().ab_llama_decode_device(
+            self._h, arr, n, steps,
+            out.ctypes.data_as(C.POINTER(C.c_int32)) if want_tokens else None))
+        return out
+
+    def scheme(self) -> "Scheme":
+        h = C.c_void_p()
+        _check(_abi.lib().ab_llama_scheme(self._h, C.byref(h)))
+        s = Scheme.__new__(Scheme)
+        s._h = h
+        s.rt = self.rt
+        s._keep = [self]
+        s.close = lambda: None  # owned by the model
+        return s
 
     def logits_tensor(self) -> Tensor:
         t = _abi.Tensor_t()

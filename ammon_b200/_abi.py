@@ -84,6 +84,8 @@ SIGNATURES = {
     "ab_scheme_node_count": (C.c_int, [P, C.POINTER(u32)]),
     "ab_scheme_replay_stats": (C.c_int, [P, C.POINTER(u32), C.POINTER(u32)]),
     "ab_scheme_use_graph": (C.c_int, [P, i32]),
+    "ab_scheme_time_nodes": (C.c_int, [P, u32, C.POINTER(f32), u32]),
+    "ab_scheme_node_label": (C.c_int, [P, u32, C.c_char_p, u32]),
     "ab_kernel_embed": (C.c_int, [P, T, T, T]),
     "ab_kernel_gemv": (C.c_int, [P, T, T, T, T]),
     "ab_kernel_rmsnorm": (C.c_int, [P, T, T, T]),
@@ -120,6 +122,9 @@ SIGNATURES = {
     "ab_llama_cache": (C.c_int, [P, PP]),
     "ab_llama_step": (C.c_int, [P, C.POINTER(DecodeStep_t), u32, C.POINTER(f32),
                                 C.POINTER(i32)]),
+    "ab_llama_decode_device": (C.c_int, [P, C.POINTER(DecodeStep_t), u32, u32,
+                                         C.POINTER(i32)]),
+    "ab_llama_scheme": (C.c_int, [P, PP]),
     "ab_llama_logits": (C.c_int, [P, C.POINTER(T)]),
     "ab_llama_reset": (C.c_int, [P]),
     "ab_llama_as_model": (C.c_int, [P, C.POINTER(Model_t)]),

@@ -65,6 +65,27 @@ __global__ void __launch_bounds__(1024)
     pdl_trigger();
 }
 
+// Device-side sample feedback: the next DecodeStep of row b is {argmax[b], position + 1};
+// the id is also kept in history[position + 1, b].
+__global__ void feedback_kernel(const int32_t* __restrict__ argmax, Step* step,
+                                int32_t* __restrict__ history, uint32_t batch, uint32_t seq,
+                                uint32_t* flags) {
+    pdl_wait();
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < batch) {
+        const uint32_t next = step[b].position + 1;
+        if (next >= seq) {
+            atomicOr(flags, kFlagPositionRange);
+        } else {
+            const int32_t tok = argmax[b];
+            history[(uint64_t)next * batch + b] = tok;
+            step[b].token = (uint32_t)tok;
+            step[b].position = next;
+        }
+    }
+    pdl_trigger();
+}
+
 }  // namespace ab
 
 struct ab_llama {
@@ -75,8 +96,9 @@ struct ab_llama {
     ab_kvcache* cache = nullptr;
     ab_attention_block* attn = nullptr;
     ab_swiglu_block* ffn = nullptr;
-    ab_tensor x = {}, logits = {}, step = {}, argmax = {};
-    ab_scheme* scheme = nullptr;
+    ab_tensor x = {}, logits = {}, step = {}, argmax = {}, history = {};
+    ab_scheme* scheme = nullptr;       // one decode step
+    ab_scheme* loop_scheme = nullptr;  // one decode step + device sample feedback
     float* h_logits = nullptr;  // pinned [batch, vocab]
     int32_t* h_argmax = nullptr;
     ab_decode_step* h_steps = nullptr;
@@ -111,6 +133,7 @@ void destroy_model(ab_llama* m) {
         cudaStreamSynchronize(rt->stream);
     }
     if (m->scheme) ab_scheme_destroy(m->scheme);
+    if (m->loop_scheme) ab_scheme_destroy(m->loop_scheme);
     if (m->attn) ab_attention_block_destroy(m->attn);
     if (m->ffn) ab_swiglu_block_destroy(m->ffn);
     if (m->cache) ab_kvcache_destroy(m->cache);
@@ -118,7 +141,7 @@ void destroy_model(ab_llama* m) {
                     &m->w3})
         for (auto& t : *v) free_t(rt, t);
     for (ab_tensor* t : {&m->embed, &m->wcls, &m->rms_final, &m->x, &m->logits, &m->step,
-                         &m->argmax})
+                         &m->argmax, &m->history})
         free_t(rt, *t);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_argmax) cudaFreeHost(m->h_argmax);
@@ -126,9 +149,8 @@ void destroy_model(ab_llama* m) {
     delete m;
 }
 
-// Records the full decode step into the model's scheme.
-void record_step(ab_llama* m) {
-    ab_scheme* s = m->scheme;
+// Records the full decode step into `s` (with the device sample feedback when asked).
+void record_step(ab_llama* m, ab_scheme* s, bool feedback) {
     s->nodes.clear();
     s->dirty = true;
     const auto& c = m->c;
@@ -169,6 +191,16 @@ void record_step(ab_llama* m) {
     s->add("argmax", [=](cudaStream_t st) {
         return launch(st, dim3(batch), dim3(1024), 0, true, argmax_kernel, lg, vocab, am);
     });
+    if (feedback) {
+        Step* stp = (Step*)m->step.data;
+        int32_t* hist = (int32_t*)m->history.data;
+        const uint32_t seq = c.seq;
+        uint32_t* flags = m->rt->flags;
+        s->add("sample_feedback", [=](cudaStream_t st) {
+            return launch(st, dim3((batch + 127) / 128), dim3(128), 0, true, feedback_kernel, am,
+                          stp, hist, batch, seq, flags);
+        });
+    }
 }
 
 int vt_step(void* self, uint32_t token, uint32_t pos, const float** logits) {
@@ -279,12 +311,14 @@ int ab_llama_create(ab_runtime* rt, const ab_llama_config* cfg, ab_llama** out) 
             m->x = alloc_t(rt, AB_F32, {c.batch, c.dim});
             m->logits = alloc_t(rt, AB_F32, {c.batch, c.vocab});
             m->argmax = alloc_t(rt, AB_U32, {c.batch});
+            m->history = alloc_t(rt, AB_U32, {c.seq, c.batch});
             check(ab_step_parcel(rt, c.batch, &m->step));
             cuda_check(cudaMallocHost(&m->h_logits, (size_t)c.batch * c.vocab * 4), "pinned logits");
             cuda_check(cudaMallocHost(&m->h_argmax, (size_t)c.batch * 4), "pinned argmax");
             cuda_check(cudaMallocHost(&m->h_steps, (size_t)c.batch * sizeof(ab_decode_step)),
                        "pinned steps");
             check(ab_scheme_create(rt, &m->scheme));
+            check(ab_scheme_create(rt, &m->loop_scheme));
         } catch (...) {
             destroy_model(m);
             throw;
@@ -367,7 +401,7 @@ int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* l
         }
         Runtime* rt = m->rt;
         rt->activate();
-        if (m->scheme->nodes.empty()) record_step(m);
+        if (m->scheme->nodes.empty()) record_step(m, m->scheme, false);
         std::memcpy(m->h_steps, steps, sizeof(ab_decode_step) * n);
         cuda_check(cudaMemcpyAsync(m->step.data, m->h_steps, sizeof(ab_decode_step) * n,
                                    cudaMemcpyHostToDevice, rt->stream),
@@ -386,6 +420,53 @@ int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* l
         rt->check_flags();
         if (logits_host) std::memcpy(logits_host, m->h_logits, lbytes);
         if (argmax_host) std::memcpy(argmax_host, m->h_argmax, (size_t)n * 4);
+    });
+}
+
+int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n, uint32_t steps,
+                           int32_t* tokens_out) {
+    return guard([&] {
+        if (!m || !start) fail(AB_ERR_ARGUMENT, "null argument");
+        const auto& c = m->c;
+        if (n != c.batch)
+            fail(AB_ERR_ARGUMENT, "decode needs " + std::to_string(c.batch) + " start steps");
+        for (uint32_t b = 0; b < n; b++) {
+            if (start[b].token >= c.vocab) fail(AB_ERR_ARGUMENT, "start token out of range");
+            if ((uint64_t)start[b].position + steps > c.seq)
+                fail(AB_ERR_ARGUMENT, "decode of " + std::to_string(steps) + " steps from position " +
+                                          std::to_string(start[b].position) + " passes max_seq_len " +
+                                          std::to_string(c.seq));
+        }
+        Runtime* rt = m->rt;
+        rt->activate();
+        if (m->loop_scheme->nodes.empty()) record_step(m, m->loop_scheme, true);
+        std::memcpy(m->h_steps, start, sizeof(ab_decode_step) * n);
+        cuda_check(cudaMemcpyAsync(m->step.data, m->h_steps, sizeof(ab_decode_step) * n,
+                                   cudaMemcpyHostToDevice, rt->stream),
+                   "deposit steps");
+        for (uint32_t i = 0; i < steps; i++) check(ab_scheme_submit(m->loop_scheme));
+        if (tokens_out) {
+            std::vector<int32_t> hist((size_t)c.seq * c.batch);
+            cuda_check(cudaMemcpyAsync(hist.data(), m->history.data, hist.size() * 4,
+                                       cudaMemcpyDeviceToHost, rt->stream),
+                       "history readback");
+            cuda_check(cudaStreamSynchronize(rt->stream), "decode synchronize");
+            for (uint32_t i = 0; i < steps; i++)
+                for (uint32_t b = 0; b < n; b++) {
+                    const uint64_t p = (uint64_t)start[b].position + 1 + i;
+                    tokens_out[(size_t)i * n + b] = p < c.seq ? hist[p * c.batch + b] : -1;
+                }
+        }
+        cuda_check(cudaStreamSynchronize(rt->stream), "decode synchronize");
+        rt->check_flags();
+    });
+}
+
+int ab_llama_scheme(ab_llama* m, ab_scheme** out) {
+    return guard([&] {
+        if (!m || !out) fail(AB_ERR_ARGUMENT, "null argument");
+        if (m->scheme->nodes.empty()) record_step(m, m->scheme, false);
+        *out = m->scheme;
     });
 }
 

@@ -413,4 +413,45 @@ int ab_scheme_use_graph(ab_scheme* s, int32_t enable) {
     });
 }
 
+int ab_scheme_time_nodes(ab_scheme* s, uint32_t iters, float* ms, uint32_t n) {
+    return guard([&] {
+        if (!s || !ms) fail(AB_ERR_ARGUMENT, "null argument");
+        if (!s->rt) fail(AB_ERR_ARGUMENT, "scheme has no runtime");
+        if (n < s->nodes.size()) fail(AB_ERR_ARGUMENT, "output holds fewer entries than nodes");
+        if (iters == 0) iters = 1;
+        Runtime& rt = *s->rt;
+        rt.activate();
+        cudaEvent_t a, b;
+        cuda_check(cudaEventCreate(&a), "event create");
+        cuda_check(cudaEventCreate(&b), "event create");
+        std::string err;
+        for (size_t i = 0; i < s->nodes.size() && err.empty(); i++) {
+            cudaError_t e = s->nodes[i].launch(rt.stream);  // warm
+            if (e == cudaSuccess) e = cudaEventRecord(a, rt.stream);
+            for (uint32_t k = 0; k < iters && e == cudaSuccess; k++) e = s->nodes[i].launch(rt.stream);
+            if (e == cudaSuccess) e = cudaEventRecord(b, rt.stream);
+            if (e == cudaSuccess) e = cudaEventSynchronize(b);
+            float t = 0.0f;
+            if (e == cudaSuccess) e = cudaEventElapsedTime(&t, a, b);
+            if (e != cudaSuccess) err = s->nodes[i].label + ": " + cudaGetErrorString(e);
+            ms[i] = t / (float)iters;
+        }
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        if (!err.empty()) fail(AB_ERR_CUDA, "time_nodes: " + err);
+        rt.check_flags();
+    });
+}
+
+int ab_scheme_node_label(const ab_scheme* s, uint32_t i, char* buf, uint32_t cap) {
+    return guard([&] {
+        if (!s || !buf || cap == 0) fail(AB_ERR_ARGUMENT, "null argument");
+        if (i >= s->nodes.size()) fail(AB_ERR_ARGUMENT, "node index out of range");
+        const std::string& l = s->nodes[i].label;
+        const size_t n = std::min<size_t>(l.size(), cap - 1);
+        std::memcpy(buf, l.data(), n);
+        buf[n] = 0;
+    });
+}
+
 }  // extern "C"

@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Decode throughput of the B200-native Ammon decode layer path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--batch B]
+                    [--impl ammon|reference]
+
+Workload (default): the Llama-3-8B-shaped bf16 decode (dim 4096, 32 layers, 32/8 heads,
+head_dim 128, SwiGLU 14336, vocab 128256, RoPE theta 500000, max context 8192,
+N(0, 0.02) synthetic weights from seed 3, a 128-token uniform prompt) at batch 1.
+One step = one greedy decode token for every stream of the batch.
+
+value:  tokens/s of the device-resident greedy loop (graph replays, device argmax feeds
+        the next DecodeStep), CUDA events on the decode stream, max over ranks.
+e2e:    tokens/s through the reference-facing step() (AutoregressiveModel::step): every
+        step uploads the DecodeSteps and reads [batch, vocab] fp32 logits back to the
+        host, where sample_argmax picks the next ids.
+With N > 1 every rank decodes its own batch of independent streams (replicas, no
+collective); value is the sum over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/sec (batch 1 and 64) at 1/2/4/8 B200; per-kernel HBM GB/s vs peak"
+
+WORKLOADS = {
+    "llama3-8b-bf16": dict(dim=4096, layers=32, heads=32, kv_heads=8, head_dim=128,
+                           hidden=14336, vocab=128256, seq=8192, theta=500000.0, bf16=True,
+                           seed=3, prompt=128,
+                           title="Llama-3-8B-shaped bf16 decode"),
+    "llama-110m-f32": dict(dim=768, layers=12, heads=12, kv_heads=12, head_dim=64, hidden=2048,
+                           vocab=32000, seq=1024, theta=10000.0, bf16=False, seed=1, prompt=16,
+                           title="Llama-shaped 110M fp32 multi-stream decode"),
+    "tiny-llama-f32": dict(dim=288, layers=6, heads=6, kv_heads=6, head_dim=48, hidden=768,
+                           vocab=32000, seq=256, theta=10000.0, bf16=False, seed=0, prompt=8,
+                           title="Tiny llama2.c fp32 decode"),
+}
+
+SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+# ----------------------------------------------------------------------------- helpers
+def _mix64(z):
+    M = (1 << 64) - 1
+    z = (z + 0x9E3779B97F4A7C15) & M
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+    return z ^ (z >> 31)
+
+
+def prompt_tokens(seed, stream, n, lo, hi):
+    """Uniform ids in [lo, hi): the generator the oracle uses (splitmix64 of seed/stream)."""
+    M = (1 << 64) - 1
+    key = _mix64(((seed * 0xD1B54A32D192ED03) & M) ^ _mix64(stream))
+    return [lo + _mix64((key + i) & M) % (hi - lo) for i in range(n)]
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(kernel, workload):
+    """Per-launch DRAM bytes of `kernel` from a committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={SMI_FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def layer_bytes(w, batch):
+    """Algorithmic bytes per launch of each fused kernel (weights once, activations and
+    KV rows read/written), for the kernel labels the step graph records."""
+    e = 2 if w["bf16"] else 4
+    d, F, V = w["dim"], w["hidden"], w["vocab"]
+    qd, kvd = w["heads"] * w["head_dim"], w["kv_heads"] * w["head_dim"]
+    return {
+        "ffn_gate_up_swiglu": 2 * F * d * e + batch * (d * 4 + F * e) + d * e,
+        "ffn_down_residual": d * F * e + batch * (F * e + 2 * d * 4),
+        "attn_qkv_rope": (qd + 2 * kvd) * d * e + batch * (d * 4 + qd * 4 + 2 * kvd * e) + d * e,
+        "attn_wo_residual": d * qd * e + batch * (qd * e + 2 * d * 4),
+        "final_norm_classifier": V * d * e + batch * (d * 4 + V * 4) + d * e,
+    }
+
+
+def step_bytes(w, batch, mean_pos):
+    """Algorithmic bytes of one decode step: all weights once, the K/V rows read by
+    attention for every stream (positions 0..pos), the new K/V row written."""
+    e = 2 if w["bf16"] else 4
+    L = w["layers"]
+    kvd = w["kv_heads"] * w["head_dim"]
+    lb = layer_bytes(w, batch)
+    per_layer = (lb["attn_qkv_rope"] + lb["attn_wo_residual"] + lb["ffn_gate_up_swiglu"] +
+                 lb["ffn_down_residual"])
+    kv = L * batch * 2 * kvd * e * (mean_pos + 1)
+    return L * per_layer + lb["final_norm_classifier"] + kv
+
+
+# ----------------------------------------------------------------------------- CPU
+def cpu_sample(w, batch, positions, threads):
+    """Times the oracle port of the reference's kernels on a bounded sample: one decoder
+    layer of the workload's shape at the given positions, and a 4096-row slice of the
+    classifier; scales to a full token (layers x layer time + classifier / slice)."""
+    from oracle import oracle as orc
+
+    orc.set_threads(threads)
+    vslice = min(4096, w["vocab"])
+    m = orc.Model(w["dim"], 1, w["heads"], w["kv_heads"], w["head_dim"], w["hidden"], vslice,
+                  max(positions) + 2, theta=w["theta"], bf16=w["bf16"], seed=w["seed"])
+    x = orc.normal(w["dim"], 9, 9, 0.0, 1.0)
+    per_token = []
+    for pos in positions:
+        m.set_x(x)
+        t0 = time.perf_counter()
+        m.attention_block(0, pos)
+        m.ffn_block(0)
+        t1 = time.perf_counter()
+        m.classify()
+        t2 = time.perf_counter()
+        per_token.append(w["layers"] * (t1 - t0) + (t2 - t1) * w["vocab"] / vslice)
+    m.close()
+    # the port decodes streams one after another
+    return per_token, batch
+
+
+def run_reference(args, w, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    nsteps = args.warmup + args.steps
+    positions = [w["prompt"] + i for i in range(nsteps)]
+    per_token, batch = cpu_sample(w, args.batch, positions, threads)
+    timed = per_token[args.warmup:]
+    step_s = statistics.mean(timed) * batch
+    value = batch / step_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
+        "config": {"workload": w["title"], "batch": args.batch, "parallelism": "cpu",
+                   "positions": f"{positions[args.warmup]}..{positions[-1]}"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": "one decoder layer x layers + 4096-row classifier slice "
+                                   "scaled to the vocab, per step; streams decoded in turn"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="default: min(steps, 64)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    w = WORKLOADS[args.workload]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, w, rank, world)
+        return
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+
+    import ammon_b200 as ab
+
+    B = args.batch
+    rt = ab.create_runtime(local)
+    cfg = ab.LlamaConfig(w["dim"], w["layers"], w["heads"], w["kv_heads"], w["head_dim"],
+                         w["hidden"], w["vocab"], w["seq"], batch=B, rope_theta=w["theta"],
+                         dtype=ab.BF16 if w["bf16"] else ab.F32)
+    model = ab.LlamaModel(rt, cfg)
+    model.init_synthetic(w["seed"], 0.02)
+    P = w["prompt"]
+    prompts = [prompt_tokens(w["seed"], 1000 + rank * B + b, P, 3, w["vocab"]) for b in range(B)]
+    # prompt: forced tokens at positions 0..P-2
+    for pos in range(P - 1):
+        model.step_batch([prompts[b][pos] for b in range(B)], [pos] * B, logits=False)
+    start_tok = [prompts[b][P - 1] for b in range(B)]
+    pos0 = P - 1
+    e2e_steps = args.e2e_steps or min(args.steps, 64)
+    need = pos0 + args.warmup + args.steps + e2e_steps + 1
+    if need > w["seq"]:
+        raise SystemExit(f"steps exceed the workload's max context ({need} > {w['seq']})")
+
+    # warm-up (device greedy loop)
+    toks = model.decode_device(start_tok, [pos0] * B, args.warmup)
+    start_tok = toks[-1].tolist()
+    pos0 += args.warmup
+
+    ext = torch.cuda.ExternalStream(rt.stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    rt.synchronize()
+    with ClockSampler(local) as clocks:
+        ev0.record(ext)
+        toks = model.decode_device(start_tok, [pos0] * B, args.steps)
+        ev1.record(ext)
+        ev1.synchronize()
+    rt.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t = ev0.elapsed_time(ev1) / 1e3
+    if dist:
+        tt = torch.tensor([t], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    start_tok = toks[-1].tolist()
+    pos0 += args.steps
+    value = world * B * args.steps / t
+    nodes_loop = len(model.scheme().node_labels()) + 1  # + sample feedback
+
+    # e2e through the reference-facing step(): DecodeSteps up, [B, vocab] logits down
+    import numpy as np
+
+    tok = start_tok
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        logits, _ = model.step_batch(tok, [pos0 + i] * B, logits=True)
+        tok = [int(np.argmax(logits[b])) for b in range(B)]
+    t_e2e = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([t_e2e], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_e2e = float(tt.item())
+    e2e = world * B * e2e_steps / t_e2e
+
+    # per-kernel times (each node launched alone between CUDA events on the decode stream)
+    sch = model.scheme()
+    labels = sch.node_labels()
+    times = sch.time_nodes(iters=3)
+    per_label = {}
+    for l, ms in zip(labels, times):
+        c = per_label.setdefault(l, [0, 0.0])
+        c[0] += 1
+        c[1] += ms
+    total_ms = sum(times)
+    lb = layer_bytes(w, B)
+    dom = max(per_label, key=lambda l: per_label[l][1])
+    n_dom, ms_dom = per_label[dom]
+    t_launch = ms_dom / n_dom / 1e3
+    peak, peak_kind = load_peaks()
+    achieved = lb[dom] / t_launch / 1e9 if dom in lb else None
+    mean_pos = pos0 - args.steps - e2e_steps + args.steps / 2
+    sb = step_bytes(w, B, mean_pos)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
+        "config": {"workload": w["title"], "batch": B, "seq_len": w["seq"],
+                   "positions": f"{pos0 - args.steps - e2e_steps}.."
+                                f"{pos0 - e2e_steps - 1}",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (weights stream every step)"},
+        "step_bytes": sb, "step_gbs": sb / (t / args.steps) / 1e9,
+        "step_frac": sb / (t / args.steps) / 1e9 / peak,
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": achieved / peak if achieved else None,
+                     "bytes_per_launch": lb.get(dom), "launch_ms": t_launch * 1e3,
+                     "traffic": profile_traffic(dom, args.workload)},
+        "kernels": {l: {"launches": c[0], "ms": round(c[1], 4),
+                        "share": round(c[1] / total_ms, 4),
+                        "gbs": round(lb[l] * c[0] / (c[1] / 1e3) / 1e9, 1) if l in lb else None}
+                    for l, c in sorted(per_label.items(), key=lambda kv: -kv[1][1])},
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
+                "d2h_bytes_per_step": 4 * B * w["vocab"]},
+        "gpu_launches": nodes_loop * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        cpos = [w["prompt"] + i for i in range(3)]
+        per_token, batch = cpu_sample(w, B, cpos, threads)
+        v = 1.0 / statistics.mean(per_token)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": "oracle: one decoder layer x layers + 4096-row "
+                                          "classifier slice scaled to the vocab, positions "
+                                          f"{cpos[0]}..{cpos[-1]}, one stream"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    rt.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -114,6 +114,13 @@ int ab_scheme_node_count(const ab_scheme* s, uint32_t* out);
 int ab_scheme_replay_stats(const ab_scheme* s, uint32_t* records, uint32_t* replays);
 /* enable = 0 launches nodes directly on each submit (debugging); default 1 (graph). */
 int ab_scheme_use_graph(ab_scheme* s, int32_t enable);
+/* Profiling aid with no reference counterpart (the reference labels dispatches for
+ * Goldy's tooling, src/blocks.rs:113-257): launches each recorded node on its own,
+ * `iters` times, between CUDA events on the runtime stream, and writes the mean
+ * milliseconds per launch of node i to ms[i] (n >= node count). */
+int ab_scheme_time_nodes(ab_scheme* s, uint32_t iters, float* ms, uint32_t n);
+/* Label of node i ("attn_qkv_rope", "ffn_gate_up_swiglu", ...), NUL-terminated. */
+int ab_scheme_node_label(const ab_scheme* s, uint32_t i, char* buf, uint32_t cap);
 
 /* ---- kernels (src/kernels.rs; each records one dispatch) ------------------- */
 /* embed (src/kernels.rs:35-47): x[b, :] = table[step[b].token, :]. */
@@ -239,6 +246,16 @@ int ab_llama_cache(ab_llama* m, ab_kvcache** out);
  * receives [batch] ids from the device argmax (same tie rule as sample_argmax). */
 int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* logits_host,
                   int32_t* argmax_host);
+/* Greedy decode of `steps` tokens with no host round-trip: the argmax of
+ * src/tokenizer.rs:179-189 runs on the device and feeds the next step. Deposits the
+ * n = batch `start` steps, then replays the step graph `steps` times, each replay
+ * feeding its argmax back as the next DecodeStep {token, position + 1}. tokens_out
+ * (may be NULL) receives [steps, batch] ids. A row whose position reaches seq_len stops
+ * advancing and raises AB_ERR_DEVICE at the end. */
+int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n, uint32_t steps,
+                           int32_t* tokens_out);
+/* The model's step scheme (recorded on first use), for profiling. */
+int ab_llama_scheme(ab_llama* m, ab_scheme** out);
 /* Device logits [batch, vocab] of the last step. */
 int ab_llama_logits(ab_llama* m, ab_tensor* out);
 /* Zero the KV cache (a new sequence). */

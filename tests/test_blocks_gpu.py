@@ -193,6 +193,33 @@ def test_tiny_llama_greedy_tokens_bit_identical(rt, orc):
     assert out_py.tokens == want
 
 
+def test_device_greedy_loop_matches_host_loop(rt, orc):
+    """decode_device (argmax and the next DecodeStep on the device) emits the ids the
+    reference loop (generate.rs:43-91 with host sample_argmax) emits."""
+    B = 2
+    o, g = make_pair(rt, orc, batch=B, seq=64)
+    refs = [orc.Model(128, 2, 4, 2, 32, 256, 96, 64, seed=7) for _ in range(B)]
+    prompts = [[3, 9, 27], [81, 50, 2]]
+    want = [r.generate_tokens(p, 40)[0] for r, p in zip(refs, prompts)]
+    for pos in range(2):
+        g.step_batch([prompts[b][pos] for b in range(B)], [pos] * B, logits=False)
+    got = g.decode_device([prompts[b][2] for b in range(B)], [2] * B, 37)
+    for b in range(B):
+        assert got[:, b].tolist() == want[b][2:], b
+    with pytest.raises(ab.AmmonError, match="passes max_seq_len"):
+        g.decode_device([1] * B, [60] * B, 10)
+
+
+def test_step_scheme_labels_and_node_timing(rt, orc):
+    o, g = make_pair(rt, orc)
+    s = g.scheme()
+    labels = s.node_labels()
+    assert labels[0] == "embed" and labels[-1] == "argmax"
+    assert labels.count("attn_qkv_rope") == g.cfg.layers
+    ms = s.time_nodes(iters=2)
+    assert len(ms) == len(labels) and all(t > 0 for t in ms)
+
+
 def test_position_beyond_seq_is_rejected(rt, orc):
     o, g = make_pair(rt, orc)
     with pytest.raises(ab.AmmonError, match="beyond max_seq_len"):
