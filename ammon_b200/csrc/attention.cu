@@ -14,6 +14,8 @@
 //    split order and writes the output, so no second kernel runs; it resets the ticket
 //    for the next replay.
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "internal.h"
@@ -346,3 +348,121 @@ void record_attention(ab_scheme* s, const char* label, AttnParams p) {
 }
 
 }  // namespace ab
+
+// ---- allocation-free variant ------------------------------------------------------------
+// ab_attention_decode_noalloc runs attn_decode_kernel with its split partials and tickets in
+// one fixed array of device memory that is part of the library image, so the call itself
+// allocates nothing. Layout of the array: kNoAllocFloats floats of partials, then
+// kNoAllocTickets 32-bit tickets, then one flag word.
+namespace ab {
+
+constexpr uint64_t kNoAllocFloats = 1ull << 20;  // 4 MiB of split partials
+constexpr uint32_t kNoAllocTickets = 16384;      // 64 KiB of tickets (batch * kv_heads)
+constexpr uint64_t kNoAllocBytes = kNoAllocFloats * 4 + (uint64_t)kNoAllocTickets * 4 + 256;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once per device.
+static unsigned char* noalloc_scratch(int* device) {
+    cuda_check(cudaGetDevice(device), "cudaGetDevice");
+    if (*device < 0 || *device >= kNoAllocMaxDevices)
+        fail(AB_ERR_ARGUMENT, "device index out of range for the static scratch table");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[*device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            fail(AB_ERR_CUDA, std::string("cudaGetSymbolAddress of the attention scratch: ") +
+                                  cudaGetErrorString(e));
+        g_noalloc_addr[*device] = p;
+    }
+    return (unsigned char*)g_noalloc_addr[*device];
+}
+
+}  // namespace ab
+
+using namespace ab;
+
+extern "C" int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor key_cache,
+                                           ab_tensor value_cache, ab_tensor out, ab_tensor step) {
+    return guard([&] {
+        expect_data("q", q);
+        expect_data("key_cache", key_cache);
+        expect_data("value_cache", value_cache);
+        expect_data("out", out);
+        expect_dtype("q", q, AB_F32);
+        expect_rank_in("q", q, 2, 3);
+        const uint32_t batch = q.rank == 3 ? q.dims[0] : 1;
+        const uint32_t heads = q.dims[q.rank - 2], head = q.dims[q.rank - 1];
+        expect_float("key_cache", key_cache);
+        expect_dtype("value_cache", value_cache, key_cache.dtype);
+        const int cr = q.rank == 3 ? 4 : 3;
+        expect_rank("key_cache", key_cache, cr);
+        expect_rank("value_cache", value_cache, cr);
+        for (int a = 0; a < cr; a++)
+            if (value_cache.dims[a] != key_cache.dims[a])
+                invalid("parameter `value_cache`: dims must match key_cache " + shape_str(key_cache));
+        const int o = cr - 3;
+        if (cr == 4 && key_cache.dims[0] < batch)
+            expect_dim("key_cache", key_cache, 0, "batch", batch);
+        const uint32_t seq = key_cache.dims[o], kv_heads = key_cache.dims[o + 1];
+        expect_dim("key_cache", key_cache, o + 2, "head", head);
+        expect_float("out", out);
+        if (numel(out) != (uint64_t)batch * heads * head)
+            invalid("parameter `out`: expected " + std::to_string((uint64_t)batch * heads * head) +
+                    " elements ([batch, heads * head]), got " + shape_str(out));
+        expect_step(step, batch);
+        if (!attention_fusable(heads, kv_heads, head, key_cache.dtype))
+            invalid("attention: needs query_heads / kv_heads in {1, 2, 4, 8} and head * element "
+                    "size a multiple of 16 bytes, head <= 128");
+
+        int device = 0;
+        unsigned char* base = noalloc_scratch(&device);
+        int sms = 148;
+        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device),
+                   "query SM count");
+        const uint32_t nsplit = attention_choose_splits(batch, kv_heads, seq, sms, 256);
+        uint64_t floats = 0, tickets = 0;
+        attention_scratch_size(batch, heads, head, nsplit, &floats, &tickets);
+        tickets = (uint64_t)batch * kv_heads;
+        if (floats > kNoAllocFloats || tickets > kNoAllocTickets)
+            fail(AB_ERR_ARGUMENT,
+                 "ab_attention_decode_noalloc: this shape needs " + std::to_string(floats * 4) +
+                     " bytes of split partials and " + std::to_string(tickets) +
+                     " tickets; the static scratch holds " + std::to_string(kNoAllocFloats * 4) +
+                     " bytes and " + std::to_string(kNoAllocTickets) + " tickets");
+
+        AttnParams p = {};
+        p.q = (const float*)q.data;
+        p.kcache = key_cache.data;
+        p.vcache = value_cache.data;
+        p.kv_dtype = key_cache.dtype;
+        p.cache_stride = (uint64_t)seq * kv_heads * head;
+        p.out = out.data;
+        p.out_dtype = out.dtype;
+        p.heads = heads;
+        p.kv_heads = kv_heads;
+        p.head = head;
+        p.seq = seq;
+        p.batch = batch;
+        p.nsplit = nsplit;
+        p.part_o = (float*)base;
+        p.part_ml = (float*)base + (uint64_t)batch * heads * nsplit * head;
+        p.counters = (uint32_t*)(base + kNoAllocFloats * 4);
+        p.flags = (uint32_t*)(base + kNoAllocFloats * 4 + (uint64_t)kNoAllocTickets * 4);
+        p.step = (const Step*)step.data;
+
+        cudaStream_t st = (cudaStream_t)stream;
+        // tickets must start at zero; the kernel resets them, but a failed earlier call
+        // could have left them set
+        cuda_check(cudaMemsetAsync(p.counters, 0, tickets * 4, st), "clear tickets");
+        // record into a throw-away list of launch closures, then launch them directly
+        ab_scheme tmp;
+        record_attention(&tmp, "attn_decode_noalloc", p);
+        for (auto& n : tmp.nodes) cuda_check(n.launch(st), "attention launch");
+    });
+}

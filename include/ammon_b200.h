@@ -203,6 +203,25 @@ int ab_swiglu_block_record(ab_swiglu_block* b, ab_scheme* s, ab_tensor x,
                            const ab_swiglu_weights* w);
 int ab_swiglu_block_destroy(ab_swiglu_block* b);
 
+/* ---- allocation-free attention ----------------------------------------------------
+ * No counterpart in the reference. Runs the block path's flash-decoding attention
+ * (q [heads, head] or [batch, heads, head] f32, caches [seq, kv_heads, head] or
+ * [batch, seq, kv_heads, head], out [batch, heads * head], DecodeStep parcel) on `stream`
+ * (a cudaStream_t of the current device; NULL = default stream) without allocating any
+ * device memory: the split partials and tickets live in one static device array of the
+ * library (4 MiB of partials = batch * heads * splits * (head + 2) floats, and 16384
+ * tickets = batch * kv_heads). For callers that must not call cudaMalloc/cudaFree, such
+ * as hosts whose device memory is owned by their own pooling allocator, or latency-bound
+ * loops that cannot take cudaFree's device-wide synchronisation. A shape needing more
+ * scratch than the array holds fails with AB_ERR_ARGUMENT before anything is launched.
+ * Every call on a device shares the array and it keeps the last call's contents (the
+ * tickets are cleared on the stream before each launch): calls that overlap on the GPU
+ * race. The first call on each device looks up the array's address with
+ * cudaGetSymbolAddress, with that device current; make that first call before any
+ * stream capture begins. Positions >= seq produce zero rows. */
+int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor key_cache,
+                                ab_tensor value_cache, ab_tensor out, ab_tensor step);
+
 /* ---- host decode loop (src/model.rs, src/generate.rs, src/tokenizer.rs) ------ */
 /* sample_argmax (src/tokenizer.rs:179-189): first index of the maximum. */
 int32_t ab_sample_argmax(const float* logits, uint32_t n);
