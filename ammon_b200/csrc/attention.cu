@@ -5,14 +5,18 @@
 //  - Grid (splits, kv_heads, batch). One CTA serves every query head of its GQA group
 //    from one staged K/V tile, so K/V bytes are read once per kv head rather than once
 //    per query head.
+//  - K/V tiles of 64 positions are staged in shared memory by TMA (2-D tensor maps over
+//    the cache, no multicast), double-buffered on mbarriers, in the 32/64/128-byte
+//    swizzle that lets row-parallel lanes read distinct banks. Head sizes TMA cannot tile
+//    use the same algorithm with plain 16-byte loads into padded rows.
 //  - The position range [0, pos] is cut into `nsplit` chunks (multiples of the 64-row
 //    tile) computed on the device from the step's position, so a graph recorded once
-//    serves every position. Splits beyond pos write an empty partial.
+//    serves every position. Only the splits that hold positions do work.
 //  - Scores, the online softmax (running max m, sum l) and the P.V accumulation happen
 //    in one pass over each tile.
-//  - The last CTA of a (batch, kv head) to finish (atomic ticket) folds the partials in
-//    split order and writes the output, so no second kernel runs; it resets the ticket
-//    for the next replay.
+//  - The last active CTA of a (batch, kv head) to finish (atomic ticket) folds the
+//    partials in split order and writes the output, so no second kernel runs; it resets
+//    the ticket for the next replay.
 #include <algorithm>
 #include <mutex>
 #include <string>
@@ -20,11 +24,13 @@
 #include "common.cuh"
 #include "internal.h"
 #include "ops.h"
+#include "tma.cuh"
 
 namespace ab {
 
 constexpr int kAttnThreads = 128;
 constexpr int kAttnTile = 64;
+constexpr int kAttnStages = 2;
 
 // 16-byte vector of K/V elements converted to floats (4 for f32, 8 for bf16).
 __device__ __forceinline__ void unpack(const uint4& v, float* f, float) {
@@ -44,59 +50,383 @@ __device__ __forceinline__ void unpack(const uint4& v, float* f, bf16) {
     f[7] = bf16hi(v.w);
 }
 
-struct AttnLayout {
-    uint32_t row_words, kstride_words;
-    size_t q_off, k_off, v_off, s_off, p_off, st_off, fold_off, w_off, total;
+// Shared state after the K/V stage buffers (both kernels).
+struct AttnTail {
+    size_t q_off, s_off, p_off, st_off, fold_off, w_off, end;
 };
 
-// Shared-memory layout; K rows are padded to a stride of 4 (mod 8) words so that lanes
-// reading different rows at the same column hit distinct banks.
+__host__ __device__ inline AttnTail attn_tail(size_t o, uint32_t head, uint32_t G, uint32_t nsplit) {
+    AttnTail T;
+    o = (o + 15) & ~(size_t)15;
+    T.q_off = o;
+    o += (size_t)G * head * 4;
+    T.s_off = o;
+    o += (size_t)G * kAttnTile * 4;
+    T.p_off = o;
+    o += (size_t)kAttnTile * (G < 4 ? 4 : G) * 4;
+    T.st_off = o;
+    o += 3 * 8 * 4 + 16;
+    T.fold_off = o;
+    o += (size_t)kAttnThreads * G * 4;
+    T.w_off = o;
+    o += (size_t)nsplit * G * 4;
+    T.end = (o + 15) & ~(size_t)15;
+    return T;
+}
+
+// Plain-load layout: K rows padded to a stride of 4 (mod 8) words so that lanes reading
+// different rows at the same column hit distinct banks.
+struct AttnLayout {
+    uint32_t row_words, kstride_words;
+    size_t k_off, v_off;
+    AttnTail t;
+    size_t total;
+};
+
 __host__ __device__ inline AttnLayout attn_layout(uint32_t head, uint32_t esz, uint32_t G,
                                                   uint32_t nsplit) {
     AttnLayout L;
     L.row_words = head * esz / 4;
     L.kstride_words = L.row_words + ((12 - L.row_words % 8) % 8);
-    size_t o = 0;
-    L.q_off = o;
-    o += (size_t)G * head * 4;
-    o = (o + 15) & ~(size_t)15;
-    L.k_off = o;
-    o += (size_t)kAttnTile * L.kstride_words * 4;
-    L.v_off = o;
-    o += (size_t)kAttnTile * L.row_words * 4;
-    L.s_off = o;
-    o += (size_t)G * kAttnTile * 4;
-    L.p_off = o;
-    o += (size_t)kAttnTile * (G < 4 ? 4 : G) * 4;
-    L.st_off = o;
-    o += 3 * 8 * 4 + 16;
-    L.fold_off = o;
-    o += (size_t)kAttnThreads * G * 4;
-    L.w_off = o;
-    o += (size_t)nsplit * G * 4;
-    L.total = (o + 15) & ~(size_t)15;
+    L.k_off = 0;
+    L.v_off = (size_t)kAttnTile * L.kstride_words * 4;
+    L.t = attn_tail(L.v_off + (size_t)kAttnTile * L.row_words * 4, head, G, nsplit);
+    L.total = L.t.end;
     return L;
 }
 
-template <typename KT, typename OT, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    constexpr int VE = 16 / sizeof(KT);  // elements per 16-byte vector
+// TMA layout: kAttnStages x [K tile | V tile], each tile nbox boxes of [64 rows x SWZ
+// bytes] on a 1024-byte aligned base (the dynamic buffer carries 1 KB of slack).
+struct AttnTmaLayout {
+    uint32_t rowbytes, stage_bytes;
+    AttnTail t;
+    size_t total;
+};
+
+__host__ __device__ inline AttnTmaLayout attn_tma_layout(uint32_t head, uint32_t esz, uint32_t G,
+                                                         uint32_t nsplit) {
+    AttnTmaLayout L;
+    L.rowbytes = head * esz;
+    L.stage_bytes = 2u * kAttnTile * L.rowbytes;
+    L.t = attn_tail((size_t)kAttnStages * L.stage_bytes, head, G, nsplit);
+    L.total = L.t.end + 1024;
+    return L;
+}
+
+// Online-softmax update of one tile: scores sc[G][64] -> probabilities pt[64][PS],
+// running m/l and the rescale factor alpha per head. Warp w takes heads w, w + 4.
+template <int G>
+__device__ __forceinline__ void attn_softmax_tile(const float* sc, float* pt, float* sm_m,
+                                                  float* sm_l, float* sm_a, uint32_t warp,
+                                                  uint32_t lane) {
+    constexpr int PS = G < 4 ? 4 : G;
+    for (int h = warp; h < G; h += 4) {
+        const float s0 = sc[h * kAttnTile + lane], s1 = sc[h * kAttnTile + lane + 32];
+        const float tmax = warp_max(fmaxf(s0, s1));
+        const float mold = sm_m[h];
+        const float mnew = fmaxf(mold, tmax);
+        const float alpha = expf(mold - mnew);
+        const float e0 = expf(s0 - mnew), e1 = expf(s1 - mnew);
+        const float lsum = warp_sum(e0 + e1);
+        pt[lane * PS + h] = e0;
+        pt[(lane + 32) * PS + h] = e1;
+        if (lane == 0) {
+            sm_m[h] = mnew;
+            sm_l[h] = sm_l[h] * alpha + lsum;
+            sm_a[h] = alpha;
+        }
+    }
+}
+
+// After the last tile: fold the ways, then either write the output (one active split) or
+// publish this split's partial and, in the last CTA of the group, combine the partials.
+template <typename OT, int G>
+__device__ __forceinline__ void attn_finish(const AttnParams& p, float* acc, uint32_t way,
+                                            uint32_t ways, uint32_t di, float* fold, float* wts,
+                                            float* sm_m, float* sm_l, int* sm_last,
+                                            uint32_t split, uint32_t active, uint32_t kvh,
+                                            uint32_t b, uint32_t tid) {
     const uint32_t hd = p.head;
-    const AttnLayout L = attn_layout(hd, sizeof(KT), G, p.nsplit);
-    float* qs = (float*)(smem + L.q_off);       // [G][hd], pre-scaled by 1/sqrt(hd)
-    uint32_t* ks = (uint32_t*)(smem + L.k_off);  // [TP][kstride_words]
-    uint32_t* vs = (uint32_t*)(smem + L.v_off);  // [TP][row_words]
-    float* sc = (float*)(smem + L.s_off);        // [G][TP] scores
-    float* pt = (float*)(smem + L.p_off);        // [TP][max(G,4)] probabilities
-    float* st = (float*)(smem + L.st_off);       // m[8], l[8], alpha[8], flag
-    float* fold = (float*)(smem + L.fold_off);   // [ways][G][hd]
-    float* wts = (float*)(smem + L.w_off);       // [nsplit][G] combine weights
+    if (way < ways) {
+#pragma unroll
+        for (int h = 0; h < G; h++) fold[((size_t)way * G + h) * hd + di] = acc[h];
+    }
+    __syncthreads();
+    if (way == 0) {
+        for (uint32_t w = 1; w < ways; w++) {
+#pragma unroll
+            for (int h = 0; h < G; h++) acc[h] += fold[((size_t)w * G + h) * hd + di];
+        }
+    }
+    const uint64_t orow = (uint64_t)b * p.heads * hd + (uint64_t)kvh * G * hd;
+    if (active == 1) {
+        if (way == 0) {
+#pragma unroll
+            for (int h = 0; h < G; h++) {
+                const float l = sm_l[h];
+                const float v = l > 0.0f ? acc[h] / l : 0.0f;
+                ((OT*)p.out)[orow + (uint64_t)h * hd + di] = from_f32<OT>(v);
+            }
+        }
+        return;
+    }
+    const uint64_t grp = (uint64_t)b * p.kv_heads + kvh;
+    float* po = p.part_o + (grp * p.nsplit + split) * G * hd;
+    float* pml = p.part_ml + (grp * p.nsplit + split) * G * 2;
+    if (way == 0) {
+#pragma unroll
+        for (int h = 0; h < G; h++) po[(size_t)h * hd + di] = acc[h];
+    }
+    if (tid < (uint32_t)G) {
+        pml[tid * 2] = sm_m[tid];
+        pml[tid * 2 + 1] = sm_l[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(p.counters + grp, 1u);
+        *sm_last = prev == active - 1;
+    }
+    __syncthreads();
+    if (!*sm_last) return;
+    __threadfence();
+    const float* go = p.part_o + grp * p.nsplit * G * hd;
+    const float* gml = p.part_ml + grp * p.nsplit * G * 2;
+    // per-head maximum over the active splits (threads stride the splits)
+    float red[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) red[h] = -INFINITY;
+    for (uint32_t s = tid; s < active; s += kAttnThreads) {
+#pragma unroll
+        for (int h = 0; h < G; h++) red[h] = fmaxf(red[h], __ldcg(gml + (s * G + h) * 2));
+    }
+#pragma unroll
+    for (int h = 0; h < G; h++) fold[tid * G + h] = red[h];
+    __syncthreads();
+    if (tid < (uint32_t)G) {
+        float M = -INFINITY;
+        for (uint32_t t = 0; t < kAttnThreads; t++) M = fmaxf(M, fold[t * G + tid]);
+        sm_m[tid] = M;
+    }
+    __syncthreads();
+    // split weights exp(m_s - M) and the normaliser sum_s w_s l_s
+#pragma unroll
+    for (int h = 0; h < G; h++) red[h] = 0.0f;
+    for (uint32_t s = tid; s < active; s += kAttnThreads) {
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            const float w = expf(__ldcg(gml + (s * G + h) * 2) - sm_m[h]);
+            wts[s * G + h] = w;
+            red[h] += w * __ldcg(gml + (s * G + h) * 2 + 1);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; h++) fold[tid * G + h] = red[h];
+    __syncthreads();
+    if (tid < (uint32_t)G) {
+        float L = 0.0f;
+        for (uint32_t t = 0; t < kAttnThreads; t++) L += fold[t * G + tid];
+        sm_l[tid] = L;
+    }
+    __syncthreads();
+    for (uint32_t o = tid; o < G * hd; o += kAttnThreads) {
+        const uint32_t h = o / hd;
+        float v = 0.0f;
+#pragma unroll 4
+        for (uint32_t s = 0; s < active; s++) v += wts[s * G + h] * __ldcg(go + (size_t)s * G * hd + o);
+        const float L = sm_l[h];
+        ((OT*)p.out)[orow + o] = from_f32<OT>(L > 0.0f ? v / L : 0.0f);
+    }
+    if (tid == 0) p.counters[grp] = 0;
+}
+
+// The split's position range [start, end) and the number of splits holding positions.
+__device__ __forceinline__ void attn_split_range(const AttnParams& p, uint32_t split, uint32_t b,
+                                                 uint32_t* start, uint32_t* end, uint32_t* active) {
+    const uint32_t pos = p.step[b].position;
+    const bool bad = pos >= p.seq;
+    if (bad && split == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+        atomicOr(p.flags, kFlagPositionRange);
+    const uint32_t total = bad ? 0u : pos + 1;
+    uint32_t chunk = (total + p.nsplit - 1) / p.nsplit;
+    chunk = max(1u, (chunk + kAttnTile - 1) / kAttnTile) * kAttnTile;
+    *active = max(1u, (total + chunk - 1) / chunk);
+    *start = min(split * chunk, total);
+    *end = min(*start + chunk, total);
+}
+
+// ---- TMA kernel -----------------------------------------------------------------------------
+template <typename KT, typename OT, int G, int SWZ>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_decode_tma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kAttnStages];
+    constexpr int ESZ = sizeof(KT);
+    constexpr int VE = 16 / ESZ;
+    constexpr int PS = G < 4 ? 4 : G;
+    constexpr uint32_t CPB = SWZ / 16;   // 16-byte chunks per box row
+    constexpr uint32_t BOXE = SWZ / ESZ;  // elements per box row
+    const uint32_t hd = p.head;
+    const AttnTmaLayout L = attn_tma_layout(hd, ESZ, G, p.nsplit);
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* qs = (float*)(smem + L.t.q_off);
+    float* sc = (float*)(smem + L.t.s_off);
+    float* pt = (float*)(smem + L.t.p_off);
+    float* st = (float*)(smem + L.t.st_off);
+    float* fold = (float*)(smem + L.t.fold_off);
+    float* wts = (float*)(smem + L.t.w_off);
     float* sm_m = st;
     float* sm_l = st + 8;
     float* sm_a = st + 16;
     int* sm_last = (int*)(st + 24);
+
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    const uint32_t nbox = L.rowbytes / SWZ;
+
+    pdl_wait();
+    uint32_t start, end, active;
+    attn_split_range(p, split, b, &start, &end, &active);
+    if (split >= active) {
+        pdl_trigger();
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kAttnStages; s++) mbar_init(smem_u32(&full_bar[s]), 1);
+        fence_barrier_init();
+    }
+    const float qscale = 1.0f / sqrtf((float)hd);
+    const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * hd;
+    for (uint32_t i = tid; i < G * hd; i += kAttnThreads) qs[i] = qsrc[i] * qscale;
+    if (tid < 8) {
+        sm_m[tid] = -INFINITY;
+        sm_l[tid] = 0.0f;
+    }
+    const uint32_t ways = kAttnThreads / hd;
+    const uint32_t way = tid / hd, di = tid % hd;
+    float acc[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) acc[h] = 0.0f;
+    __syncthreads();
+
+    const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
+    const int32_t ybase = (int32_t)(b * p.seq + start);
+    auto issue = [&](uint32_t i) {
+        const uint32_t s = i % kAttnStages;
+        const uint32_t bar = smem_u32(&full_bar[s]);
+        unsigned char* kst = smem + (size_t)s * L.stage_bytes;
+        unsigned char* vst = kst + L.stage_bytes / 2;
+        mbar_arrive_expect_tx(bar, L.stage_bytes);
+        const int32_t y = ybase + (int32_t)(i * kAttnTile);
+        for (uint32_t j = 0; j < nbox; j++) {
+            const int32_t x = (int32_t)(kvh * hd + j * BOXE);
+            tma_load_2d(smem_u32(kst + (size_t)j * kAttnTile * SWZ), &kmap, x, y, bar);
+            tma_load_2d(smem_u32(vst + (size_t)j * kAttnTile * SWZ), &vmap, x, y, bar);
+        }
+    };
+    if (tid == 0)
+        for (uint32_t i = 0; i < ntiles && i < (uint32_t)kAttnStages; i++) issue(i);
+
+    uint32_t failed_at = ntiles;
+    for (uint32_t i = 0; i < ntiles; i++) {
+        const uint32_t s = i % kAttnStages;
+        const bool got = mbar_wait_bounded(smem_u32(&full_bar[s]), (i / kAttnStages) & 1);
+        if (!__syncthreads_and(got)) {
+            failed_at = i;
+            break;
+        }
+        const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
+        const unsigned char* kst = smem + (size_t)s * L.stage_bytes;
+        const unsigned char* vst = kst + L.stage_bytes / 2;
+        // scores: thread -> (position pp, head group hg)
+        {
+            const uint32_t pp = tid % kAttnTile, hg = tid / kAttnTile;
+            float d[G];
+#pragma unroll
+            for (int h = 0; h < G; h++) d[h] = 0.0f;
+            if (hg < (uint32_t)G) {
+                for (uint32_t j = 0; j < nbox; j++) {
+#pragma unroll
+                    for (uint32_t c = 0; c < CPB; c++) {
+                        const uint32_t off =
+                            swizzle_off<SWZ>(j * kAttnTile * SWZ + pp * SWZ + c * 16);
+                        float kf[VE];
+                        unpack(*reinterpret_cast<const uint4*>(kst + off), kf, KT());
+                        const uint32_t e0 = j * BOXE + c * VE;
+#pragma unroll
+                        for (int h = 0; h < G; h++) {
+                            if ((h % 2) != (int)hg && G > 1) continue;
+                            const float* qh = qs + h * hd + e0;
+#pragma unroll
+                            for (int e = 0; e < VE; e++) d[h] = fmaf(qh[e], kf[e], d[h]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < G; h++) {
+                    if ((h % 2) != (int)hg && G > 1) continue;
+                    sc[h * kAttnTile + pp] = pp < rows ? d[h] : -INFINITY;
+                }
+            }
+        }
+        __syncthreads();
+        attn_softmax_tile<G>(sc, pt, sm_m, sm_l, sm_a, warp, lane);
+        __syncthreads();
+        // P.V: thread -> (dim di, way); ways split the tile's positions
+        if (way < ways) {
+#pragma unroll
+            for (int h = 0; h < G; h++) acc[h] *= sm_a[h];
+            const uint32_t byte = di * ESZ;
+            const uint32_t vcol = (byte / SWZ) * kAttnTile * SWZ + byte % SWZ;
+            for (uint32_t r = way; r < rows; r += ways) {
+                const float v =
+                    to_f32(*reinterpret_cast<const KT*>(vst + swizzle_off<SWZ>(vcol + r * SWZ)));
+                const float* pr = pt + r * PS;
+#pragma unroll
+                for (int h = 0; h < G; h++) acc[h] = fmaf(pr[h], v, acc[h]);
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && i + kAttnStages < ntiles) issue(i + kAttnStages);
+    }
+    if (failed_at < ntiles) {
+        // a bounded wait ran out: flag it, let the copies in flight land, and stop
+        if (tid == 0) {
+            atomicOr(p.flags, kFlagWaitTimeout);
+            for (uint32_t i = failed_at; i < ntiles && i < failed_at + kAttnStages; i++)
+                mbar_wait_bounded(smem_u32(&full_bar[i % kAttnStages]), (i / kAttnStages) & 1);
+        }
+        __syncthreads();
+        pdl_trigger();
+        return;
+    }
+    pdl_trigger();
+    attn_finish<OT, G>(p, acc, way, ways, di, fold, wts, sm_m, sm_l, sm_last, split, active, kvh,
+                       b, tid);
+}
+
+// ---- plain-load kernel (head sizes the TMA boxes cannot tile) --------------------------------
+template <typename KT, typename OT, int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int VE = 16 / sizeof(KT);  // elements per 16-byte vector
     constexpr int PS = G < 4 ? 4 : G;
+    const uint32_t hd = p.head;
+    const AttnLayout L = attn_layout(hd, sizeof(KT), G, p.nsplit);
+    uint32_t* ks = (uint32_t*)(smem + L.k_off);  // [TP][kstride_words]
+    uint32_t* vs = (uint32_t*)(smem + L.v_off);  // [TP][row_words]
+    float* qs = (float*)(smem + L.t.q_off);      // [G][hd], pre-scaled by 1/sqrt(hd)
+    float* sc = (float*)(smem + L.t.s_off);      // [G][TP] scores
+    float* pt = (float*)(smem + L.t.p_off);      // [TP][max(G,4)] probabilities
+    float* st = (float*)(smem + L.t.st_off);     // m[8], l[8], alpha[8], flag
+    float* fold = (float*)(smem + L.t.fold_off);
+    float* wts = (float*)(smem + L.t.w_off);
+    float* sm_m = st;
+    float* sm_l = st + 8;
+    float* sm_a = st + 16;
+    int* sm_last = (int*)(st + 24);
 
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
@@ -104,17 +434,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     const uint32_t nvec = hd / VE;  // 16-byte vectors per K/V row
 
     pdl_wait();
-    pdl_trigger();
-
-    const uint32_t pos = p.step[b].position;
-    const bool bad = pos >= p.seq;
-    if (bad && split == 0 && kvh == 0 && tid == 0) atomicOr(p.flags, kFlagPositionRange);
-    const uint32_t total = bad ? 0u : pos + 1;
-    uint32_t chunk = (total + p.nsplit - 1) / p.nsplit;
-    chunk = (chunk + kAttnTile - 1) / kAttnTile * kAttnTile;
-    const uint32_t start = min(split * chunk, total);
-    const uint32_t end = min(start + chunk, total);
-
+    uint32_t start, end, active;
+    attn_split_range(p, split, b, &start, &end, &active);
+    if (split >= active) {
+        pdl_trigger();
+        return;
+    }
     const float qscale = 1.0f / sqrtf((float)hd);
     const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * hd;
     for (uint32_t i = tid; i < G * hd; i += kAttnThreads) qs[i] = qsrc[i] * qscale;
@@ -134,7 +459,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
 
     for (uint32_t t0 = start; t0 < end; t0 += kAttnTile) {
         const uint32_t rows = min((uint32_t)kAttnTile, end - t0);
-        // stage K and V rows of the tile (zero rows past the end)
         for (uint32_t v = tid; v < kAttnTile * nvec; v += kAttnThreads) {
             const uint32_t r = v / nvec, c = v % nvec;
             uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
@@ -147,7 +471,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
             *reinterpret_cast<uint4*>(vs + (size_t)r * L.row_words + c * 4) = vv;
         }
         __syncthreads();
-        // scores: thread -> (position p, head group hg)
         {
             const uint32_t pp = tid % kAttnTile, hg = tid / kAttnTile;
             float d[G];
@@ -174,29 +497,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
             }
         }
         __syncthreads();
-        // online softmax per head: warp w takes heads w, w + 4
-        for (int h = warp; h < G; h += 4) {
-            const float s0 = sc[h * kAttnTile + lane], s1 = sc[h * kAttnTile + lane + 32];
-            const float tmax = warp_max(fmaxf(s0, s1));
-            const float mold = sm_m[h];
-            const float mnew = fmaxf(mold, tmax);
-            const float alpha = expf(mold - mnew);
-            const float e0 = expf(s0 - mnew), e1 = expf(s1 - mnew);
-            const float lsum = warp_sum(e0 + e1);
-            pt[lane * PS + h] = e0;
-            pt[(lane + 32) * PS + h] = e1;
-            if (lane == 0) {
-                sm_m[h] = mnew;
-                sm_l[h] = sm_l[h] * alpha + lsum;
-                sm_a[h] = alpha;
-            }
-        }
+        attn_softmax_tile<G>(sc, pt, sm_m, sm_l, sm_a, warp, lane);
         __syncthreads();
-        // P.V: thread -> (dim di, way); ways split the tile's positions
         if (way < ways) {
 #pragma unroll
             for (int h = 0; h < G; h++) acc[h] *= sm_a[h];
-            for (uint32_t r = way; r < kAttnTile; r += ways) {
+            for (uint32_t r = way; r < rows; r += ways) {
                 const KT* vr = reinterpret_cast<const KT*>(vs + (size_t)r * L.row_words);
                 const float v = to_f32(vr[di]);
                 const float* pr = pt + r * PS;
@@ -206,80 +512,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         }
         __syncthreads();
     }
-
-    // fold the ways in order
-    if (way < ways) {
-#pragma unroll
-        for (int h = 0; h < G; h++) fold[((size_t)way * G + h) * hd + di] = acc[h];
-    }
-    __syncthreads();
-    if (way == 0) {
-        for (uint32_t w = 1; w < ways; w++) {
-#pragma unroll
-            for (int h = 0; h < G; h++) acc[h] += fold[((size_t)w * G + h) * hd + di];
-        }
-    }
-
-    const uint64_t orow = (uint64_t)b * p.heads * hd + (uint64_t)kvh * G * hd;
-    if (p.nsplit == 1) {
-        if (way == 0) {
-#pragma unroll
-            for (int h = 0; h < G; h++) {
-                const float l = sm_l[h];
-                const float v = l > 0.0f ? acc[h] / l : 0.0f;
-                ((OT*)p.out)[orow + (uint64_t)h * hd + di] = from_f32<OT>(v);
-            }
-        }
-        return;
-    }
-
-    // write this split's partial, then the last CTA of the group combines
-    const uint64_t grp = (uint64_t)b * p.kv_heads + kvh;
-    float* po = p.part_o + (grp * p.nsplit + split) * G * hd;
-    float* pml = p.part_ml + (grp * p.nsplit + split) * G * 2;
-    if (way == 0) {
-#pragma unroll
-        for (int h = 0; h < G; h++) po[(size_t)h * hd + di] = acc[h];
-    }
-    if (tid < (uint32_t)G) {
-        pml[tid * 2] = sm_m[tid];
-        pml[tid * 2 + 1] = sm_l[tid];
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(p.counters + grp, 1u);
-        *sm_last = prev == p.nsplit - 1;
-    }
-    __syncthreads();
-    if (!*sm_last) return;
-    __threadfence();
-    const float* go = p.part_o + grp * p.nsplit * G * hd;
-    const float* gml = p.part_ml + grp * p.nsplit * G * 2;
-    if (tid < (uint32_t)G) {
-        float M = -INFINITY;
-        for (uint32_t s = 0; s < p.nsplit; s++) M = fmaxf(M, __ldcg(gml + (s * G + tid) * 2));
-        float Lsum = 0.0f;
-        for (uint32_t s = 0; s < p.nsplit; s++) {
-            const float m = __ldcg(gml + (s * G + tid) * 2);
-            const float w = (m == -INFINITY) ? 0.0f : expf(m - M);
-            wts[s * G + tid] = w;
-            Lsum += w * __ldcg(gml + (s * G + tid) * 2 + 1);
-        }
-        sm_l[tid] = Lsum;
-    }
-    __syncthreads();
-    for (uint32_t o = tid; o < G * hd; o += kAttnThreads) {
-        const uint32_t h = o / hd;
-        float v = 0.0f;
-        for (uint32_t s = 0; s < p.nsplit; s++) {
-            const float w = wts[s * G + h];
-            if (w != 0.0f) v += w * __ldcg(go + (size_t)s * G * hd + o);
-        }
-        const float Lsum = sm_l[h];
-        ((OT*)p.out)[orow + o] = from_f32<OT>(Lsum > 0.0f ? v / Lsum : 0.0f);
-    }
-    if (tid == 0) p.counters[grp] = 0;
+    pdl_trigger();
+    attn_finish<OT, G>(p, acc, way, ways, di, fold, wts, sm_m, sm_l, sm_last, split, active, kvh,
+                       b, tid);
 }
 
 bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t kv_dtype) {
@@ -293,7 +528,8 @@ bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t
 
 uint32_t attention_choose_splits(uint32_t batch, uint32_t kv_heads, uint32_t seq, int sm_count,
                                  uint32_t max_splits) {
-    const uint64_t target = (uint64_t)std::max(sm_count, 1) * 8;
+    // about four CTAs per SM over the (batch, kv head, split) grid
+    const uint64_t target = (uint64_t)std::max(sm_count, 1) * 4;
     const uint64_t groups = std::max<uint64_t>(1, (uint64_t)batch * kv_heads);
     uint64_t ns = (target + groups - 1) / groups;
     ns = std::min<uint64_t>(ns, (seq + kAttnTile - 1) / kAttnTile);
@@ -307,19 +543,50 @@ void attention_scratch_size(uint32_t batch, uint32_t heads, uint32_t head, uint3
     *counters = (uint64_t)batch * heads;
 }
 
+static cudaError_t set_smem(const void* kern, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
 template <typename KT, typename OT, int G>
 static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
-    const AttnLayout L = attn_layout(p.head, sizeof(KT), G, p.nsplit);
-    const size_t smem = L.total;
+    const int esz = sizeof(KT);
+    const uint32_t rowbytes = p.head * esz;
+    dim3 grid(p.nsplit, p.kv_heads, p.batch);
+    const int swz = rowbytes % 128 == 0 ? 128 : rowbytes % 64 == 0 ? 64 : 0;
+    if (swz) {
+        CUtensorMap kmap, vmap;
+        const uint64_t inner = (uint64_t)p.kv_heads * p.head;
+        const uint64_t rows = (uint64_t)p.batch * p.seq;
+        encode_tmap_2d(&kmap, esz == 2 ? AB_BF16 : AB_F32, p.kcache, inner, rows, inner * esz,
+                       swz / esz, kAttnTile, swz);
+        encode_tmap_2d(&vmap, esz == 2 ? AB_BF16 : AB_F32, p.vcache, inner, rows, inner * esz,
+                       swz / esz, kAttnTile, swz);
+        const size_t smem = attn_tma_layout(p.head, esz, G, p.nsplit).total;
+        if (smem > 220 * 1024) invalid("attention: shared-memory stage too large");
+        if (swz == 128) {
+            auto kern = attn_decode_tma_kernel<KT, OT, G, 128>;
+            s->add(label, [=](cudaStream_t st) {
+                cudaError_t e = set_smem((const void*)kern, smem);
+                if (e != cudaSuccess) return e;
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+            });
+        } else {
+            auto kern = attn_decode_tma_kernel<KT, OT, G, 64>;
+            s->add(label, [=](cudaStream_t st) {
+                cudaError_t e = set_smem((const void*)kern, smem);
+                if (e != cudaSuccess) return e;
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+            });
+        }
+        return;
+    }
+    const size_t smem = attn_layout(p.head, esz, G, p.nsplit).total;
     if (smem > 200 * 1024) invalid("attention: shared-memory stage too large");
     auto kern = attn_decode_kernel<KT, OT, G>;
-    dim3 grid(p.nsplit, p.kv_heads, p.batch);
     s->add(label, [=](cudaStream_t st) {
-        if (smem > 48 * 1024) {
-            cudaError_t e =
-                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-        }
+        cudaError_t e = set_smem((const void*)kern, smem);
+        if (e != cudaSuccess) return e;
         return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p);
     });
 }
@@ -420,6 +687,16 @@ extern "C" int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor 
             invalid("attention: needs query_heads / kv_heads in {1, 2, 4, 8} and head * element "
                     "size a multiple of 16 bytes, head <= 128");
 
+        // this entry launches directly: refuse anything that is not device memory first
+        for (const ab_tensor* t : {&q, &key_cache, &value_cache, &out, &step}) {
+            cudaPointerAttributes attr;
+            if (cudaPointerGetAttributes(&attr, t->data) != cudaSuccess ||
+                (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)) {
+                cudaGetLastError();
+                fail(AB_ERR_ARGUMENT, "ab_attention_decode_noalloc: a tensor pointer is not "
+                                      "device memory");
+            }
+        }
         int device = 0;
         unsigned char* base = noalloc_scratch(&device);
         int sms = 148;

@@ -97,7 +97,7 @@ __device__ __forceinline__ void unit_rows(const GemvParams& p, uint32_t u, const
 }
 
 template <typename WT, int NB, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, 4) gemv_kernel(const GemvParams p) {
     using XS = WT;
     constexpr int V = VecTraits<WT>::V;
     constexpr int CH = 32 * V;  // elements per warp chunk (512 bytes)
@@ -177,7 +177,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
         }
     }
     __syncthreads();
-    pdl_trigger();
 
     // 4. Main loop over this warp's (unit, chunk) range.
     uint32_t idx = wa;
@@ -231,6 +230,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
         idx += c1 - c0;
     }
     __syncthreads();
+
+    // The next kernel may launch now: letting it in earlier takes SM slots while this
+    // kernel still streams (measured slower), so the trigger follows the main loop.
+    pdl_trigger();
 
     // 5. Fold the warps' partial sums in warp order and apply the epilogue.
     for (uint32_t t = tid; t < ucta * NB; t += kGemvThreads) {
@@ -374,7 +377,8 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
         } else {
             q.out = (char*)p.out + (uint64_t)b0 * p.out_stride * dtype_size(p.out_dtype);
         }
-        unsigned grid = (unsigned)std::min<uint64_t>(p.units, (uint64_t)sms * 2);
+        // 4 CTAs (32 warps) per SM keep enough 16-byte loads in flight to cover HBM latency
+        unsigned grid = (unsigned)std::min<uint64_t>(p.units, (uint64_t)sms * 4);
         grid = std::max(1u, grid);
         const uint32_t ucta = (p.units + grid - 1) / grid;
         const size_t smem = (size_t)NB * Kpad * (wdtype == AB_BF16 ? 2 : 4) +

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <functional>
 #include <stdexcept>
 #include <string>
@@ -128,12 +129,23 @@ struct Scheme {
     void release_graph();
 };
 
+// Programmatic dependent launch is on unless AMMON_B200_PDL=0 (a tuning switch: the
+// kernels compute the same results either way).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("AMMON_B200_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 // Launch with optional programmatic dependent launch (PDL): the kernel may begin while
 // its predecessor drains; kernels call griddepcontrol.wait before reading predecessor
 // outputs.
 template <typename... KArgs, typename... Args>
 cudaError_t launch(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl,
                    void (*kernel)(KArgs...), Args... args) {
+    pdl = pdl && pdl_enabled();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;

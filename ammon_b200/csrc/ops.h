@@ -1,11 +1,20 @@
 // Host-side interfaces of the fused decode kernels (gemv.cu, attention.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include "internal.h"
 
 namespace ab {
 
 struct Step;
+
+// Encodes a 2-D tiled TMA descriptor over a row-major [rows, inner] tensor (row stride in
+// bytes), box [box_rows, box_inner], with a 0/32/64/128-byte swizzle. dtype is AB_F32 or
+// AB_BF16. Throws on failure.
+void encode_tmap_2d(CUtensorMap* map, int32_t dtype, const void* base, uint64_t inner,
+                    uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_rows, int swizzle_bytes);
 
 // Prologue applied to the activations a GEMV reads.
 enum GemvPro : int {

@@ -9,8 +9,11 @@
 #include <cstring>
 #include <sstream>
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "internal.h"
+#include "ops.h"
 
 namespace ab {
 
@@ -91,6 +94,36 @@ void Runtime::check_flags() {
         if (f & kFlagWaitTimeout) m += " a bounded wait timed out;";
         fail(AB_ERR_DEVICE, m);
     }
+}
+
+void encode_tmap_2d(CUtensorMap* map, int32_t dtype, const void* base, uint64_t inner,
+                    uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_rows, int swizzle_bytes) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess) fn = nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    }();
+    if (!encode) fail(AB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    if ((uintptr_t)base % 16 || row_stride_bytes % 16)
+        fail(AB_ERR_ARGUMENT, "TMA tensor base and row stride must be 16-byte aligned");
+    CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (swizzle_bytes == 128) swz = CU_TENSOR_MAP_SWIZZLE_128B;
+    else if (swizzle_bytes == 64) swz = CU_TENSOR_MAP_SWIZZLE_64B;
+    else if (swizzle_bytes == 32) swz = CU_TENSOR_MAP_SWIZZLE_32B;
+    cuuint64_t gdim[2] = {inner, rows};
+    cuuint64_t gstride[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = encode(map, dtype == AB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        2, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        fail(AB_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
 }
 
 void Scheme::release_graph() {

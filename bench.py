@@ -224,9 +224,18 @@ def main():
     ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="default: min(steps, 64)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling aid: fewer layers of the same shapes (not a bench line)")
+    ap.add_argument("--prompt", type=int, default=0,
+                    help="profiling aid: shorter prompt (fewer launches before the timed loop)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.layers:
+        w["layers"] = args.layers
+        w["title"] += f" ({args.layers} layers: profiling case)"
+    if args.prompt:
+        w["prompt"] = args.prompt
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

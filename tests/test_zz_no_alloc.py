@@ -78,15 +78,29 @@ def test_noalloc_attention_matches_existing_entry_point(rt, orc, kv_dtype):
 
 
 def test_noalloc_rejects_shapes_beyond_the_static_scratch(rt):
-    """64 heads x 148 splits x 130 floats exceeds the 4 MiB of partials: refused before any
-    launch (no tensor memory is touched, so plain descriptors suffice)."""
+    """batch 64 x 128 heads x (128 + 2) floats exceeds the 4 MiB of partials for any split
+    count, so the call is refused on the host. The tensors are real device allocations all
+    the same, so nothing could read foreign memory even if it were not."""
     lib = _abi.lib()
-    fake = 0x200000
-    q = ab.Tensor(ab.Tensor._desc(fake, ab.F32, (64, 128)))
-    kc = ab.Tensor(ab.Tensor._desc(fake, ab.BF16, (131072, 8, 128)))
-    out = ab.Tensor(ab.Tensor._desc(fake, ab.F32, (64 * 128,)))
-    step = ab.Tensor(ab.Tensor._desc(fake, ab.U32, (1, 2)))
+    B, H, KV, hd, S = 64, 128, 16, 128, 64
+    q = ab.Tensor.zeros(rt, (B, H, hd))
+    kc = ab.Tensor.zeros(rt, (B, S, KV, hd), ab.BF16)
+    out = ab.Tensor.zeros(rt, (B, H * hd))
+    step = ab.DecodeStep.parcel(rt, B)
     status = lib.ab_attention_decode_noalloc(rt.stream, q.t, kc.t, kc.t, out.t, step.t)
     assert status == _abi.AB_ERR_ARGUMENT
     msg = lib.ab_last_error().decode()
     assert "static scratch holds" in msg, msg
+
+
+def test_noalloc_rejects_host_pointers(rt):
+    """A pointer that is not device memory is refused before any launch."""
+    lib = _abi.lib()
+    host = np.zeros(8 * 128, np.float32)
+    q = ab.Tensor(ab.Tensor._desc(host.ctypes.data, ab.F32, (8, 128)))
+    kc = ab.Tensor.zeros(rt, (64, 2, 128), ab.BF16)
+    out = ab.Tensor.zeros(rt, (8 * 128,))
+    step = ab.DecodeStep.parcel(rt)
+    status = lib.ab_attention_decode_noalloc(rt.stream, q.t, kc.t, kc.t, out.t, step.t)
+    assert status == _abi.AB_ERR_ARGUMENT
+    assert "device memory" in lib.ab_last_error().decode()
