@@ -31,12 +31,14 @@ struct ab_attention_block {
     void* attn_out = nullptr;   // [max_batch, heads * head] (f32 or bf16)
     float* part = nullptr;      // split partials
     uint32_t* counters = nullptr;
+    GemmScratch tc;  // tensor-core GEMM scratch (max_batch > kGemvMaxBatch)
 };
 
 struct ab_swiglu_block {
     Runtime* rt;
     uint32_t hidden, inter, max_batch;
     void* hb = nullptr;  // [max_batch, inter] (f32 or bf16)
+    GemmScratch tc;
 };
 
 namespace {
@@ -213,11 +215,13 @@ int ab_attention_block_create(ab_runtime* rt, uint32_t hidden, uint32_t query_he
             b->attn_out = device_alloc(rt, max_batch * qd * 4);
             b->part = (float*)device_alloc(rt, floats * 4);
             b->counters = (uint32_t*)device_alloc(rt, counters * 4);
+            alloc_tc_scratch(rt, &b->tc, max_batch, hidden, (3 * hidden + 127) / 128);
         } catch (...) {
             cudaFree(b->q);
             cudaFree(b->attn_out);
             cudaFree(b->part);
             cudaFree(b->counters);
+            free_tc_scratch(&b->tc);
             delete b;
             throw;
         }
@@ -311,6 +315,7 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         g.cache_stride = cache_stride;
         g.step = st;
         g.flags = flags;
+        attach_tc_scratch(&g, blk->tc);
         // validation is complete: nothing below throws a validation error after the
         // first node is added
         const uint32_t nsplit = attention_choose_splits(
@@ -349,6 +354,7 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         o2.out = x.data;
         o2.out_dtype = AB_F32;
         o2.out_stride = hidden;
+        attach_tc_scratch(&o2, blk->tc);
 
         const size_t before = s->nodes.size();
         try {
@@ -371,6 +377,7 @@ int ab_attention_block_destroy(ab_attention_block* b) {
         cudaFree(b->attn_out);
         cudaFree(b->part);
         cudaFree(b->counters);
+        free_tc_scratch(&b->tc);
         delete b;
     });
 }
@@ -389,7 +396,10 @@ int ab_swiglu_block_create(ab_runtime* rt, uint32_t hidden, uint32_t intermediat
         b->max_batch = max_batch;
         try {
             b->hb = device_alloc(rt, (size_t)max_batch * intermediate * 4);
+            alloc_tc_scratch(rt, &b->tc, max_batch, hidden,
+                             std::max((intermediate + 63) / 64, (hidden + 127) / 128));
         } catch (...) {
+            if (b->hb) cudaFree(b->hb);
             delete b;
             throw;
         }
@@ -434,6 +444,7 @@ int ab_swiglu_block_record(ab_swiglu_block* blk, ab_scheme* s, ab_tensor x,
         g.out = blk->hb;
         g.out_dtype = wdt;
         g.out_stride = inter;
+        attach_tc_scratch(&g, blk->tc);
 
         GemvParams d = {};
         d.seg[0] = w->down.data;
@@ -447,6 +458,7 @@ int ab_swiglu_block_record(ab_swiglu_block* blk, ab_scheme* s, ab_tensor x,
         d.out = x.data;
         d.out_dtype = AB_F32;
         d.out_stride = hidden;
+        attach_tc_scratch(&d, blk->tc);
 
         const size_t before = s->nodes.size();
         try {
@@ -465,6 +477,7 @@ int ab_swiglu_block_destroy(ab_swiglu_block* b) {
         b->rt->activate();
         cudaStreamSynchronize(b->rt->stream);
         cudaFree(b->hb);
+        free_tc_scratch(&b->tc);
         delete b;
     });
 }

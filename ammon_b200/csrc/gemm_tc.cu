@@ -1,0 +1,488 @@
+// Tensor-core decode GEMM for batches above the GEMV's range: out[b, r] = W[r, :] . X[b, :]
+// with W the (virtual) weight matrix and X the batch of bf16 activations. It replaces
+// Goldy's matmul_into (src/kernels.rs:518-528) at batch >= 5 and keeps the GEMV's fused
+// epilogues (RoPE + K/V append, SwiGLU, residual add).
+//
+// Design (B200, sm_100a):
+//  - One CTA computes a 128-row tile of W against all (padded) batch columns BN over a
+//    range of 64-element k-blocks; tiles x k-splits cover the matrix, sized to one wave.
+//  - Warp-specialised: thread 0 issues TMA loads (W tile 128 x 64, X tile BN x 64, both
+//    K-major with the 128-byte swizzle, plain CTA-local copies, no multicast) into a
+//    multi-stage ring guarded by full/empty mbarriers; thread 32 issues
+//    tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> f32) into a TMEM accumulator of BN
+//    columns and commits each stage back to its empty barrier; all four warps then read
+//    their 32 TMEM lanes with tcgen05.ld.
+//  - TMEM is allocated only after griddepcontrol.wait, so a successor launched early by
+//    programmatic dependent launch never holds TMEM that this kernel's later CTAs need.
+//  - Split-K partials go to an L2-resident fp32 workspace; the last CTA of a tile (atomic
+//    ticket) folds them in split order and applies the epilogue.
+//  - Every mbarrier wait is bounded (%globaltimer); a wait that runs out raises the device
+//    flag, and the CTA still releases its TMEM.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+#include "ops.h"
+#include "tma.cuh"
+
+namespace ab {
+
+constexpr int kTcThreads = 128;
+constexpr int kTcBM = 128;
+constexpr int kTcBK = 64;  // bf16 elements per k-block: one 128-byte swizzled row
+constexpr int kTcMaxStages = 8;
+
+// ---- tcgen05 wrappers -------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] x B[smem desc]^T, both K-major.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+    const uint32_t m = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m)
+        : "memory");
+}
+// Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+// 16 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes
+// apart (stride byte offset), leading byte offset unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor of kind::f16: f32 accumulate, bf16 A and B, both K-major.
+__host__ __device__ constexpr uint32_t tc_idesc_bf16(uint32_t M, uint32_t N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// ---- epilogue on a chunk of 16 batch columns held by the thread of TMEM lane `row` ------------
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue_chunk(const GemmTcParams& p, uint32_t tile,
+                                                  uint32_t row, uint32_t c0, const float* v,
+                                                  float* xch) {
+    const uint32_t live = p.nb > c0 ? min(16u, p.nb - c0) : 0u;
+    if (EPI == kEpiSwiglu) {
+        // tile rows 0-63 are w1 rows tile*64 + row, rows 64-127 the matching w3 rows
+        if (row >= 64) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) xch[j * 64 + (row - 64)] = v[j];
+        }
+        __syncthreads();
+        if (row < 64) {
+            const uint32_t u = tile * 64 + row;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                if ((uint32_t)j >= live) break;
+                const float y0 = v[j], y1 = xch[j * 64 + row];
+                const float s = y0 * (1.0f / (1.0f + expf(-y0)));
+                const uint64_t o = (uint64_t)(c0 + j) * p.out_stride + u;
+                if (p.out_dtype == AB_F32) ((float*)p.out)[o] = s * y1;
+                else ((bf16*)p.out)[o] = __float2bfloat16_rn(s * y1);
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    float partner[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) partner[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
+    const uint32_t r = tile * kTcBM + row;
+    if (r >= p.n_rows) return;
+    if (EPI == kEpiStore || EPI == kEpiResidual) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            if ((uint32_t)j >= live) break;
+            const uint64_t o = (uint64_t)(c0 + j) * p.out_stride + r;
+            if (EPI == kEpiResidual) ((float*)p.out)[o] += v[j];
+            else if (p.out_dtype == AB_F32) ((float*)p.out)[o] = v[j];
+            else ((bf16*)p.out)[o] = __float2bfloat16_rn(v[j]);
+        }
+        return;
+    }
+    // kEpiQkv: the even row of each pair rotates / stores both
+    if (r & 1) return;
+#pragma unroll 4
+    for (int j = 0; j < 16; j++) {
+        if ((uint32_t)j >= live) break;
+        const uint32_t b = c0 + j;
+        const float y0 = v[j], y1 = partner[j];
+        const uint32_t pos = p.step[b].position;
+        if (r < p.qd) {
+            float c, s;
+            rope_cos_sin(r, p.head, pos, p.theta, &c, &s);
+            float* q = p.q + (uint64_t)b * p.qd + r;
+            q[0] = y0 * c - y1 * s;
+            q[1] = y0 * s + y1 * c;
+        } else if (pos >= p.seq) {
+            if (r == p.qd) atomicOr(p.flags, kFlagPositionRange);
+        } else if (r < p.qd + p.kvd) {
+            const uint32_t i = r - p.qd;
+            float c, s;
+            rope_cos_sin(i, p.head, pos, p.theta, &c, &s);
+            const uint64_t o = (uint64_t)b * p.cache_stride + (uint64_t)pos * p.kvd + i;
+            if (p.kv_dtype == AB_F32) {
+                ((float*)p.kcache)[o] = y0 * c - y1 * s;
+                ((float*)p.kcache)[o + 1] = y0 * s + y1 * c;
+            } else {
+                ((bf16*)p.kcache)[o] = __float2bfloat16_rn(y0 * c - y1 * s);
+                ((bf16*)p.kcache)[o + 1] = __float2bfloat16_rn(y0 * s + y1 * c);
+            }
+        } else {
+            const uint32_t i = r - p.qd - p.kvd;
+            const uint64_t o = (uint64_t)b * p.cache_stride + (uint64_t)pos * p.kvd + i;
+            if (p.kv_dtype == AB_F32) {
+                ((float*)p.vcache)[o] = y0;
+                ((float*)p.vcache)[o + 1] = y1;
+            } else {
+                ((bf16*)p.vcache)[o] = __float2bfloat16_rn(y0);
+                ((bf16*)p.vcache)[o + 1] = __float2bfloat16_rn(y1);
+            }
+        }
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const GemmTcParams p, const __grid_constant__ CUtensorMap ta0,
+                   const __grid_constant__ CUtensorMap ta1, const __grid_constant__ CUtensorMap ta2,
+                   const __grid_constant__ CUtensorMap tb) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int sm_last;
+    __shared__ int sm_ok;
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t a_bytes = kTcBM * 128;
+    const uint32_t stage_bytes = a_bytes + p.bn * 128;
+    float* xch = (float*)(smem + (size_t)p.stages * stage_bytes);  // [16][64]
+    const uint32_t tile = blockIdx.x, split = blockIdx.y;
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t kb0 = (uint32_t)((uint64_t)split * p.kblocks / p.ksplit);
+    const uint32_t kb1 = (uint32_t)((uint64_t)(split + 1) * p.kblocks / p.ksplit);
+    const uint32_t nk = kb1 - kb0;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < p.stages; s++) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        mbar_init(smem_u32(&done_bar), 1);
+        fence_barrier_init();
+        sm_ok = 1;
+    }
+    // activations come from the previous kernel, and TMEM is taken only after it finished
+    pdl_wait();
+    if (warp == 0) tmem_alloc(smem_u32(&tmem_slot), p.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (threadIdx.x == 0) {
+        // TMA producer
+        for (uint32_t i = 0; i < nk; i++) {
+            const uint32_t s = i % p.stages;
+            if (i >= p.stages &&
+                !mbar_wait_bounded(smem_u32(&empty_bar[s]), ((i / p.stages) - 1) & 1)) {
+                sm_ok = 0;
+                break;
+            }
+            const int32_t kx = (int32_t)((kb0 + i) * kTcBK);
+            const uint32_t bar = smem_u32(&full_bar[s]);
+            const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
+            mbar_arrive_expect_tx(bar, stage_bytes);
+            if (p.interleave) {
+                tma_load_2d(a, &ta0, kx, (int32_t)(tile * 64), bar);
+                tma_load_2d(a + 64 * 128, &ta1, kx, (int32_t)(tile * 64), bar);
+            } else if (tile < p.seg_tiles[0]) {
+                tma_load_2d(a, &ta0, kx, (int32_t)(tile * kTcBM), bar);
+            } else if (tile < p.seg_tiles[0] + p.seg_tiles[1]) {
+                tma_load_2d(a, &ta1, kx, (int32_t)((tile - p.seg_tiles[0]) * kTcBM), bar);
+            } else {
+                tma_load_2d(a, &ta2, kx,
+                            (int32_t)((tile - p.seg_tiles[0] - p.seg_tiles[1]) * kTcBM), bar);
+            }
+            tma_load_2d(a + a_bytes, &tb, kx, 0, bar);
+        }
+    } else if (threadIdx.x == 32) {
+        // MMA issuer
+        const uint32_t idesc = tc_idesc_bf16(kTcBM, p.bn);
+        for (uint32_t i = 0; i < nk; i++) {
+            const uint32_t s = i % p.stages;
+            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+                sm_ok = 0;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
+            const uint32_t b = a + a_bytes;
+#pragma unroll
+            for (uint32_t k = 0; k < kTcBK / 16; k++)
+                tc_mma_bf16(tmem, sw128_desc(a + 32 * k), sw128_desc(b + 32 * k), idesc,
+                            (i | k) != 0);
+            tc_commit(smem_u32(&empty_bar[s]));
+        }
+        tc_commit(smem_u32(&done_bar));
+    }
+    const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0);
+    tc_fence_after();
+    __syncthreads();
+    const bool ok = __syncthreads_and(got && sm_ok != 0);
+    pdl_trigger();
+
+    if (ok) {
+        const uint32_t row = warp * 32 + lane;  // TMEM lane = tile row
+        const uint32_t taddr = tmem + ((warp * 32u) << 16);
+        if (p.ksplit == 1) {
+            for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+                float v[16];
+                tmem_ld16(taddr + c0, v);
+                tc_epilogue_chunk<EPI>(p, tile, row, c0, v, xch);
+            }
+        } else {
+            float* ws = p.ws + ((size_t)split * p.tiles + tile) * p.bn * kTcBM;
+            for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+                float v[16];
+                tmem_ld16(taddr + c0, v);
+#pragma unroll
+                for (int j = 0; j < 16; j++) ws[(size_t)(c0 + j) * kTcBM + row] = v[j];
+            }
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x == 0) sm_last = atomicAdd(p.tickets + tile, 1u) == p.ksplit - 1;
+            __syncthreads();
+            if (sm_last) {
+                __threadfence();
+                for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = 0.0f;
+                    for (uint32_t sp = 0; sp < p.ksplit; sp++) {
+                        const float* w = p.ws + ((size_t)sp * p.tiles + tile) * p.bn * kTcBM;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) v[j] += __ldcg(w + (size_t)(c0 + j) * kTcBM + row);
+                    }
+                    tc_epilogue_chunk<EPI>(p, tile, row, c0, v, xch);
+                }
+                if (threadIdx.x == 0) p.tickets[tile] = 0;
+            }
+        }
+    } else {
+        if (threadIdx.x == 0) {
+            atomicOr(p.flags, kFlagWaitTimeout);
+            // let the committed MMAs drain before TMEM is released
+            mbar_wait_bounded(smem_u32(&done_bar), 0);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, p.tmem_cols);
+    }
+}
+
+// RMSNorm of fp32 rows into bf16 rows (the GEMM's activation operand): o = w * (ss * x),
+// ss = 1 / sqrt(mean(x^2) + eps) (src/kernels.rs:75-101). One 256-thread block per row.
+template <typename WT>
+__global__ void __launch_bounds__(256)
+    rmsnorm_rows_bf16_kernel(const float* __restrict__ x, const WT* __restrict__ w,
+                             bf16* __restrict__ out, uint32_t dim, float eps) {
+    pdl_wait();
+    __shared__ float red[8];
+    const float* xr = x + (uint64_t)blockIdx.x * dim;
+    bf16* orow = out + (uint64_t)blockIdx.x * dim;
+    float ss = 0.0f;
+    for (uint32_t k = threadIdx.x; k < dim; k += 256) ss = fmaf(xr[k], xr[k], ss);
+    ss = warp_sum(ss);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += red[i];
+    const float scale = 1.0f / sqrtf(t / (float)dim + eps);
+    for (uint32_t k = threadIdx.x; k < dim; k += 256)
+        orow[k] = __float2bfloat16_rn(to_f32(w[k]) * (scale * xr[k]));
+    pdl_trigger();
+}
+
+GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave) {
+    GemmTcPlan pl = {};
+    pl.bn = std::max(16u, (batch + 15) / 16 * 16);
+    pl.tiles = interleave ? rows / 64 : (rows + kTcBM - 1) / kTcBM;
+    pl.kblocks = K / kTcBK;
+    const uint32_t stage_bytes = kTcBM * 128 + pl.bn * 128;
+    const uint32_t per_sm = pl.bn <= 128 ? 2 : 1;
+    const uint32_t budget = (per_sm == 2 ? 100u : 200u) * 1024;
+    pl.stages = std::max(2u, std::min((uint32_t)kTcMaxStages, budget / stage_bytes));
+    const uint32_t target = (uint32_t)std::max(sms, 1) * per_sm;
+    uint32_t ks = (target + pl.tiles / 2) / std::max(pl.tiles, 1u);
+    ks = std::min(ks, std::max(1u, pl.kblocks / 4));
+    pl.ksplit = std::max(1u, ks);
+    pl.smem = (size_t)pl.stages * stage_bytes + 16 * 64 * 4 + 1024;
+    uint32_t cols = 32;
+    while (cols < pl.bn) cols <<= 1;
+    pl.tmem_cols = cols;
+    pl.ws_floats = pl.ksplit > 1 ? (uint64_t)pl.ksplit * pl.tiles * pl.bn * kTcBM : 0;
+    return pl;
+}
+
+void gemm_tc_scratch(uint32_t max_tiles, uint32_t max_batch, int sms, uint64_t* ws_floats,
+                     uint32_t* tickets) {
+    // ksplit <= round(target / tiles) keeps ksplit * tiles <= target + tiles
+    const uint32_t bn = std::max(16u, (max_batch + 15) / 16 * 16);
+    const uint64_t target = (uint64_t)std::max(sms, 1) * 2;
+    *ws_floats = (target + max_tiles) * (uint64_t)std::min(bn, 256u) * kTcBM;
+    *tickets = max_tiles;
+}
+
+void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t hidden,
+                      uint32_t max_tiles) {
+    if (max_batch <= kGemvMaxBatch) return;
+    rt->activate();
+    GemmScratch t;
+    try {
+        const size_t xb = (size_t)max_batch * hidden * 2;
+        cuda_check(cudaMalloc(&t.xn, xb), "cudaMalloc");
+        cuda_check(cudaMemset(t.xn, 0, xb), "cudaMemset");
+        gemm_tc_scratch(max_tiles, max_batch, rt->sm_count, &t.ws_floats, &t.tickets_n);
+        cuda_check(cudaMalloc(&t.ws, t.ws_floats * 4), "cudaMalloc");
+        cuda_check(cudaMalloc(&t.tickets, (size_t)t.tickets_n * 4), "cudaMalloc");
+        cuda_check(cudaMemset(t.tickets, 0, (size_t)t.tickets_n * 4), "cudaMemset");
+    } catch (...) {
+        free_tc_scratch(&t);
+        throw;
+    }
+    *g = t;
+}
+
+void free_tc_scratch(GemmScratch* g) {
+    if (g->xn) cudaFree(g->xn);
+    if (g->ws) cudaFree(g->ws);
+    if (g->tickets) cudaFree(g->tickets);
+    *g = GemmScratch();
+}
+
+void attach_tc_scratch(GemvParams* p, const GemmScratch& g) {
+    p->xn = g.xn;
+    p->ws = g.ws;
+    p->ws_floats = g.ws_floats;
+    p->tickets = g.tickets;
+    p->tickets_n = g.tickets_n;
+}
+
+bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave) {
+    if (batch == 0 || batch > 256 || K == 0 || K % kTcBK) return false;
+    return interleave ? rows % 64 == 0 : rows % kTcBM == 0;
+}
+
+template <int EPI>
+static void add_gemm_tc(ab_scheme* s, const char* label, const GemmTcParams& p,
+                        const CUtensorMap* maps, size_t smem) {
+    auto kern = gemm_tc_kernel<EPI>;
+    const CUtensorMap a0 = maps[0], a1 = maps[1], a2 = maps[2], b = maps[3];
+    dim3 grid(p.tiles, p.ksplit);
+    s->add(label, [=](cudaStream_t st) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        return launch(st, grid, dim3(kTcThreads), smem, true, kern, p, a0, a1, a2, b);
+    });
+}
+
+void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void* const* segs,
+                    const uint32_t* seg_rows, int nseg, const void* x_bf16, uint32_t x_stride,
+                    int epi) {
+    const int sms = s->rt ? s->rt->sm_count : 148;
+    uint32_t rows = 0;
+    for (int i = 0; i < nseg; i++) rows += seg_rows[i];
+    if (p.interleave) rows = seg_rows[0];
+    const GemmTcPlan pl = gemm_tc_plan(rows, p.K, p.nb, sms, p.interleave != 0);
+    p.bn = pl.bn;
+    p.tiles = pl.tiles;
+    p.kblocks = pl.kblocks;
+    p.ksplit = pl.ksplit;
+    p.stages = pl.stages;
+    p.tmem_cols = pl.tmem_cols;
+    if (pl.ws_floats > p.ws_floats || (pl.ksplit > 1 && p.tickets_n < pl.tiles))
+        fail(AB_ERR_ARGUMENT, std::string(label) + ": GEMM workspace too small");
+    CUtensorMap maps[4];
+    const uint32_t box_rows = p.interleave ? 64 : kTcBM;
+    for (int i = 0; i < 3; i++) {
+        const int j = i < nseg ? i : 0;
+        p.seg_tiles[i] = i < nseg && !p.interleave ? seg_rows[i] / kTcBM : 0;
+        encode_tmap_2d(&maps[i], AB_BF16, segs[j], p.K, seg_rows[j], (uint64_t)p.K * 2, kTcBK,
+                       box_rows, 128);
+    }
+    encode_tmap_2d(&maps[3], AB_BF16, x_bf16, p.K, p.nb, (uint64_t)x_stride * 2, kTcBK, pl.bn, 128);
+    switch (epi) {
+        case kEpiStore: return add_gemm_tc<kEpiStore>(s, label, p, maps, pl.smem);
+        case kEpiQkv: return add_gemm_tc<kEpiQkv>(s, label, p, maps, pl.smem);
+        case kEpiSwiglu: return add_gemm_tc<kEpiSwiglu>(s, label, p, maps, pl.smem);
+        case kEpiResidual: return add_gemm_tc<kEpiResidual>(s, label, p, maps, pl.smem);
+        default: fail(AB_ERR_ARGUMENT, "unsupported GEMM epilogue");
+    }
+}
+
+void record_rmsnorm_rows_bf16(ab_scheme* s, const char* label, const float* x, const void* w,
+                              int32_t w_dtype, void* out, uint32_t rows, uint32_t dim, float eps) {
+    bf16* o = (bf16*)out;
+    if (w_dtype == AB_F32) {
+        const float* wp = (const float*)w;
+        s->add(label, [=](cudaStream_t st) {
+            return launch(st, dim3(rows), dim3(256), 0, true, rmsnorm_rows_bf16_kernel<float>, x, wp,
+                          o, dim, eps);
+        });
+    } else {
+        const bf16* wp = (const bf16*)w;
+        s->add(label, [=](cudaStream_t st) {
+            return launch(st, dim3(rows), dim3(256), 0, true, rmsnorm_rows_bf16_kernel<bf16>, x, wp,
+                          o, dim, eps);
+        });
+    }
+}
+
+}  // namespace ab

@@ -363,6 +363,56 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
     p.nchunks = (p.K + CH - 1) / CH;
     const uint32_t Kpad = p.nchunks * CH;
     const int sms = s->rt ? s->rt->sm_count : 148;
+    if (wdtype == AB_BF16 && batch > kGemvMaxBatch && p.ws != nullptr) {
+        // a dense contraction: tensor-core tiles read each weight once for the whole batch
+        const bool inter = epi == kEpiSwiglu;
+        int nseg = 0;
+        bool segs_ok = true;
+        for (int i = 0; i < 3; i++) {
+            if (!p.seg_rows[i]) continue;
+            nseg = i + 1;
+            if (!inter && p.seg_rows[i] % 128) segs_ok = false;
+        }
+        const uint32_t rows = inter ? p.seg_rows[0] : p.n_rows;
+        const bool x_ok = pro == kProNorm ? p.xn != nullptr : p.x_dtype == AB_BF16;
+        if (segs_ok && x_ok && gemm_tc_fits(rows, p.K, batch, inter)) {
+            const void* xb = p.x;
+            uint32_t xs = p.x_stride;
+            if (pro == kProNorm) {
+                record_rmsnorm_rows_bf16(s, (std::string(label) + "_norm").c_str(),
+                                         (const float*)p.x, p.norm_w, p.norm_dtype, p.xn, batch,
+                                         p.K, p.eps);
+                xb = p.xn;
+                xs = p.K;
+            }
+            GemmTcParams g = {};
+            g.K = p.K;
+            g.nb = batch;
+            g.interleave = inter ? 1 : 0;
+            g.ws = p.ws;
+            g.ws_floats = p.ws_floats;
+            g.tickets = p.tickets;
+            g.tickets_n = p.tickets_n;
+            g.out = p.out;
+            g.out_dtype = p.out_dtype;
+            g.out_stride = p.out_stride;
+            g.n_rows = p.n_rows;
+            g.q = p.q;
+            g.qd = p.qd;
+            g.kvd = p.kvd;
+            g.head = p.head;
+            g.seq = p.seq;
+            g.theta = p.theta;
+            g.kcache = p.kcache;
+            g.vcache = p.vcache;
+            g.kv_dtype = p.kv_dtype;
+            g.cache_stride = p.cache_stride;
+            g.step = p.step;
+            g.flags = p.flags;
+            record_gemm_tc(s, label, g, p.seg, p.seg_rows, nseg, xb, xs, epi);
+            return;
+        }
+    }
     for (uint32_t b0 = 0; b0 < batch; b0 += 4) {
         const uint32_t nb = std::min(4u, batch - b0);
         const uint32_t NB = nb == 1 ? 1 : nb == 2 ? 2 : 4;

@@ -99,6 +99,7 @@ struct ab_llama {
     ab_tensor x = {}, logits = {}, step = {}, argmax = {}, history = {};
     ab_scheme* scheme = nullptr;       // one decode step
     ab_scheme* loop_scheme = nullptr;  // one decode step + device sample feedback
+    GemmScratch cls_tc;                // classifier's tensor-core GEMM scratch
     float* h_logits = nullptr;  // pinned [batch, vocab]
     int32_t* h_argmax = nullptr;
     ab_decode_step* h_steps = nullptr;
@@ -134,6 +135,7 @@ void destroy_model(ab_llama* m) {
     }
     if (m->scheme) ab_scheme_destroy(m->scheme);
     if (m->loop_scheme) ab_scheme_destroy(m->loop_scheme);
+    free_tc_scratch(&m->cls_tc);
     if (m->attn) ab_attention_block_destroy(m->attn);
     if (m->ffn) ab_swiglu_block_destroy(m->ffn);
     if (m->cache) ab_kvcache_destroy(m->cache);
@@ -184,6 +186,7 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback) {
     g.out = m->logits.data;
     g.out_dtype = AB_F32;
     g.out_stride = c.vocab;
+    attach_tc_scratch(&g, m->cls_tc);
     record_gemv(s, "final_norm_classifier", g, c.dtype, c.batch, kProNorm, kEpiStore);
     const float* lg = (const float*)m->logits.data;
     int32_t* am = (int32_t*)m->argmax.data;
@@ -308,6 +311,7 @@ int ab_llama_create(ab_runtime* rt, const ab_llama_config* cfg, ab_llama** out) 
             check(ab_attention_block_create(rt, c.dim, c.heads, c.seq, c.batch, c.rope_theta,
                                             &m->attn));
             check(ab_swiglu_block_create(rt, c.dim, c.hidden, c.batch, &m->ffn));
+            alloc_tc_scratch(rt, &m->cls_tc, c.batch, c.dim, (c.vocab + 127) / 128);
             m->x = alloc_t(rt, AB_F32, {c.batch, c.dim});
             m->logits = alloc_t(rt, AB_F32, {c.batch, c.vocab});
             m->argmax = alloc_t(rt, AB_U32, {c.batch});

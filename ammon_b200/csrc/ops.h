@@ -62,7 +62,75 @@ struct GemvParams {
     uint64_t cache_stride;  // elements between consecutive batch rows of the cache
     const Step* step;
     uint32_t* flags;
+    // scratch for the tensor-core path at batch > 4 (bf16 weights); null = GEMV only
+    void* xn;        // bf16 [batch, K]: the normalised activation (kProNorm)
+    float* ws;       // split-K partials
+    uint64_t ws_floats;
+    uint32_t* tickets;  // one per row tile, zero between launches
+    uint32_t tickets_n;
 };
+
+// Largest batch the GEMV serves in one launch; above it bf16 weights go to the
+// tensor-core GEMM (gemm_tc.cu).
+constexpr uint32_t kGemvMaxBatch = 4;
+
+// Parameters of one tensor-core GEMM launch (gemm_tc.cu).
+struct GemmTcParams {
+    uint32_t K, nb, bn, tiles, kblocks, ksplit, stages, tmem_cols;
+    uint32_t seg_tiles[3];
+    int32_t interleave;  // tile t = rows [64t, 64t + 64) of segment 0, then of segment 1
+    float* ws;
+    uint64_t ws_floats;
+    uint32_t* tickets;
+    uint32_t tickets_n;
+    // epilogue (as GemvParams)
+    void* out;
+    int32_t out_dtype;
+    uint32_t out_stride;
+    uint32_t n_rows;
+    float* q;
+    uint32_t qd, kvd, head, seq;
+    float theta;
+    void* kcache;
+    void* vcache;
+    int32_t kv_dtype;
+    uint64_t cache_stride;
+    const Step* step;
+    uint32_t* flags;
+};
+
+struct GemmTcPlan {
+    uint32_t bn, tiles, kblocks, ksplit, stages, tmem_cols;
+    size_t smem;
+    uint64_t ws_floats;
+};
+
+GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave);
+bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave);
+void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void* const* segs,
+                    const uint32_t* seg_rows, int nseg, const void* x_bf16, uint32_t x_stride,
+                    int epi);
+void record_rmsnorm_rows_bf16(ab_scheme* s, const char* label, const float* x, const void* w,
+                              int32_t w_dtype, void* out, uint32_t rows, uint32_t dim, float eps);
+// Workspace floats and tickets that cover every tensor-core GEMM with up to `max_tiles`
+// row tiles at batches up to `max_batch`.
+void gemm_tc_scratch(uint32_t max_tiles, uint32_t max_batch, int sms, uint64_t* ws_floats,
+                     uint32_t* tickets);
+
+// Scratch of the tensor-core GEMM path owned by a module: the bf16 normalised
+// activation [max_batch, hidden], the split-K partials and one ticket per row tile.
+// Nothing is allocated when max_batch is within the GEMV's range.
+struct GemmScratch {
+    void* xn = nullptr;
+    float* ws = nullptr;
+    uint64_t ws_floats = 0;
+    uint32_t* tickets = nullptr;
+    uint32_t tickets_n = 0;
+};
+void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t hidden,
+                      uint32_t max_tiles);
+void free_tc_scratch(GemmScratch* g);
+void attach_tc_scratch(GemvParams* p, const GemmScratch& g);
 
 // Records one fused GEMV (weights of dtype wdtype) over batch rows [0, batch).
 void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, uint32_t batch,

@@ -193,6 +193,29 @@ def test_tiny_llama_greedy_tokens_bit_identical(rt, orc):
     assert out_py.tokens == want
 
 
+@pytest.mark.parametrize("batch", [5, 8, 20, 64])
+def test_batched_bf16_model_on_tensor_cores(rt, orc, batch):
+    """Batches above 4 with bf16 weights run every projection on the tcgen05 GEMM (row tiles
+    of 128, split-K where K allows): each stream matches its own oracle decode."""
+    cfg = dict(dim=512, layers=2, heads=8, kv_heads=2, head_dim=64, hidden=1024, vocab=640,
+               seq=24, theta=500000.0)
+    o, g = make_pair(rt, orc, bf16=True, batch=batch, seed=13, **cfg)
+    streams = [0, 1, batch // 2, batch - 1]
+    refs = {b: orc.Model(cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
+                         cfg["head_dim"], cfg["hidden"], cfg["vocab"], cfg["seq"],
+                         theta=cfg["theta"], bf16=True, seed=13) for b in streams}
+    rng = np.random.default_rng(batch)
+    toks = rng.integers(0, cfg["vocab"], size=(5, batch))
+    for pos in range(5):
+        logits, am = g.step_batch(toks[pos].tolist(), [pos] * batch, logits=True, argmax=True)
+        for b in streams:
+            want = refs[b].step(int(toks[pos, b]), pos)
+            assert rel(logits[b], want) < BF16_TOL, (batch, pos, b, rel(logits[b], want))
+        assert all(am[b] == int(np.argmax(logits[b])) for b in range(batch))
+    labels = g.scheme().node_labels()
+    assert "attn_qkv_rope_norm" in labels and "ffn_gate_up_swiglu_norm" in labels
+
+
 def test_device_greedy_loop_matches_host_loop(rt, orc):
     """decode_device (argmax and the next DecodeStep on the device) emits the ids the
     reference loop (generate.rs:43-91 with host sample_argmax) emits."""
