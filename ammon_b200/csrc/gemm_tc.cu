@@ -283,31 +283,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_epilogue_chunk<EPI>(p, tile, row, c0, v, xch);
             }
         } else {
+            // partial of this k-split; splitk_epilogue_kernel folds the splits
             float* ws = p.ws + ((size_t)split * p.tiles + tile) * p.bn * kTcBM;
             for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
                 float v[16];
                 tmem_ld16(taddr + c0, v);
 #pragma unroll
                 for (int j = 0; j < 16; j++) ws[(size_t)(c0 + j) * kTcBM + row] = v[j];
-            }
-            __threadfence();
-            __syncthreads();
-            if (threadIdx.x == 0) sm_last = atomicAdd(p.tickets + tile, 1u) == p.ksplit - 1;
-            __syncthreads();
-            if (sm_last) {
-                __threadfence();
-                for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
-                    float v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] = 0.0f;
-                    for (uint32_t sp = 0; sp < p.ksplit; sp++) {
-                        const float* w = p.ws + ((size_t)sp * p.tiles + tile) * p.bn * kTcBM;
-#pragma unroll
-                        for (int j = 0; j < 16; j++) v[j] += __ldcg(w + (size_t)(c0 + j) * kTcBM + row);
-                    }
-                    tc_epilogue_chunk<EPI>(p, tile, row, c0, v, xch);
-                }
-                if (threadIdx.x == 0) p.tickets[tile] = 0;
             }
         }
     } else {
@@ -347,6 +329,109 @@ __global__ void __launch_bounds__(256)
     for (uint32_t k = threadIdx.x; k < dim; k += 256)
         orow[k] = __float2bfloat16_rn(to_f32(w[k]) * (scale * xr[k]));
     pdl_trigger();
+}
+
+// Folds the k-split partials of the tensor-core GEMM (ws[split][tile][col][row]) in split
+// order and applies the epilogue. Thread -> (column, 4 consecutive rows) of a tile: float4
+// loads of every split are independent, and each thread holds whole row pairs.
+// Grid (tiles, ceil(bn / 8)), 256 threads = 8 columns x 32 row quads.
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_epilogue_kernel(const GemmTcParams p) {
+    const uint32_t tile = blockIdx.x;
+    const uint32_t col = blockIdx.y * 8 + threadIdx.x / 32;
+    const uint32_t quad = threadIdx.x % 32;
+    const uint32_t r4 = quad * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col < p.bn) {
+        const size_t stride = (size_t)p.tiles * p.bn * kTcBM;
+        const float* base = p.ws + ((size_t)tile * p.bn + col) * kTcBM + r4;
+        uint32_t sp = 0;
+        for (; sp + 4 <= p.ksplit; sp += 4) {
+            const float4 a = __ldcg((const float4*)(base + sp * stride));
+            const float4 b = __ldcg((const float4*)(base + (sp + 1) * stride));
+            const float4 c = __ldcg((const float4*)(base + (sp + 2) * stride));
+            const float4 d = __ldcg((const float4*)(base + (sp + 3) * stride));
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+            acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
+            acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
+            acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+        }
+        for (; sp < p.ksplit; sp++) {
+            const float4 a = __ldcg((const float4*)(base + sp * stride));
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+        }
+    }
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (EPI == kEpiSwiglu) {
+        // rows 0-63 (w1) pair with rows 64-127 (w3): quad k with quad k + 16
+        float h3[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) h3[i] = __shfl_down_sync(0xffffffffu, v[i], 16);
+        if (quad >= 16 || col >= p.nb) return;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t u = tile * 64 + r4 + i;
+            const float s = v[i] * (1.0f / (1.0f + expf(-v[i])));
+            const uint64_t o = (uint64_t)col * p.out_stride + u;
+            if (p.out_dtype == AB_F32) ((float*)p.out)[o] = s * h3[i];
+            else ((bf16*)p.out)[o] = __float2bfloat16_rn(s * h3[i]);
+        }
+        return;
+    }
+    if (col >= p.nb) return;
+#pragma unroll
+    for (int i = 0; i < 4; i += 2) {
+        const uint32_t r = tile * kTcBM + r4 + i;
+        if (r >= p.n_rows) return;
+        const float y0 = v[i], y1 = v[i + 1];
+        const uint64_t o = (uint64_t)col * p.out_stride + r;
+        if (EPI == kEpiResidual) {
+            float* out = (float*)p.out;
+            out[o] += y0;
+            if (r + 1 < p.n_rows) out[o + 1] += y1;
+        } else if (EPI == kEpiStore) {
+            if (p.out_dtype == AB_F32) {
+                ((float*)p.out)[o] = y0;
+                if (r + 1 < p.n_rows) ((float*)p.out)[o + 1] = y1;
+            } else {
+                ((bf16*)p.out)[o] = __float2bfloat16_rn(y0);
+                if (r + 1 < p.n_rows) ((bf16*)p.out)[o + 1] = __float2bfloat16_rn(y1);
+            }
+        } else {  // kEpiQkv
+            const uint32_t pos = p.step[col].position;
+            if (r < p.qd) {
+                float c, s;
+                rope_cos_sin(r, p.head, pos, p.theta, &c, &s);
+                float* q = p.q + (uint64_t)col * p.qd + r;
+                q[0] = y0 * c - y1 * s;
+                q[1] = y0 * s + y1 * c;
+            } else if (pos >= p.seq) {
+                if (r == p.qd) atomicOr(p.flags, kFlagPositionRange);
+            } else if (r < p.qd + p.kvd) {
+                const uint32_t k = r - p.qd;
+                float c, s;
+                rope_cos_sin(k, p.head, pos, p.theta, &c, &s);
+                const uint64_t ko = (uint64_t)col * p.cache_stride + (uint64_t)pos * p.kvd + k;
+                if (p.kv_dtype == AB_F32) {
+                    ((float*)p.kcache)[ko] = y0 * c - y1 * s;
+                    ((float*)p.kcache)[ko + 1] = y0 * s + y1 * c;
+                } else {
+                    ((bf16*)p.kcache)[ko] = __float2bfloat16_rn(y0 * c - y1 * s);
+                    ((bf16*)p.kcache)[ko + 1] = __float2bfloat16_rn(y0 * s + y1 * c);
+                }
+            } else {
+                const uint32_t k = r - p.qd - p.kvd;
+                const uint64_t vo = (uint64_t)col * p.cache_stride + (uint64_t)pos * p.kvd + k;
+                if (p.kv_dtype == AB_F32) {
+                    ((float*)p.vcache)[vo] = y0;
+                    ((float*)p.vcache)[vo + 1] = y1;
+                } else {
+                    ((bf16*)p.vcache)[vo] = __float2bfloat16_rn(y0);
+                    ((bf16*)p.vcache)[vo + 1] = __float2bfloat16_rn(y1);
+                }
+            }
+        }
+    }
 }
 
 GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave) {
@@ -431,6 +516,13 @@ static void add_gemm_tc(ab_scheme* s, const char* label, const GemmTcParams& p,
         if (e != cudaSuccess) return e;
         return launch(st, grid, dim3(kTcThreads), smem, true, kern, p, a0, a1, a2, b);
     });
+    if (p.ksplit > 1) {
+        auto fold = splitk_epilogue_kernel<EPI>;
+        dim3 fgrid(p.tiles, (p.bn + 7) / 8);
+        s->add((std::string(label) + "_splitk").c_str(), [=](cudaStream_t st) {
+            return launch(st, fgrid, dim3(256), 0, true, fold, p);
+        });
+    }
 }
 
 void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void* const* segs,

@@ -228,6 +228,8 @@ def main():
                     help="profiling aid: fewer layers of the same shapes (not a bench line)")
     ap.add_argument("--prompt", type=int, default=0,
                     help="profiling aid: shorter prompt (fewer launches before the timed loop)")
+    ap.add_argument("--seq", type=int, default=0,
+                    help="profiling aid: smaller KV cache (max context)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = dict(WORKLOADS[args.workload])
@@ -236,6 +238,8 @@ def main():
         w["title"] += f" ({args.layers} layers: profiling case)"
     if args.prompt:
         w["prompt"] = args.prompt
+    if args.seq:
+        w["seq"] = args.seq
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
