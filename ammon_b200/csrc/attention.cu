@@ -251,6 +251,7 @@ __device__ __forceinline__ void attn_split_range(const AttnParams& p, uint32_t s
     const uint32_t total = bad ? 0u : pos + 1;
     uint32_t chunk = (total + p.nsplit - 1) / p.nsplit;
     chunk = max(1u, (chunk + kAttnTile - 1) / kAttnTile) * kAttnTile;
+    chunk = max(chunk, p.min_chunk);
     *active = max(1u, (total + chunk - 1) / chunk);
     *start = min(split * chunk, total);
     *end = min(*start + chunk, total);
@@ -407,6 +408,279 @@ __global__ void __launch_bounds__(kAttnThreads)
                        b, tid);
 }
 
+// ---- tensor-core kernel (bf16 K/V, head 64 or 128) --------------------------------------------
+// Same algorithm and TMA pipeline as above, with both products on mma.sync m16n8k16:
+//   S^T[64 pos x 8 heads] = K[64 x head] . Q^T[head x 8]   (each warp: 16 positions)
+//   O^T[head x 8]        += V^T[head x 64] . P^T[64 x 8]    (each warp: head/4 dims)
+// Q and P are split into bf16 high and low parts (two MMAs each), so scores and
+// weights keep close to fp32 precision; K and V are bf16 already. Operand fragments
+// come from the swizzled TMA tiles through ldmatrix (V transposed).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Two floats as a bf16 pair (first in the low half) and the pair of what rounding left.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t* hi, uint32_t* lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    *hi = *reinterpret_cast<const uint32_t*>(&h);
+    *lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int HD>
+struct AttnMmaLayout {
+    static constexpr uint32_t kRowBytes = HD * 2;
+    static constexpr uint32_t kStage = 2 * kAttnTile * kRowBytes;
+    static constexpr uint32_t kP = kAttnStages * kStage;  // [2 parts][8 heads][64 pos] bf16
+    static constexpr uint32_t kO = kP + 2 * 8 * kAttnTile * 2;  // [8][HD] f32
+    static constexpr uint32_t kTail = kO + 8 * HD * 4;
+};
+
+template <typename OT, int G, int HD>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_decode_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap) {
+    using LY = AttnMmaLayout<HD>;
+    constexpr uint32_t NBOX = LY::kRowBytes / 128;
+    constexpr int MT = HD / 64;  // 16-dim m-tiles per warp in P.V
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kAttnStages];
+    __shared__ float red[4][8];
+    __shared__ float run_m[8], run_l[8], run_a[8];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const AttnTail T = attn_tail(LY::kTail, HD, G, p.nsplit);
+    bf16* pbuf = (bf16*)(smem + LY::kP);
+    float* obuf = (float*)(smem + LY::kO);
+    float* fold = (float*)(smem + T.fold_off);
+    float* wts = (float*)(smem + T.w_off);
+    int* sm_last = (int*)(smem + T.st_off);
+
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    const uint32_t g = lane / 4, t = lane % 4;
+
+    pdl_wait();
+    uint32_t start, end, active;
+    attn_split_range(p, split, b, &start, &end, &active);
+    if (split >= active) {
+        pdl_trigger();
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kAttnStages; s++) mbar_init(smem_u32(&full_bar[s]), 1);
+        fence_barrier_init();
+    }
+    if (tid < 8) {
+        run_m[tid] = -INFINITY;
+        run_l[tid] = 0.0f;
+    }
+    // Q^T fragments (k = head dim, n = query head), pre-scaled, bf16 high + low parts
+    uint32_t qh[HD / 16][2], ql[HD / 16][2];
+    {
+        const float qscale = 1.0f / sqrtf((float)HD);
+        const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * HD;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ks++) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; h2++) {
+                const uint32_t d = ks * 16 + 2 * t + 8 * h2;
+                float a = 0.0f, c = 0.0f;
+                if (g < (uint32_t)G) {
+                    a = qsrc[g * HD + d] * qscale;
+                    c = qsrc[g * HD + d + 1] * qscale;
+                }
+                split_bf16x2(a, c, &qh[ks][h2], &ql[ks][h2]);
+            }
+        }
+    }
+    float o[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; m++) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.0f;
+    __syncthreads();
+
+    const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
+    const int32_t ybase = (int32_t)(b * p.seq + start);
+    auto issue = [&](uint32_t i) {
+        const uint32_t s = i % kAttnStages;
+        const uint32_t bar = smem_u32(&full_bar[s]);
+        unsigned char* kst = smem + (size_t)s * LY::kStage;
+        unsigned char* vst = kst + LY::kStage / 2;
+        mbar_arrive_expect_tx(bar, LY::kStage);
+        const int32_t y = ybase + (int32_t)(i * kAttnTile);
+#pragma unroll
+        for (uint32_t j = 0; j < NBOX; j++) {
+            const int32_t x = (int32_t)(kvh * HD + j * 64);
+            tma_load_2d(smem_u32(kst + j * kAttnTile * 128), &kmap, x, y, bar);
+            tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
+        }
+    };
+    if (tid == 0)
+        for (uint32_t i = 0; i < ntiles && i < (uint32_t)kAttnStages; i++) issue(i);
+
+    uint32_t failed_at = ntiles;
+    for (uint32_t i = 0; i < ntiles; i++) {
+        const uint32_t s = i % kAttnStages;
+        const bool got = mbar_wait_bounded(smem_u32(&full_bar[s]), (i / kAttnStages) & 1);
+        if (!__syncthreads_and(got)) {
+            failed_at = i;
+            break;
+        }
+        const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
+        const uint32_t kst = smem_u32(smem + (size_t)s * LY::kStage);
+        const uint32_t vst = kst + LY::kStage / 2;
+        // S^T for positions 16*warp .. +15
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        {
+            const uint32_t row = warp * 16 + (lane % 16);
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ks++) {
+                const uint32_t colb = (ks % 4) * 32 + (lane / 16) * 16;
+                uint32_t a[4];
+                ldsm_x4(kst + swizzle_off<128>((ks / 4) * kAttnTile * 128 + row * 128 + colb), a);
+                mma_16816(sc, a, qh[ks][0], qh[ks][1]);
+                mma_16816(sc, a, ql[ks][0], ql[ks][1]);
+            }
+        }
+        const uint32_t p0 = warp * 16 + g, p1 = p0 + 8;
+        if (p0 >= rows) sc[0] = sc[1] = -INFINITY;
+        if (p1 >= rows) sc[2] = sc[3] = -INFINITY;
+        // tile maximum per head (heads 2t, 2t+1 live in this thread)
+        float ma = fmaxf(sc[0], sc[2]), mb = fmaxf(sc[1], sc[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, off));
+            mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        }
+        if (g == 0) {
+            red[warp][2 * t] = ma;
+            red[warp][2 * t + 1] = mb;
+        }
+        __syncthreads();
+        if (tid < 8) {
+            const float tmax = fmaxf(fmaxf(red[0][tid], red[1][tid]), fmaxf(red[2][tid], red[3][tid]));
+            const float mnew = fmaxf(run_m[tid], tmax);
+            run_a[tid] = expf(run_m[tid] - mnew);
+            run_m[tid] = mnew;
+        }
+        __syncthreads();
+        const float m0 = run_m[2 * t], m1 = run_m[2 * t + 1];
+        const float e0 = expf(sc[0] - m0), e1 = expf(sc[1] - m1);
+        const float e2 = expf(sc[2] - m0), e3 = expf(sc[3] - m1);
+        float la = e0 + e2, lb = e1 + e3;
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            la += __shfl_xor_sync(0xffffffffu, la, off);
+            lb += __shfl_xor_sync(0xffffffffu, lb, off);
+        }
+        // P^T (bf16 high / low) as [part][head][position]
+        {
+            uint32_t h01, l01, h23, l23;
+            split_bf16x2(e0, e1, &h01, &l01);  // (p0, heads 2t / 2t+1)
+            split_bf16x2(e2, e3, &h23, &l23);  // (p1, ...)
+            const __nv_bfloat162 H01 = *reinterpret_cast<__nv_bfloat162*>(&h01);
+            const __nv_bfloat162 L01 = *reinterpret_cast<__nv_bfloat162*>(&l01);
+            const __nv_bfloat162 H23 = *reinterpret_cast<__nv_bfloat162*>(&h23);
+            const __nv_bfloat162 L23 = *reinterpret_cast<__nv_bfloat162*>(&l23);
+            bf16* ph = pbuf;
+            bf16* pl = pbuf + 8 * kAttnTile;
+            ph[(2 * t) * kAttnTile + p0] = H01.x;
+            ph[(2 * t + 1) * kAttnTile + p0] = H01.y;
+            ph[(2 * t) * kAttnTile + p1] = H23.x;
+            ph[(2 * t + 1) * kAttnTile + p1] = H23.y;
+            pl[(2 * t) * kAttnTile + p0] = L01.x;
+            pl[(2 * t + 1) * kAttnTile + p0] = L01.y;
+            pl[(2 * t) * kAttnTile + p1] = L23.x;
+            pl[(2 * t + 1) * kAttnTile + p1] = L23.y;
+        }
+        __syncthreads();
+        if (g == 0) {
+            red[warp][2 * t] = la;
+            red[warp][2 * t + 1] = lb;
+        }
+        // O^T += V^T . P^T for dims [warp * HD/4, +HD/4)
+        {
+            const float a0 = run_a[2 * t], a1 = run_a[2 * t + 1];
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                o[m][0] *= a0;
+                o[m][1] *= a1;
+                o[m][2] *= a0;
+                o[m][3] *= a1;
+            }
+            const uint32_t* phw = reinterpret_cast<const uint32_t*>(pbuf);
+            const uint32_t* plw = reinterpret_cast<const uint32_t*>(pbuf + 8 * kAttnTile);
+            const uint32_t mi = lane / 8, r8 = lane % 8;
+#pragma unroll
+            for (int ks = 0; ks < kAttnTile / 16; ks++) {
+                const uint32_t bi = (g * kAttnTile + ks * 16 + 2 * t) / 2;
+                const uint32_t bh0 = phw[bi], bh1 = phw[bi + 4];
+                const uint32_t bl0 = plw[bi], bl1 = plw[bi + 4];
+                const uint32_t pos = ks * 16 + r8 + (mi >= 2 ? 8 : 0);
+#pragma unroll
+                for (int m = 0; m < MT; m++) {
+                    const uint32_t dim = warp * (HD / 4) + m * 16 + ((mi & 1) ? 8 : 0);
+                    const uint32_t byte = dim * 2;
+                    uint32_t a[4];
+                    ldsm_x4_t(vst + swizzle_off<128>((byte / 128) * kAttnTile * 128 + pos * 128 +
+                                                     byte % 128),
+                              a);
+                    mma_16816(o[m], a, bh0, bh1);
+                    mma_16816(o[m], a, bl0, bl1);
+                }
+            }
+        }
+        __syncthreads();
+        if (tid < 8)
+            run_l[tid] = run_l[tid] * run_a[tid] + red[0][tid] + red[1][tid] + red[2][tid] +
+                         red[3][tid];
+        if (tid == 0 && i + kAttnStages < ntiles) issue(i + kAttnStages);
+    }
+    if (failed_at < ntiles) {
+        if (tid == 0) {
+            atomicOr(p.flags, kFlagWaitTimeout);
+            for (uint32_t i = failed_at; i < ntiles && i < failed_at + kAttnStages; i++)
+                mbar_wait_bounded(smem_u32(&full_bar[i % kAttnStages]), (i / kAttnStages) & 1);
+        }
+        __syncthreads();
+        pdl_trigger();
+        return;
+    }
+    pdl_trigger();
+    // O^T fragments -> obuf[head][dim]
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        const uint32_t d0 = warp * (HD / 4) + m * 16 + g;
+        if (2 * t < (uint32_t)G) {
+            obuf[(2 * t) * HD + d0] = o[m][0];
+            obuf[(2 * t) * HD + d0 + 8] = o[m][2];
+        }
+        if (2 * t + 1 < (uint32_t)G) {
+            obuf[(2 * t + 1) * HD + d0] = o[m][1];
+            obuf[(2 * t + 1) * HD + d0 + 8] = o[m][3];
+        }
+    }
+    __syncthreads();
+    float acc[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) acc[h] = tid < (uint32_t)HD ? obuf[h * HD + tid] : 0.0f;
+    attn_finish<OT, G>(p, acc, tid / HD, 1, tid % HD, fold, wts, run_m, run_l, sm_last, split,
+                       active, kvh, b, tid);
+}
+
 // ---- plain-load kernel (head sizes the TMA boxes cannot tile) --------------------------------
 template <typename KT, typename OT, int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
@@ -554,6 +828,33 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
     const uint32_t rowbytes = p.head * esz;
     dim3 grid(p.nsplit, p.kv_heads, p.batch);
     const int swz = rowbytes % 128 == 0 ? 128 : rowbytes % 64 == 0 ? 64 : 0;
+    if (esz == 2 && (p.head == 128 || p.head == 64)) {
+        // bf16 K/V: both products on the tensor cores
+        CUtensorMap kmap, vmap;
+        const uint64_t inner = (uint64_t)p.kv_heads * p.head;
+        const uint64_t rows = (uint64_t)p.batch * p.seq;
+        encode_tmap_2d(&kmap, AB_BF16, p.kcache, inner, rows, inner * 2, 64, kAttnTile, 128);
+        encode_tmap_2d(&vmap, AB_BF16, p.vcache, inner, rows, inner * 2, 64, kAttnTile, 128);
+        const uint32_t tail = p.head == 128 ? AttnMmaLayout<128>::kTail : AttnMmaLayout<64>::kTail;
+        const size_t smem = attn_tail(tail, p.head, G, p.nsplit).end + 1024;
+        if (smem > 220 * 1024) invalid("attention: shared-memory stage too large");
+        if (p.head == 128) {
+            auto kern = attn_decode_mma_kernel<OT, G, 128>;
+            s->add(label, [=](cudaStream_t st) {
+                cudaError_t e = set_smem((const void*)kern, smem);
+                if (e != cudaSuccess) return e;
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+            });
+        } else {
+            auto kern = attn_decode_mma_kernel<OT, G, 64>;
+            s->add(label, [=](cudaStream_t st) {
+                cudaError_t e = set_smem((const void*)kern, smem);
+                if (e != cudaSuccess) return e;
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+            });
+        }
+        return;
+    }
     if (swz) {
         CUtensorMap kmap, vmap;
         const uint64_t inner = (uint64_t)p.kv_heads * p.head;

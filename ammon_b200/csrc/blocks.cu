@@ -334,6 +334,11 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         a.seq = blk->seq;
         a.batch = batch;
         a.nsplit = nsplit;
+        // with a (batch, kv head) group per SM or more, short contexts are not split: a
+        // split pays a partial write and a fold, and the groups already fill the GPU
+        a.min_chunk = (uint64_t)batch * kv_heads >= (uint64_t)(s->rt ? s->rt->sm_count : 148)
+                          ? 256u
+                          : 0u;
         uint64_t floats = 0, counters = 0;
         attention_scratch_size(batch, heads, head, nsplit, &floats, &counters);
         a.part_o = blk->part;

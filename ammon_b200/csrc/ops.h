@@ -150,6 +150,7 @@ struct AttnParams {
     int32_t out_dtype;
     uint32_t heads, kv_heads, head, seq, batch;
     uint32_t nsplit;
+    uint32_t min_chunk;  // fewest positions per split (a multiple of 64; 0 = 64)
     float* part_o;   // [B, KV, nsplit, g, hd]
     float* part_ml;  // [B, KV, nsplit, g, 2]
     uint32_t* counters;  // [B, KV], zero between launches
