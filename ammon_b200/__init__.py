@@ -512,19 +512,66 @@ class LlamaConfig:
         return elems * (2 if self.dtype == AB_BF16 else 4)
 
 
+class Comm:
+    """NCCL communicator of one rank (tensor parallelism over NVLink). Rank 0 makes the id
+    with ``Comm.unique_id()`` and shares it with the other ranks (e.g. a torch.distributed
+    broadcast); every rank then builds its Comm with the same id."""
+
+    def __init__(self, rt: Runtime, uid: bytes, rank: int, world: int):
+        if len(uid) != _abi.COMM_ID_BYTES:
+            raise ValueError("communicator id must be 128 bytes")
+        buf = (C.c_uint8 * _abi.COMM_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        _check(_abi.lib().ab_comm_create(rt.handle, buf, rank, world, C.byref(h)))
+        self._h = h
+        self.rt = rt
+        self.rank, self.world = rank, world
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * _abi.COMM_ID_BYTES)()
+        _check(_abi.lib().ab_comm_unique_id(buf))
+        return bytes(buf)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def abort(self):
+        if getattr(self, "_h", None):
+            _abi.lib().ab_comm_abort(self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _abi.lib().ab_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class LlamaModel:
     """Llama-shaped decode model on the fused kernels (an architecture-crate role the
-    reference leaves open, README.md:5,21). ``step`` is AutoregressiveModel::step."""
+    reference leaves open, README.md:5,21). ``step`` is AutoregressiveModel::step.
+    With ``comm`` the model is this rank's tensor-parallel shard."""
 
-    def __init__(self, rt: Runtime, cfg: LlamaConfig):
+    def __init__(self, rt: Runtime, cfg: LlamaConfig, comm: Optional[Comm] = None):
         c = _abi.LlamaConfig_t(cfg.dim, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim,
                                cfg.hidden, cfg.vocab, cfg.seq, cfg.batch, cfg.rope_theta,
                                cfg.norm_eps, cfg.dtype)
         h = C.c_void_p()
-        _check(_abi.lib().ab_llama_create(rt.handle, C.byref(c), C.byref(h)))
+        if comm is None:
+            _check(_abi.lib().ab_llama_create(rt.handle, C.byref(c), C.byref(h)))
+        else:
+            _check(_abi.lib().ab_llama_create_tp(rt.handle, C.byref(c), comm.handle,
+                                                 C.byref(h)))
         self._h = h
         self.rt = rt
         self.cfg = cfg
+        self.comm = comm
         self._logits = np.zeros((cfg.batch, cfg.vocab), np.float32)
         self._argmax = np.zeros(cfg.batch, np.int32)
 
@@ -666,7 +713,7 @@ __all__ = [
     "AmmonError", "ValidationError", "DeviceError", "Runtime", "create_runtime", "Tensor",
     "DecodeStep", "Scheme", "Embedding", "RmsNorm", "Linear", "KvCache", "KvLayer",
     "CausalAttentionBlock", "CausalAttentionBlockWeights", "SwiGluBlock",
-    "SwiGluBlockWeights", "LlamaConfig", "LlamaModel", "AutoregressiveModel",
+    "SwiGluBlockWeights", "LlamaConfig", "LlamaModel", "Comm", "AutoregressiveModel",
     "generate_tokens", "generate", "GenerateOptions", "GenerateOutput", "GenerateTokenOutput",
     "sample_argmax", "BpeTokenizer", "Tokenizer", "kernels", "DEFAULT_ROPE_THETA",
     "ATTENTION_SPLIT", "ATTENTION_MAX_HEAD", "F32", "BF16", "U32", "load",

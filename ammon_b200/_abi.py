@@ -130,7 +130,16 @@ SIGNATURES = {
     "ab_llama_reset": (C.c_int, [P]),
     "ab_llama_as_model": (C.c_int, [P, C.POINTER(Model_t)]),
     "ab_llama_destroy": (C.c_int, [P]),
+    "ab_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
+    "ab_comm_create": (C.c_int, [P, C.POINTER(C.c_uint8), i32, i32, PP]),
+    "ab_comm_rank": (C.c_int, [P, C.POINTER(i32), C.POINTER(i32)]),
+    "ab_comm_abort": (C.c_int, [P]),
+    "ab_comm_destroy": (C.c_int, [P]),
+    "ab_comm_last_error": (C.c_char_p, []),
+    "ab_llama_create_tp": (C.c_int, [P, C.POINTER(LlamaConfig_t), P, PP]),
 }
+
+COMM_ID_BYTES = 128
 
 _lib = None
 

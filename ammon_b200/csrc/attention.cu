@@ -6,7 +6,7 @@
 //    from one staged K/V tile, so K/V bytes are read once per kv head rather than once
 //    per query head.
 //  - K/V tiles of 64 positions are staged in shared memory by TMA (2-D tensor maps over
-//    the cache, no multicast), double-buffered on mbarriers, in the 32/64/128-byte
+//    the cache, CTA-local copies), double-buffered on mbarriers, in the 32/64/128-byte
 //    swizzle that lets row-parallel lanes read distinct banks. Head sizes TMA cannot tile
 //    use the same algorithm with plain 16-byte loads into padded rows.
 //  - The position range [0, pos] is cut into `nsplit` chunks (multiples of the 64-row

@@ -32,6 +32,8 @@ struct ab_attention_block {
     float* part = nullptr;      // split partials
     uint32_t* counters = nullptr;
     GemmScratch tc;  // tensor-core GEMM scratch (max_batch > kGemvMaxBatch)
+    ab_comm* tp = nullptr;   // tensor parallelism: wo output is all-reduced into x
+    float* tp_y = nullptr;   // [max_batch, hidden] partial projection
 };
 
 struct ab_swiglu_block {
@@ -39,6 +41,8 @@ struct ab_swiglu_block {
     uint32_t hidden, inter, max_batch;
     void* hb = nullptr;  // [max_batch, inter] (f32 or bf16)
     GemmScratch tc;
+    ab_comm* tp = nullptr;
+    float* tp_y = nullptr;
 };
 
 namespace {
@@ -74,6 +78,75 @@ void* device_alloc(Runtime* rt, size_t bytes) {
 }
 
 }  // namespace
+
+namespace ab {
+
+ab_attention_block* attention_block_new(ab_runtime* rt, uint32_t hidden, uint32_t heads,
+                                        uint32_t head, uint32_t seq_len, uint32_t max_batch,
+                                        float rope_theta, ab_comm* tp) {
+    if (!heads || !head) fail(AB_ERR_ARGUMENT, "query_heads and head size must be > 0");
+    if (!seq_len || !max_batch) fail(AB_ERR_ARGUMENT, "seq_len and max_batch must be > 0");
+    auto* b = new ab_attention_block();
+    b->rt = rt;
+    b->hidden = hidden;
+    b->heads = heads;
+    b->head = head;
+    b->seq = seq_len;
+    b->max_batch = max_batch;
+    b->theta = rope_theta;
+    b->tp = tp;
+    // worst case over kv_heads (1 kv head gives the most splits per group)
+    b->nsplit_max = attention_choose_splits(max_batch, 1, seq_len, rt->sm_count, 256);
+    uint64_t floats = 0, counters = 0;
+    attention_scratch_size(max_batch, heads, head, b->nsplit_max, &floats, &counters);
+    const uint64_t qd = (uint64_t)heads * head;
+    try {
+        b->q = (float*)device_alloc(rt, max_batch * qd * 4);
+        b->attn_out = device_alloc(rt, max_batch * qd * 4);
+        b->part = (float*)device_alloc(rt, floats * 4);
+        b->counters = (uint32_t*)device_alloc(rt, counters * 4);
+        if (tp) b->tp_y = (float*)device_alloc(rt, (size_t)max_batch * hidden * 4);
+        alloc_tc_scratch(rt, &b->tc, max_batch, hidden,
+                         (uint32_t)((3 * std::max<uint64_t>(qd, hidden) + 127) / 128));
+    } catch (...) {
+        cudaFree(b->q);
+        cudaFree(b->attn_out);
+        cudaFree(b->part);
+        cudaFree(b->counters);
+        if (b->tp_y) cudaFree(b->tp_y);
+        free_tc_scratch(&b->tc);
+        delete b;
+        throw;
+    }
+    return b;
+}
+
+ab_swiglu_block* swiglu_block_new(ab_runtime* rt, uint32_t hidden, uint32_t intermediate,
+                                  uint32_t max_batch, ab_comm* tp) {
+    if (!hidden || !intermediate || !max_batch)
+        fail(AB_ERR_ARGUMENT, "hidden, intermediate and max_batch must be > 0");
+    auto* b = new ab_swiglu_block();
+    b->rt = rt;
+    b->hidden = hidden;
+    b->inter = intermediate;
+    b->max_batch = max_batch;
+    b->tp = tp;
+    try {
+        b->hb = device_alloc(rt, (size_t)max_batch * intermediate * 4);
+        if (tp) b->tp_y = (float*)device_alloc(rt, (size_t)max_batch * hidden * 4);
+        alloc_tc_scratch(rt, &b->tc, max_batch, hidden,
+                         std::max((intermediate + 63) / 64, (hidden + 127) / 128));
+    } catch (...) {
+        if (b->hb) cudaFree(b->hb);
+        if (b->tp_y) cudaFree(b->tp_y);
+        free_tc_scratch(&b->tc);
+        delete b;
+        throw;
+    }
+    return b;
+}
+
+}  // namespace ab
 
 extern "C" {
 
@@ -196,36 +269,8 @@ int ab_attention_block_create(ab_runtime* rt, uint32_t hidden, uint32_t query_he
             fail(AB_ERR_VALIDATION, "hidden " + std::to_string(hidden) +
                                         " is not divisible by query_heads " +
                                         std::to_string(query_heads));
-        if (!seq_len || !max_batch) fail(AB_ERR_ARGUMENT, "seq_len and max_batch must be > 0");
-        auto* b = new ab_attention_block();
-        b->rt = rt;
-        b->hidden = hidden;
-        b->heads = query_heads;
-        b->head = hidden / query_heads;
-        b->seq = seq_len;
-        b->max_batch = max_batch;
-        b->theta = rope_theta;
-        // worst case over kv_heads (1 kv head gives the most splits per group)
-        b->nsplit_max = attention_choose_splits(max_batch, 1, seq_len, rt->sm_count, 256);
-        uint64_t floats = 0, counters = 0;
-        attention_scratch_size(max_batch, query_heads, b->head, b->nsplit_max, &floats, &counters);
-        const uint64_t qd = (uint64_t)query_heads * b->head;
-        try {
-            b->q = (float*)device_alloc(rt, max_batch * qd * 4);
-            b->attn_out = device_alloc(rt, max_batch * qd * 4);
-            b->part = (float*)device_alloc(rt, floats * 4);
-            b->counters = (uint32_t*)device_alloc(rt, counters * 4);
-            alloc_tc_scratch(rt, &b->tc, max_batch, hidden, (3 * hidden + 127) / 128);
-        } catch (...) {
-            cudaFree(b->q);
-            cudaFree(b->attn_out);
-            cudaFree(b->part);
-            cudaFree(b->counters);
-            free_tc_scratch(&b->tc);
-            delete b;
-            throw;
-        }
-        *out = b;
+        *out = attention_block_new(rt, hidden, query_heads, hidden / query_heads, seq_len,
+                                   max_batch, rope_theta, nullptr);
     });
 }
 
@@ -365,7 +410,17 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         try {
             record_gemv(s, "attn_qkv_rope", g, wdt, batch, kProNorm, kEpiQkv);
             record_attention(s, "attn_decode", a);
-            record_gemv(s, "attn_wo_residual", o2, wdt, batch, kProNone, kEpiResidual);
+            if (blk->tp) {
+                // partial projection of this rank's heads; rank 0 adds the residual, and
+                // the all-reduce sums every rank's part straight into x
+                o2.out = blk->tp_y;
+                o2.addend = comm_rank(blk->tp) == 0 ? (const float*)x.data : nullptr;
+                record_gemv(s, "attn_wo_partial", o2, wdt, batch, kProNone, kEpiStore);
+                record_allreduce_f32(s, "attn_allreduce", blk->tp, blk->tp_y, (float*)x.data,
+                                     (size_t)batch * hidden);
+            } else {
+                record_gemv(s, "attn_wo_residual", o2, wdt, batch, kProNone, kEpiResidual);
+            }
         } catch (...) {
             s->nodes.resize(before);
             throw;
@@ -382,6 +437,7 @@ int ab_attention_block_destroy(ab_attention_block* b) {
         cudaFree(b->attn_out);
         cudaFree(b->part);
         cudaFree(b->counters);
+        if (b->tp_y) cudaFree(b->tp_y);
         free_tc_scratch(&b->tc);
         delete b;
     });
@@ -392,23 +448,7 @@ int ab_swiglu_block_create(ab_runtime* rt, uint32_t hidden, uint32_t intermediat
                            uint32_t max_batch, ab_swiglu_block** out) {
     return guard([&] {
         if (!rt || !out) fail(AB_ERR_ARGUMENT, "null argument");
-        if (!hidden || !intermediate || !max_batch)
-            fail(AB_ERR_ARGUMENT, "hidden, intermediate and max_batch must be > 0");
-        auto* b = new ab_swiglu_block();
-        b->rt = rt;
-        b->hidden = hidden;
-        b->inter = intermediate;
-        b->max_batch = max_batch;
-        try {
-            b->hb = device_alloc(rt, (size_t)max_batch * intermediate * 4);
-            alloc_tc_scratch(rt, &b->tc, max_batch, hidden,
-                             std::max((intermediate + 63) / 64, (hidden + 127) / 128));
-        } catch (...) {
-            if (b->hb) cudaFree(b->hb);
-            delete b;
-            throw;
-        }
-        *out = b;
+        *out = swiglu_block_new(rt, hidden, intermediate, max_batch, nullptr);
     });
 }
 
@@ -468,7 +508,15 @@ int ab_swiglu_block_record(ab_swiglu_block* blk, ab_scheme* s, ab_tensor x,
         const size_t before = s->nodes.size();
         try {
             record_gemv(s, "ffn_gate_up_swiglu", g, wdt, batch, kProNorm, kEpiSwiglu);
-            record_gemv(s, "ffn_down_residual", d, wdt, batch, kProNone, kEpiResidual);
+            if (blk->tp) {
+                d.out = blk->tp_y;
+                d.addend = comm_rank(blk->tp) == 0 ? (const float*)x.data : nullptr;
+                record_gemv(s, "ffn_down_partial", d, wdt, batch, kProNone, kEpiStore);
+                record_allreduce_f32(s, "ffn_allreduce", blk->tp, blk->tp_y, (float*)x.data,
+                                     (size_t)batch * hidden);
+            } else {
+                record_gemv(s, "ffn_down_residual", d, wdt, batch, kProNone, kEpiResidual);
+            }
         } catch (...) {
             s->nodes.resize(before);
             throw;
@@ -482,6 +530,7 @@ int ab_swiglu_block_destroy(ab_swiglu_block* b) {
         b->rt->activate();
         cudaStreamSynchronize(b->rt->stream);
         cudaFree(b->hb);
+        if (b->tp_y) cudaFree(b->tp_y);
         free_tc_scratch(&b->tc);
         delete b;
     });

@@ -7,7 +7,7 @@
 //  - One CTA computes a 128-row tile of W against all (padded) batch columns BN over a
 //    range of 64-element k-blocks; tiles x k-splits cover the matrix, sized to one wave.
 //  - Warp-specialised: thread 0 issues TMA loads (W tile 128 x 64, X tile BN x 64, both
-//    K-major with the 128-byte swizzle, plain CTA-local copies, no multicast) into a
+//    K-major with the 128-byte swizzle, each CTA loading its own copy) into a
 //    multi-stage ring guarded by full/empty mbarriers; thread 32 issues
 //    tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> f32) into a TMEM accumulator of BN
 //    columns and commits each stage back to its empty barrier; all four warps then read
@@ -135,7 +135,8 @@ __device__ __forceinline__ void tc_epilogue_chunk(const GemmTcParams& p, uint32_
             if ((uint32_t)j >= live) break;
             const uint64_t o = (uint64_t)(c0 + j) * p.out_stride + r;
             if (EPI == kEpiResidual) ((float*)p.out)[o] += v[j];
-            else if (p.out_dtype == AB_F32) ((float*)p.out)[o] = v[j];
+            else if (p.out_dtype == AB_F32)
+                ((float*)p.out)[o] = p.addend ? p.addend[o] + v[j] : v[j];
             else ((bf16*)p.out)[o] = __float2bfloat16_rn(v[j]);
         }
         return;
@@ -391,8 +392,10 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const GemmTcParams
             if (r + 1 < p.n_rows) out[o + 1] += y1;
         } else if (EPI == kEpiStore) {
             if (p.out_dtype == AB_F32) {
-                ((float*)p.out)[o] = y0;
-                if (r + 1 < p.n_rows) ((float*)p.out)[o + 1] = y1;
+                const float a0 = p.addend ? p.addend[o] : 0.0f;
+                ((float*)p.out)[o] = a0 + y0;
+                if (r + 1 < p.n_rows)
+                    ((float*)p.out)[o + 1] = (p.addend ? p.addend[o + 1] : 0.0f) + y1;
             } else {
                 ((bf16*)p.out)[o] = __float2bfloat16_rn(y0);
                 if (r + 1 < p.n_rows) ((bf16*)p.out)[o + 1] = __float2bfloat16_rn(y1);
@@ -501,7 +504,9 @@ void attach_tc_scratch(GemvParams* p, const GemmScratch& g) {
 
 bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave) {
     if (batch == 0 || batch > 256 || K == 0 || K % kTcBK) return false;
-    return interleave ? rows % 64 == 0 : rows % kTcBM == 0;
+    // a single stacked segment may end in a partial tile: TMA fills the missing rows with
+    // zeros and the epilogues skip rows >= n_rows
+    return interleave ? rows % 64 == 0 : rows > 0;
 }
 
 template <int EPI>
@@ -545,7 +550,7 @@ void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void*
     const uint32_t box_rows = p.interleave ? 64 : kTcBM;
     for (int i = 0; i < 3; i++) {
         const int j = i < nseg ? i : 0;
-        p.seg_tiles[i] = i < nseg && !p.interleave ? seg_rows[i] / kTcBM : 0;
+        p.seg_tiles[i] = i < nseg && !p.interleave ? (seg_rows[i] + kTcBM - 1) / kTcBM : 0;
         encode_tmap_2d(&maps[i], AB_BF16, segs[j], p.K, seg_rows[j], (uint64_t)p.K * 2, kTcBK,
                        box_rows, 128);
     }

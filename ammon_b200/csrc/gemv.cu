@@ -287,6 +287,10 @@ __global__ void __launch_bounds__(kGemvThreads, 4) gemv_kernel(const GemvParams 
                 out[o] += y0;
                 if (r + 1 < p.n_rows) out[o + 1] += y1;
             } else {
+                if (p.addend) {
+                    y0 += p.addend[o];
+                    if (r + 1 < p.n_rows) y1 += p.addend[o + 1];
+                }
                 store_elem(p.out, p.out_dtype, o, y0);
                 if (r + 1 < p.n_rows) store_elem(p.out, p.out_dtype, o + 1, y1);
             }
@@ -368,11 +372,11 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
         const bool inter = epi == kEpiSwiglu;
         int nseg = 0;
         bool segs_ok = true;
-        for (int i = 0; i < 3; i++) {
-            if (!p.seg_rows[i]) continue;
-            nseg = i + 1;
-            if (!inter && p.seg_rows[i] % 128) segs_ok = false;
-        }
+        for (int i = 0; i < 3; i++)
+            if (p.seg_rows[i]) nseg = i + 1;
+        // stacked segments must each fill whole 128-row tiles; a single one may end short
+        for (int i = 0; i < nseg; i++)
+            if (!inter && nseg > 1 && p.seg_rows[i] % 128) segs_ok = false;
         const uint32_t rows = inter ? p.seg_rows[0] : p.n_rows;
         const bool x_ok = pro == kProNorm ? p.xn != nullptr : p.x_dtype == AB_BF16;
         if (segs_ok && x_ok && gemm_tc_fits(rows, p.K, batch, inter)) {
@@ -396,6 +400,7 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
             g.out = p.out;
             g.out_dtype = p.out_dtype;
             g.out_stride = p.out_stride;
+            g.addend = p.addend;
             g.n_rows = p.n_rows;
             g.q = p.q;
             g.qd = p.qd;

@@ -5,6 +5,10 @@
 //
 // One decode step is one CUDA graph recorded once: the DecodeStep parcel is refreshed
 // by a deposit before each replay, so nothing is re-recorded per token.
+//
+// Under tensor parallelism (ab_llama_create_tp) every rank holds a shard: its query and kv
+// heads, its SwiGLU columns and its slice of the vocabulary; the residual stream and the
+// embedding table are replicated. The greedy pick merges every rank's best (value, id).
 #include <chrono>
 #include <cstring>
 #include <vector>
@@ -17,17 +21,22 @@ using namespace ab;
 
 namespace ab {
 
-// Device argmax of each row of logits [batch, vocab]: first index of the maximum, the
-// tie rule of sample_argmax (src/tokenizer.rs:179-189). NaNs never win.
-__global__ void __launch_bounds__(1024)
-    argmax_kernel(const float* __restrict__ logits, uint32_t vocab, int32_t* __restrict__ out) {
-    pdl_wait();
+// Candidate of a greedy pick: best logit and its vocabulary id.
+struct ArgPair {
+    float v;
+    uint32_t i;
+};
+
+// (value, id) of the first maximum of a row of logits, ids offset by `offset`; NaNs never
+// win. The reduction keeps the lowest id among equal values: the rule of sample_argmax
+// (src/tokenizer.rs:179-189).
+__device__ __forceinline__ ArgPair row_argmax(const float* __restrict__ row, uint32_t n,
+                                              uint32_t offset) {
     __shared__ float bv[32];
     __shared__ uint32_t bi[32];
-    const float* row = logits + (uint64_t)blockIdx.x * vocab;
     float best = -INFINITY;
     uint32_t idx = 0xffffffffu;
-    for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
         const float v = row[i];
         if (v > best || (idx == 0xffffffffu && v == best)) {
             best = v;
@@ -48,6 +57,7 @@ __global__ void __launch_bounds__(1024)
         bi[warp] = idx;
     }
     __syncthreads();
+    ArgPair r = {-INFINITY, 0xffffffffu};
     if (warp == 0) {
         const uint32_t nw = blockDim.x / 32;
         best = lane < nw ? bv[lane] : -INFINITY;
@@ -60,7 +70,44 @@ __global__ void __launch_bounds__(1024)
                 idx = oi;
             }
         }
-        if (lane == 0) out[blockIdx.x] = idx == 0xffffffffu ? 0 : (int32_t)idx;
+        r.v = best;
+        r.i = idx == 0xffffffffu ? 0xffffffffu : idx + offset;
+    }
+    return r;
+}
+
+// Device argmax of each row of logits [batch, vocab].
+__global__ void __launch_bounds__(1024)
+    argmax_kernel(const float* __restrict__ logits, uint32_t vocab, int32_t* __restrict__ out) {
+    pdl_wait();
+    const ArgPair r = row_argmax(logits + (uint64_t)blockIdx.x * vocab, vocab, 0);
+    if (threadIdx.x == 0) out[blockIdx.x] = r.i == 0xffffffffu ? 0 : (int32_t)r.i;
+    pdl_trigger();
+}
+
+// Best (value, global id) of this rank's vocabulary slice, per row.
+__global__ void __launch_bounds__(1024)
+    argmax_pair_kernel(const float* __restrict__ logits, uint32_t vocab_l, uint32_t offset,
+                       ArgPair* __restrict__ out) {
+    pdl_wait();
+    const ArgPair r = row_argmax(logits + (uint64_t)blockIdx.x * vocab_l, vocab_l, offset);
+    if (threadIdx.x == 0) out[blockIdx.x] = r;
+    pdl_trigger();
+}
+
+// Merge the ranks' candidates [world, batch] into the first maximum per row.
+__global__ void argmax_merge_kernel(const ArgPair* __restrict__ all, uint32_t world,
+                                    uint32_t batch, int32_t* __restrict__ out) {
+    pdl_wait();
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < batch) {
+        ArgPair best = {-INFINITY, 0xffffffffu};
+        for (uint32_t r = 0; r < world; r++) {
+            const ArgPair c = all[(uint64_t)r * batch + b];
+            if (c.i == 0xffffffffu) continue;
+            if (c.v > best.v || (c.v == best.v && c.i < best.i) || best.i == 0xffffffffu) best = c;
+        }
+        out[b] = best.i == 0xffffffffu ? 0 : (int32_t)best.i;
     }
     pdl_trigger();
 }
@@ -91,16 +138,20 @@ __global__ void feedback_kernel(const int32_t* __restrict__ argmax, Step* step,
 struct ab_llama {
     Runtime* rt = nullptr;
     ab_llama_config c = {};
+    ab_comm* comm = nullptr;  // tensor parallelism (null: one GPU)
+    int32_t rank = 0, world = 1;
+    uint32_t heads_l = 0, kv_l = 0, hidden_l = 0, vocab_l = 0;  // this rank's shard
     ab_tensor embed = {}, wcls = {}, rms_final = {};
     std::vector<ab_tensor> rms_att, wq, wk, wv, wo, rms_ffn, w1, w2, w3;
     ab_kvcache* cache = nullptr;
     ab_attention_block* attn = nullptr;
     ab_swiglu_block* ffn = nullptr;
     ab_tensor x = {}, logits = {}, step = {}, argmax = {}, history = {};
-    ab_scheme* scheme = nullptr;       // one decode step
+    ab_tensor logits_all = {}, pairs = {}, pairs_all = {};  // tensor parallelism
+    ab_scheme* scheme = nullptr;       // one decode step (gathers the logits under TP)
     ab_scheme* loop_scheme = nullptr;  // one decode step + device sample feedback
     GemmScratch cls_tc;                // classifier's tensor-core GEMM scratch
-    float* h_logits = nullptr;  // pinned [batch, vocab]
+    float* h_logits = nullptr;         // pinned [batch, vocab]
     int32_t* h_argmax = nullptr;
     ab_decode_step* h_steps = nullptr;
     std::vector<float> vt_logits;  // host logits handed out through the vtable
@@ -108,9 +159,8 @@ struct ab_llama {
 
 namespace {
 
-void free_t(Runtime* rt, ab_tensor& t) {
+void free_t(ab_tensor& t) {
     if (t.data) cudaFree(t.data);
-    (void)rt;
     t.data = nullptr;
 }
 
@@ -141,18 +191,19 @@ void destroy_model(ab_llama* m) {
     if (m->cache) ab_kvcache_destroy(m->cache);
     for (auto* v : {&m->rms_att, &m->wq, &m->wk, &m->wv, &m->wo, &m->rms_ffn, &m->w1, &m->w2,
                     &m->w3})
-        for (auto& t : *v) free_t(rt, t);
+        for (auto& t : *v) free_t(t);
     for (ab_tensor* t : {&m->embed, &m->wcls, &m->rms_final, &m->x, &m->logits, &m->step,
-                         &m->argmax, &m->history})
-        free_t(rt, *t);
+                         &m->argmax, &m->history, &m->logits_all, &m->pairs, &m->pairs_all})
+        free_t(*t);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_argmax) cudaFreeHost(m->h_argmax);
     if (m->h_steps) cudaFreeHost(m->h_steps);
     delete m;
 }
 
-// Records the full decode step into `s` (with the device sample feedback when asked).
-void record_step(ab_llama* m, ab_scheme* s, bool feedback) {
+// Records the full decode step into `s`: with the device sample feedback (the device
+// loop) or, under tensor parallelism, with the logits gathered from every rank.
+void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
     s->nodes.clear();
     s->dirty = true;
     const auto& c = m->c;
@@ -170,12 +221,12 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback) {
         ab_swiglu_weights fw = {m->rms_ffn[l], m->w1[l], m->w3[l], m->w2[l]};
         check(ab_swiglu_block_record(m->ffn, s, x, &fw));
     }
-    // final RmsNorm fused into the classifier GEMV's prologue
+    // final RmsNorm fused into the classifier's prologue (this rank's vocabulary rows)
     GemvParams g = {};
     g.seg[0] = m->wcls.data;
-    g.seg_rows[0] = c.vocab;
-    g.n_rows = c.vocab;
-    g.units = (c.vocab + 1) / 2;
+    g.seg_rows[0] = m->vocab_l;
+    g.n_rows = m->vocab_l;
+    g.units = (m->vocab_l + 1) / 2;
     g.K = c.dim;
     g.x = m->x.data;
     g.x_dtype = AB_F32;
@@ -185,15 +236,34 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback) {
     g.eps = c.norm_eps;
     g.out = m->logits.data;
     g.out_dtype = AB_F32;
-    g.out_stride = c.vocab;
+    g.out_stride = m->vocab_l;
     attach_tc_scratch(&g, m->cls_tc);
     record_gemv(s, "final_norm_classifier", g, c.dtype, c.batch, kProNorm, kEpiStore);
     const float* lg = (const float*)m->logits.data;
     int32_t* am = (int32_t*)m->argmax.data;
-    const uint32_t vocab = c.vocab, batch = c.batch;
-    s->add("argmax", [=](cudaStream_t st) {
-        return launch(st, dim3(batch), dim3(1024), 0, true, argmax_kernel, lg, vocab, am);
-    });
+    const uint32_t batch = c.batch;
+    if (m->world == 1) {
+        const uint32_t vocab = c.vocab;
+        s->add("argmax", [=](cudaStream_t st) {
+            return launch(st, dim3(batch), dim3(1024), 0, true, argmax_kernel, lg, vocab, am);
+        });
+    } else {
+        ArgPair* pr = (ArgPair*)m->pairs.data;
+        ArgPair* pa = (ArgPair*)m->pairs_all.data;
+        const uint32_t vl = m->vocab_l, off = (uint32_t)m->rank * m->vocab_l;
+        const uint32_t world = (uint32_t)m->world;
+        s->add("argmax", [=](cudaStream_t st) {
+            return launch(st, dim3(batch), dim3(1024), 0, true, argmax_pair_kernel, lg, vl, off, pr);
+        });
+        record_allgather_bytes(s, "argmax_allgather", m->comm, pr, pa, (size_t)batch * 8);
+        s->add("argmax_merge", [=](cudaStream_t st) {
+            return launch(st, dim3((batch + 127) / 128), dim3(128), 0, true, argmax_merge_kernel,
+                          (const ArgPair*)pa, world, batch, am);
+        });
+        if (gather_logits)
+            record_allgather_bytes(s, "logits_allgather", m->comm, lg, m->logits_all.data,
+                                   (size_t)batch * m->vocab_l * 4);
+    }
     if (feedback) {
         Step* stp = (Step*)m->step.data;
         int32_t* hist = (int32_t*)m->history.data;
@@ -216,6 +286,74 @@ int vt_step(void* self, uint32_t token, uint32_t pos, const float** logits) {
 }
 uint32_t vt_vocab(void* self) { return ((ab_llama*)self)->c.vocab; }
 uint32_t vt_seq(void* self) { return ((ab_llama*)self)->c.seq; }
+
+ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm) {
+    if (!rt || !cfg) fail(AB_ERR_ARGUMENT, "null argument");
+    const ab_llama_config c = *cfg;
+    if (!c.dim || !c.layers || !c.heads || !c.kv_heads || !c.head_dim || !c.hidden || !c.vocab ||
+        !c.seq || !c.batch)
+        fail(AB_ERR_ARGUMENT, "model dims must be non-zero");
+    if (c.heads * c.head_dim != c.dim) fail(AB_ERR_VALIDATION, "heads * head_dim must equal dim");
+    if (c.dtype != AB_F32 && c.dtype != AB_BF16) fail(AB_ERR_ARGUMENT, "dtype f32 or bf16");
+    const int32_t world = comm ? comm_world(comm) : 1;
+    const int32_t rank = comm ? comm_rank(comm) : 0;
+    if (c.heads % world || c.kv_heads % world || c.hidden % world || c.vocab % world)
+        fail(AB_ERR_VALIDATION, "tensor parallelism over " + std::to_string(world) +
+                                    " ranks needs heads, kv_heads, hidden and vocab divisible by it");
+    auto* m = new ab_llama();
+    m->rt = rt;
+    m->c = c;
+    m->comm = comm;
+    m->rank = rank;
+    m->world = world;
+    m->heads_l = c.heads / world;
+    m->kv_l = c.kv_heads / world;
+    m->hidden_l = c.hidden / world;
+    m->vocab_l = c.vocab / world;
+    try {
+        const int32_t dt = c.dtype;
+        const uint32_t qd = m->heads_l * c.head_dim, kvd = m->kv_l * c.head_dim;
+        m->embed = alloc_t(rt, dt, {c.vocab, c.dim});
+        m->wcls = alloc_t(rt, dt, {m->vocab_l, c.dim});
+        m->rms_final = alloc_t(rt, dt, {c.dim});
+        for (uint32_t l = 0; l < c.layers; l++) {
+            m->rms_att.push_back(alloc_t(rt, dt, {c.dim}));
+            m->wq.push_back(alloc_t(rt, dt, {qd, c.dim}));
+            m->wk.push_back(alloc_t(rt, dt, {kvd, c.dim}));
+            m->wv.push_back(alloc_t(rt, dt, {kvd, c.dim}));
+            m->wo.push_back(alloc_t(rt, dt, {c.dim, qd}));
+            m->rms_ffn.push_back(alloc_t(rt, dt, {c.dim}));
+            m->w1.push_back(alloc_t(rt, dt, {m->hidden_l, c.dim}));
+            m->w2.push_back(alloc_t(rt, dt, {c.dim, m->hidden_l}));
+            m->w3.push_back(alloc_t(rt, dt, {m->hidden_l, c.dim}));
+        }
+        check(ab_kvcache_create(rt, c.layers, c.seq, m->kv_l, c.head_dim, dt, c.batch, &m->cache));
+        m->attn = attention_block_new(rt, c.dim, m->heads_l, c.head_dim, c.seq, c.batch,
+                                      c.rope_theta, comm);
+        m->ffn = swiglu_block_new(rt, c.dim, m->hidden_l, c.batch, comm);
+        alloc_tc_scratch(rt, &m->cls_tc, c.batch, c.dim, (m->vocab_l + 127) / 128);
+        m->x = alloc_t(rt, AB_F32, {c.batch, c.dim});
+        m->logits = alloc_t(rt, AB_F32, {c.batch, m->vocab_l});
+        m->argmax = alloc_t(rt, AB_U32, {c.batch});
+        m->history = alloc_t(rt, AB_U32, {c.seq, c.batch});
+        if (world > 1) {
+            m->logits_all = alloc_t(rt, AB_F32, {(uint32_t)world, c.batch, m->vocab_l});
+            m->pairs = alloc_t(rt, AB_U32, {c.batch, 2});
+            m->pairs_all = alloc_t(rt, AB_U32, {(uint32_t)world, c.batch, 2});
+        }
+        check(ab_step_parcel(rt, c.batch, &m->step));
+        cuda_check(cudaMallocHost(&m->h_logits, (size_t)c.batch * c.vocab * 4), "pinned logits");
+        cuda_check(cudaMallocHost(&m->h_argmax, (size_t)c.batch * 4), "pinned argmax");
+        cuda_check(cudaMallocHost(&m->h_steps, (size_t)c.batch * sizeof(ab_decode_step)),
+                   "pinned steps");
+        check(ab_scheme_create(rt, &m->scheme));
+        check(ab_scheme_create(rt, &m->loop_scheme));
+    } catch (...) {
+        destroy_model(m);
+        throw;
+    }
+    return m;
+}
 
 }  // namespace
 
@@ -278,84 +416,54 @@ int ab_generate_tokens(const ab_autoregressive_model* m, const int32_t* prompt, 
 
 int ab_llama_create(ab_runtime* rt, const ab_llama_config* cfg, ab_llama** out) {
     return guard([&] {
-        if (!rt || !cfg || !out) fail(AB_ERR_ARGUMENT, "null argument");
-        const ab_llama_config c = *cfg;
-        if (!c.dim || !c.layers || !c.heads || !c.kv_heads || !c.head_dim || !c.hidden || !c.vocab ||
-            !c.seq || !c.batch)
-            fail(AB_ERR_ARGUMENT, "model dims must be non-zero");
-        if (c.heads * c.head_dim != c.dim)
-            fail(AB_ERR_VALIDATION, "heads * head_dim must equal dim");
-        if (c.dtype != AB_F32 && c.dtype != AB_BF16) fail(AB_ERR_ARGUMENT, "dtype f32 or bf16");
-        auto* m = new ab_llama();
-        m->rt = rt;
-        m->c = c;
-        try {
-            const int32_t dt = c.dtype;
-            const uint32_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
-            m->embed = alloc_t(rt, dt, {c.vocab, c.dim});
-            m->wcls = alloc_t(rt, dt, {c.vocab, c.dim});
-            m->rms_final = alloc_t(rt, dt, {c.dim});
-            for (uint32_t l = 0; l < c.layers; l++) {
-                m->rms_att.push_back(alloc_t(rt, dt, {c.dim}));
-                m->wq.push_back(alloc_t(rt, dt, {qd, c.dim}));
-                m->wk.push_back(alloc_t(rt, dt, {kvd, c.dim}));
-                m->wv.push_back(alloc_t(rt, dt, {kvd, c.dim}));
-                m->wo.push_back(alloc_t(rt, dt, {c.dim, qd}));
-                m->rms_ffn.push_back(alloc_t(rt, dt, {c.dim}));
-                m->w1.push_back(alloc_t(rt, dt, {c.hidden, c.dim}));
-                m->w2.push_back(alloc_t(rt, dt, {c.dim, c.hidden}));
-                m->w3.push_back(alloc_t(rt, dt, {c.hidden, c.dim}));
-            }
-            check(ab_kvcache_create(rt, c.layers, c.seq, c.kv_heads, c.head_dim, dt, c.batch,
-                                    &m->cache));
-            check(ab_attention_block_create(rt, c.dim, c.heads, c.seq, c.batch, c.rope_theta,
-                                            &m->attn));
-            check(ab_swiglu_block_create(rt, c.dim, c.hidden, c.batch, &m->ffn));
-            alloc_tc_scratch(rt, &m->cls_tc, c.batch, c.dim, (c.vocab + 127) / 128);
-            m->x = alloc_t(rt, AB_F32, {c.batch, c.dim});
-            m->logits = alloc_t(rt, AB_F32, {c.batch, c.vocab});
-            m->argmax = alloc_t(rt, AB_U32, {c.batch});
-            m->history = alloc_t(rt, AB_U32, {c.seq, c.batch});
-            check(ab_step_parcel(rt, c.batch, &m->step));
-            cuda_check(cudaMallocHost(&m->h_logits, (size_t)c.batch * c.vocab * 4), "pinned logits");
-            cuda_check(cudaMallocHost(&m->h_argmax, (size_t)c.batch * 4), "pinned argmax");
-            cuda_check(cudaMallocHost(&m->h_steps, (size_t)c.batch * sizeof(ab_decode_step)),
-                       "pinned steps");
-            check(ab_scheme_create(rt, &m->scheme));
-            check(ab_scheme_create(rt, &m->loop_scheme));
-        } catch (...) {
-            destroy_model(m);
-            throw;
-        }
-        *out = m;
+        if (!out) fail(AB_ERR_ARGUMENT, "null argument");
+        *out = create_model(rt, cfg, nullptr);
+    });
+}
+
+int ab_llama_create_tp(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm,
+                       ab_llama** out) {
+    return guard([&] {
+        if (!out || !comm) fail(AB_ERR_ARGUMENT, "null argument");
+        *out = create_model(rt, cfg, comm);
     });
 }
 
 int ab_llama_init_synthetic(ab_llama* m, uint64_t seed, float std) {
     return guard([&] {
         if (!m) fail(AB_ERR_ARGUMENT, "null model");
-        ab_runtime* rt = static_cast<ab_runtime*>(m->rt);
-        auto fill = [&](ab_tensor& t, uint64_t stream, float mean, float sd) {
-            check(ab_tensor_fill_normal(rt, t, seed, stream, mean, sd));
+        Runtime* rt = m->rt;
+        const auto& c = m->c;
+        const uint64_t r = (uint64_t)m->rank;
+        const uint64_t qd = (uint64_t)c.heads * c.head_dim, kvd = (uint64_t)c.kv_heads * c.head_dim;
+        const uint64_t qd_l = (uint64_t)m->heads_l * c.head_dim;
+        const uint64_t kvd_l = (uint64_t)m->kv_l * c.head_dim;
+        // Every shard draws the global tensor's values at its own indices, so any rank
+        // count decodes the same model. Stream ids are shared with the CPU oracle.
+        auto rows = [&](ab_tensor& t, uint64_t stream, uint64_t row0, float mean, float sd) {
+            fill_normal_region(rt, t, seed, stream, mean, sd, t.dims[t.rank - 1], row0, 0);
         };
-        // stream ids shared with the CPU oracle's generator
-        fill(m->embed, 1, 0.0f, std);
-        fill(m->rms_final, 2, 1.0f, 0.01f);
-        fill(m->wcls, 3, 0.0f, std);
-        for (uint32_t l = 0; l < m->c.layers; l++) {
+        auto cols = [&](ab_tensor& t, uint64_t stream, uint64_t gcols, uint64_t col0) {
+            fill_normal_region(rt, t, seed, stream, 0.0f, std, gcols, 0, col0);
+        };
+        rows(m->embed, 1, 0, 0.0f, std);
+        rows(m->rms_final, 2, 0, 1.0f, 0.01f);
+        rows(m->wcls, 3, r * m->vocab_l, 0.0f, std);
+        for (uint32_t l = 0; l < c.layers; l++) {
             const uint64_t b = 16 + 16ull * l;
-            fill(m->rms_att[l], b + 0, 1.0f, 0.01f);
-            fill(m->wq[l], b + 1, 0.0f, std);
-            fill(m->wk[l], b + 2, 0.0f, std);
-            fill(m->wv[l], b + 3, 0.0f, std);
-            fill(m->wo[l], b + 4, 0.0f, std);
-            fill(m->rms_ffn[l], b + 5, 1.0f, 0.01f);
-            fill(m->w1[l], b + 6, 0.0f, std);
-            fill(m->w2[l], b + 7, 0.0f, std);
-            fill(m->w3[l], b + 8, 0.0f, std);
+            rows(m->rms_att[l], b + 0, 0, 1.0f, 0.01f);
+            rows(m->wq[l], b + 1, r * qd_l, 0.0f, std);
+            rows(m->wk[l], b + 2, r * kvd_l, 0.0f, std);
+            rows(m->wv[l], b + 3, r * kvd_l, 0.0f, std);
+            cols(m->wo[l], b + 4, qd, r * qd_l);
+            rows(m->rms_ffn[l], b + 5, 0, 1.0f, 0.01f);
+            rows(m->w1[l], b + 6, r * m->hidden_l, 0.0f, std);
+            cols(m->w2[l], b + 7, c.hidden, r * m->hidden_l);
+            rows(m->w3[l], b + 8, r * m->hidden_l, 0.0f, std);
         }
-        m->rt->activate();
-        cuda_check(cudaStreamSynchronize(m->rt->stream), "init synchronize");
+        (void)kvd;
+        rt->activate();
+        cuda_check(cudaStreamSynchronize(rt->stream), "init synchronize");
     });
 }
 
@@ -388,41 +496,60 @@ int ab_llama_cache(ab_llama* m, ab_kvcache** out) {
     });
 }
 
+static void check_steps(const ab_llama* m, const ab_decode_step* steps, uint32_t n,
+                        uint32_t extra) {
+    if (n != m->c.batch)
+        fail(AB_ERR_ARGUMENT, "step needs " + std::to_string(m->c.batch) + " DecodeSteps, got " +
+                                  std::to_string(n));
+    for (uint32_t b = 0; b < n; b++) {
+        if (steps[b].token >= m->c.vocab)
+            fail(AB_ERR_ARGUMENT, "token " + std::to_string(steps[b].token) +
+                                      " out of range for vocab " + std::to_string(m->c.vocab));
+        if ((uint64_t)steps[b].position + extra >= m->c.seq + (extra ? 1 : 0))
+            fail(AB_ERR_ARGUMENT, "position " + std::to_string(steps[b].position) +
+                                      (extra ? " + " + std::to_string(extra) + " steps passes"
+                                             : " beyond") +
+                                      " max_seq_len " + std::to_string(m->c.seq));
+    }
+}
+
 int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* logits_host,
                   int32_t* argmax_host) {
     return guard([&] {
         if (!m || !steps) fail(AB_ERR_ARGUMENT, "null argument");
-        if (n != m->c.batch)
-            fail(AB_ERR_ARGUMENT, "step needs " + std::to_string(m->c.batch) + " DecodeSteps, got " +
-                                      std::to_string(n));
-        for (uint32_t b = 0; b < n; b++) {
-            if (steps[b].token >= m->c.vocab)
-                fail(AB_ERR_ARGUMENT, "token " + std::to_string(steps[b].token) +
-                                          " out of range for vocab " + std::to_string(m->c.vocab));
-            if (steps[b].position >= m->c.seq)
-                fail(AB_ERR_ARGUMENT, "position " + std::to_string(steps[b].position) +
-                                          " beyond max_seq_len " + std::to_string(m->c.seq));
-        }
+        check_steps(m, steps, n, 0);
         Runtime* rt = m->rt;
         rt->activate();
-        if (m->scheme->nodes.empty()) record_step(m, m->scheme, false);
+        if (m->scheme->nodes.empty()) record_step(m, m->scheme, false, m->world > 1);
         std::memcpy(m->h_steps, steps, sizeof(ab_decode_step) * n);
         cuda_check(cudaMemcpyAsync(m->step.data, m->h_steps, sizeof(ab_decode_step) * n,
                                    cudaMemcpyHostToDevice, rt->stream),
                    "deposit steps");
         check(ab_scheme_submit(m->scheme));
         const size_t lbytes = (size_t)n * m->c.vocab * 4;
+        const void* lsrc = m->world > 1 ? m->logits_all.data : m->logits.data;
         if (logits_host)
-            cuda_check(cudaMemcpyAsync(m->h_logits, m->logits.data, lbytes, cudaMemcpyDeviceToHost,
-                                       rt->stream),
-                       "logits readback");
+            cuda_check(
+                cudaMemcpyAsync(m->h_logits, lsrc, lbytes, cudaMemcpyDeviceToHost, rt->stream),
+                "logits readback");
         if (argmax_host)
             cuda_check(cudaMemcpyAsync(m->h_argmax, m->argmax.data, (size_t)n * 4,
                                        cudaMemcpyDeviceToHost, rt->stream),
                        "argmax readback");
         cuda_check(cudaStreamSynchronize(rt->stream), "step synchronize");
         rt->check_flags();
-        if (logits_host) std::memcpy(logits_host, m->h_logits, lbytes);
+        if (logits_host) {
+            if (m->world == 1) {
+                std::memcpy(logits_host, m->h_logits, lbytes);
+            } else {
+                // gathered as [rank][batch][vocab slice] -> [batch][vocab]
+                const size_t vl = m->vocab_l;
+                for (uint32_t b = 0; b < n; b++)
+                    for (int32_t r = 0; r < m->world; r++)
+                        std::memcpy(logits_host + (size_t)b * m->c.vocab + r * vl,
+                                    m->h_logits + ((size_t)r * n + b) * vl, vl * 4);
+            }
+        }
         if (argmax_host) std::memcpy(argmax_host, m->h_argmax, (size_t)n * 4);
     });
 }
@@ -432,18 +559,10 @@ int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n,
     return guard([&] {
         if (!m || !start) fail(AB_ERR_ARGUMENT, "null argument");
         const auto& c = m->c;
-        if (n != c.batch)
-            fail(AB_ERR_ARGUMENT, "decode needs " + std::to_string(c.batch) + " start steps");
-        for (uint32_t b = 0; b < n; b++) {
-            if (start[b].token >= c.vocab) fail(AB_ERR_ARGUMENT, "start token out of range");
-            if ((uint64_t)start[b].position + steps > c.seq)
-                fail(AB_ERR_ARGUMENT, "decode of " + std::to_string(steps) + " steps from position " +
-                                          std::to_string(start[b].position) + " passes max_seq_len " +
-                                          std::to_string(c.seq));
-        }
+        check_steps(m, start, n, steps);
         Runtime* rt = m->rt;
         rt->activate();
-        if (m->loop_scheme->nodes.empty()) record_step(m, m->loop_scheme, true);
+        if (m->loop_scheme->nodes.empty()) record_step(m, m->loop_scheme, true, false);
         std::memcpy(m->h_steps, start, sizeof(ab_decode_step) * n);
         cuda_check(cudaMemcpyAsync(m->step.data, m->h_steps, sizeof(ab_decode_step) * n,
                                    cudaMemcpyHostToDevice, rt->stream),
@@ -469,7 +588,7 @@ int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n,
 int ab_llama_scheme(ab_llama* m, ab_scheme** out) {
     return guard([&] {
         if (!m || !out) fail(AB_ERR_ARGUMENT, "null argument");
-        if (m->scheme->nodes.empty()) record_step(m, m->scheme, false);
+        if (m->scheme->nodes.empty()) record_step(m, m->scheme, false, m->world > 1);
         *out = m->scheme;
     });
 }
@@ -477,7 +596,7 @@ int ab_llama_scheme(ab_llama* m, ab_scheme** out) {
 int ab_llama_logits(ab_llama* m, ab_tensor* out) {
     return guard([&] {
         if (!m || !out) fail(AB_ERR_ARGUMENT, "null argument");
-        *out = m->logits;
+        *out = m->world > 1 ? m->logits_all : m->logits;
     });
 }
 

@@ -52,6 +52,7 @@ struct GemvParams {
     void* out;
     int32_t out_dtype;
     uint32_t out_stride;
+    const float* addend;  // kEpiStore: out = addend + y (f32, laid out like out); may be null
     // kEpiQkv
     float* q;
     uint32_t qd, kvd, head, seq;
@@ -87,6 +88,7 @@ struct GemmTcParams {
     void* out;
     int32_t out_dtype;
     uint32_t out_stride;
+    const float* addend;
     uint32_t n_rows;
     float* q;
     uint32_t qd, kvd, head, seq;
@@ -131,6 +133,27 @@ void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t 
                       uint32_t max_tiles);
 void free_tc_scratch(GemmScratch* g);
 void attach_tc_scratch(GemvParams* p, const GemmScratch& g);
+
+// Module constructors with an explicit head size and an optional tensor-parallel
+// communicator (blocks.cu); the C entry points call them with tp = null.
+ab_attention_block* attention_block_new(ab_runtime* rt, uint32_t hidden, uint32_t heads,
+                                        uint32_t head, uint32_t seq_len, uint32_t max_batch,
+                                        float rope_theta, ab_comm* tp);
+ab_swiglu_block* swiglu_block_new(ab_runtime* rt, uint32_t hidden, uint32_t intermediate,
+                                  uint32_t max_batch, ab_comm* tp);
+
+// ---- tensor parallelism (comm.cu) ----
+int comm_rank(const ab_comm* c);
+int comm_world(const ab_comm* c);
+void record_allreduce_f32(ab_scheme* s, const char* label, ab_comm* c, const float* send,
+                          float* recv, size_t count);
+void record_allgather_bytes(ab_scheme* s, const char* label, ab_comm* c, const void* send,
+                            void* recv, size_t bytes);
+
+// Seeded synthetic values of a [rows, cols] region of a larger [*, global_cols] tensor
+// whose element (r, c) is element (row0 + r, col0 + c) of the global one (runtime.cu).
+void fill_normal_region(Runtime* rt, ab_tensor t, uint64_t seed, uint64_t stream, float mean,
+                        float std, uint64_t global_cols, uint64_t row0, uint64_t col0);
 
 // Records one fused GEMV (weights of dtype wdtype) over batch rows [0, batch).
 void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, uint32_t batch,

@@ -164,6 +164,45 @@ __global__ void fill_normal_kernel(T* out, uint64_t n, uint64_t key, float mean,
     }
 }
 
+template <typename T>
+__global__ void fill_normal_region_kernel(T* out, uint64_t rows, uint64_t cols, uint64_t gcols,
+                                          uint64_t row0, uint64_t col0, uint64_t key, float mean,
+                                          float std) {
+    const uint64_t n = rows * cols;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t g = (row0 + i / cols) * gcols + col0 + i % cols;
+        uint32_t s = 0;
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            uint64_t h = mix64(key + 3ull * g + (uint64_t)j);
+            s += (uint32_t)(h & 0xffff) + (uint32_t)((h >> 16) & 0xffff) +
+                 (uint32_t)((h >> 32) & 0xffff) + (uint32_t)(h >> 48);
+        }
+        float z = __fmul_rn((float)((int32_t)(2u * s) - 786420), 1.0f / 131072.0f);
+        out[i] = from_f32<T>(__fmaf_rn(std, z, mean));
+    }
+}
+
+void fill_normal_region(Runtime* rt, ab_tensor t, uint64_t seed, uint64_t stream, float mean,
+                        float std, uint64_t global_cols, uint64_t row0, uint64_t col0) {
+    expect_data("t", t);
+    expect_float("t", t);
+    const uint64_t cols = t.dims[t.rank - 1];
+    const uint64_t rows = numel(t) / cols;
+    const uint64_t key = mix64_host(seed * 0xD1B54A32D192ED03ull ^ mix64_host(stream));
+    rt->activate();
+    const unsigned grid =
+        (unsigned)std::min<uint64_t>((rows * cols + 255) / 256, (uint64_t)rt->sm_count * 16);
+    if (t.dtype == AB_F32)
+        fill_normal_region_kernel<float><<<grid, 256, 0, rt->stream>>>(
+            (float*)t.data, rows, cols, global_cols, row0, col0, key, mean, std);
+    else
+        fill_normal_region_kernel<bf16><<<grid, 256, 0, rt->stream>>>(
+            (bf16*)t.data, rows, cols, global_cols, row0, col0, key, mean, std);
+    cuda_check(cudaGetLastError(), "fill_normal_region launch");
+}
+
 }  // namespace ab
 
 using namespace ab;

@@ -1,6 +1,6 @@
 // TMA (cp.async.bulk.tensor) and mbarrier helpers for sm_100a kernels.
 //
-// Loads are plain CTA-local tensor copies: no cluster multicast anywhere, so the same
+// Loads are plain tensor copies into the issuing CTA's own shared memory, so the same
 // code is safe in multi-GPU processes. Every wait is bounded by %globaltimer.
 #pragma once
 

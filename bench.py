@@ -14,8 +14,14 @@ value:  tokens/s of the device-resident greedy loop (graph replays, device argma
 e2e:    tokens/s through the reference-facing step() (AutoregressiveModel::step): every
         step uploads the DecodeSteps and reads [batch, vocab] fp32 logits back to the
         host, where sample_argmax picks the next ids.
-With N > 1 every rank decodes its own batch of independent streams (replicas, no
-collective); value is the sum over ranks.
+With N > 1 (one process per GPU under torch.distributed.run):
+  --parallel tp (default for the bf16 8B workload): the model is tensor parallel over the
+        ranks (heads, kv heads, FFN columns and vocab split; one NCCL all-reduce after wo
+        and one after w2 per layer, captured in the step graph); all ranks decode the same
+        batch, so value is that batch's tokens/s ("scaling": "strong").
+  --parallel replicas (default for the fp32 workloads): every rank decodes its own batch
+        of independent streams with no collective; value is the sum over ranks
+        ("scaling": "weak").
 """
 from __future__ import annotations
 
@@ -51,6 +57,26 @@ SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.act
 
 
 # ----------------------------------------------------------------------------- helpers
+class StdoutToStderr:
+    """Sends file descriptor 1 to stderr while NCCL initialises (NCCL may print its
+    version banner on stdout, which must carry only the JSON line)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        import ctypes
+
+        ctypes.CDLL(None).fflush(None)
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        return False
+
+
 def _mix64(z):
     M = (1 << 64) - 1
     z = (z + 0x9E3779B97F4A7C15) & M
@@ -132,28 +158,33 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def layer_bytes(w, batch):
+def layer_bytes(w, batch, shards=1):
     """Algorithmic bytes per launch of each fused kernel (weights once, activations and
-    KV rows read/written), for the kernel labels the step graph records."""
+    KV rows read/written), for the kernel labels the step graph records. With tensor
+    parallelism over `shards` ranks, one rank's share (the weights and K/V are split)."""
     e = 2 if w["bf16"] else 4
-    d, F, V = w["dim"], w["hidden"], w["vocab"]
-    qd, kvd = w["heads"] * w["head_dim"], w["kv_heads"] * w["head_dim"]
-    return {
+    d, F, V = w["dim"], w["hidden"] // shards, w["vocab"] // shards
+    qd = w["heads"] // shards * w["head_dim"]
+    kvd = w["kv_heads"] // shards * w["head_dim"]
+    out = {
         "ffn_gate_up_swiglu": 2 * F * d * e + batch * (d * 4 + F * e) + d * e,
         "ffn_down_residual": d * F * e + batch * (F * e + 2 * d * 4),
         "attn_qkv_rope": (qd + 2 * kvd) * d * e + batch * (d * 4 + qd * 4 + 2 * kvd * e) + d * e,
         "attn_wo_residual": d * qd * e + batch * (qd * e + 2 * d * 4),
         "final_norm_classifier": V * d * e + batch * (d * 4 + V * 4) + d * e,
     }
+    out["attn_wo_partial"] = out["attn_wo_residual"]
+    out["ffn_down_partial"] = out["ffn_down_residual"]
+    return out
 
 
-def step_bytes(w, batch, mean_pos):
-    """Algorithmic bytes of one decode step: all weights once, the K/V rows read by
-    attention for every stream (positions 0..pos), the new K/V row written."""
+def step_bytes(w, batch, mean_pos, shards=1):
+    """Algorithmic bytes of one decode step (per rank): all weights once, the K/V rows
+    read by attention for every stream (positions 0..pos), the new K/V row written."""
     e = 2 if w["bf16"] else 4
     L = w["layers"]
-    kvd = w["kv_heads"] * w["head_dim"]
-    lb = layer_bytes(w, batch)
+    kvd = w["kv_heads"] // shards * w["head_dim"]
+    lb = layer_bytes(w, batch, shards)
     per_layer = (lb["attn_qkv_rope"] + lb["attn_wo_residual"] + lb["ffn_gate_up_swiglu"] +
                  lb["ffn_down_residual"])
     kv = L * batch * 2 * kvd * e * (mean_pos + 1)
@@ -222,6 +253,8 @@ def main():
     ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
+    ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
+                    help="N > 1: tensor parallel (8B default) or independent replicas")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="default: min(steps, 64)")
     ap.add_argument("--layers", type=int, default=0,
@@ -257,8 +290,9 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+        with StdoutToStderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(local)
 
@@ -269,10 +303,26 @@ def main():
     cfg = ab.LlamaConfig(w["dim"], w["layers"], w["heads"], w["kv_heads"], w["head_dim"],
                          w["hidden"], w["vocab"], w["seq"], batch=B, rope_theta=w["theta"],
                          dtype=ab.BF16 if w["bf16"] else ab.F32)
-    model = ab.LlamaModel(rt, cfg)
-    model.init_synthetic(w["seed"], 0.02)
+    mode = args.parallel
+    if mode == "auto":
+        mode = "tp" if w["bf16"] else "replicas"
+    tp = world > 1 and mode == "tp"
+    comm = None
+    if tp:
+        # rank 0 makes the NCCL id of the model's communicator; torch.distributed carries it
+        with StdoutToStderr():
+            uid = torch.zeros(ab._abi.COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(ab.Comm.unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            comm = ab.Comm(rt, bytes(uid.cpu().numpy().tobytes()), rank, world)
+    with StdoutToStderr():
+        model = ab.LlamaModel(rt, cfg, comm)
+        model.init_synthetic(w["seed"], 0.02)
     P = w["prompt"]
-    prompts = [prompt_tokens(w["seed"], 1000 + rank * B + b, P, 3, w["vocab"]) for b in range(B)]
+    # tensor parallel ranks decode the same streams; replicas each decode their own
+    sbase = 0 if tp else rank * B
+    prompts = [prompt_tokens(w["seed"], 1000 + sbase + b, P, 3, w["vocab"]) for b in range(B)]
     # prompt: forced tokens at positions 0..P-2
     for pos in range(P - 1):
         model.step_batch([prompts[b][pos] for b in range(B)], [pos] * B, logits=False)
@@ -310,8 +360,12 @@ def main():
         t = float(tt.item())
     start_tok = toks[-1].tolist()
     pos0 += args.steps
-    value = world * B * args.steps / t
-    nodes_loop = len(model.scheme().node_labels()) + 1  # + sample feedback
+    streams = B if tp else world * B
+    value = streams * args.steps / t
+    # our kernels per device-loop step: the step graph's kernel nodes (not the NCCL
+    # collectives, not the logits gather of step()) plus the sample feedback
+    nodes_loop = len([l for l in model.scheme().node_labels()
+                      if "allreduce" not in l and "allgather" not in l]) + (2 if tp else 1)
 
     # e2e through the reference-facing step(): DecodeSteps up, [B, vocab] logits down
     import numpy as np
@@ -328,7 +382,7 @@ def main():
         tt = torch.tensor([t_e2e], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_e2e = float(tt.item())
-    e2e = world * B * e2e_steps / t_e2e
+    e2e = streams * e2e_steps / t_e2e
 
     # per-kernel times (each node launched alone between CUDA events on the decode stream)
     sch = model.scheme()
@@ -340,24 +394,26 @@ def main():
         c[0] += 1
         c[1] += ms
     total_ms = sum(times)
-    lb = layer_bytes(w, B)
+    shards = world if tp else 1
+    lb = layer_bytes(w, B, shards)
     dom = max(per_label, key=lambda l: per_label[l][1])
     n_dom, ms_dom = per_label[dom]
     t_launch = ms_dom / n_dom / 1e3
     peak, peak_kind = load_peaks()
     achieved = lb[dom] / t_launch / 1e9 if dom in lb else None
     mean_pos = pos0 - args.steps - e2e_steps + args.steps / 2
-    sb = step_bytes(w, B, mean_pos)
+    sb = step_bytes(w, B, mean_pos, shards)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
         "config": {"workload": w["title"], "batch": B, "seq_len": w["seq"],
                    "positions": f"{pos0 - args.steps - e2e_steps}.."
                                 f"{pos0 - e2e_steps - 1}",
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "parallelism": (f"tp{world}" if tp else f"replicas{world}") if world > 1
+                   else "single",
                    "l2": "inputs larger than L2 (weights stream every step)"},
         "step_bytes": sb, "step_gbs": sb / (t / args.steps) / 1e9,
         "step_frac": sb / (t / args.steps) / 1e9 / peak,
@@ -387,6 +443,8 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     model.close()
+    if comm is not None:
+        comm.close()
     rt.close()
     if dist:
         dist.barrier()

@@ -283,6 +283,33 @@ int ab_llama_reset(ab_llama* m);
 int ab_llama_as_model(ab_llama* m, ab_autoregressive_model* out);
 int ab_llama_destroy(ab_llama* m);
 
+/* ---- tensor parallelism over NVLink (NCCL) --------------------------------------
+ * No counterpart in the reference (it runs on one device). One process per GPU; the
+ * communicator wraps NCCL, loaded at run time (the process's already-loaded
+ * libnccl.so.2 when there is one). Collectives are recorded into schemes and captured
+ * into the step graph like kernels. */
+typedef struct ab_comm ab_comm;
+#define AB_COMM_ID_BYTES 128
+/* A fresh communicator id (rank 0 makes it and shares it with the other ranks). */
+int ab_comm_unique_id(uint8_t* id);
+int ab_comm_create(ab_runtime* rt, const uint8_t* id, int32_t rank, int32_t world,
+                   ab_comm** out);
+int ab_comm_rank(const ab_comm* c, int32_t* rank, int32_t* world);
+/* Aborts outstanding collectives (error paths); destroy still frees the handle. */
+int ab_comm_abort(ab_comm* c);
+int ab_comm_destroy(ab_comm* c);
+/* NCCL's message for the last collective that failed inside a submit on this thread. */
+const char* ab_comm_last_error(void);
+
+/* Tensor-parallel Llama-shaped model: query heads, kv heads, SwiGLU columns and the
+ * vocabulary are split evenly over the communicator's ranks (each must divide); wq, wk,
+ * wv, w1, w3 and the classifier are row shards, wo and w2 column shards. The residual
+ * stream is replicated: after wo and after w2 one all-reduce sums the ranks' partial
+ * projections into it. The greedy pick takes every rank's best (value, id) and keeps
+ * the first maximum, the sample_argmax rule. Every rank must make the same calls. */
+int ab_llama_create_tp(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm,
+                       ab_llama** out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
