@@ -106,7 +106,7 @@ ab_attention_block* attention_block_new(ab_runtime* rt, uint32_t hidden, uint32_
         b->part = (float*)device_alloc(rt, floats * 4);
         b->counters = (uint32_t*)device_alloc(rt, counters * 4);
         if (tp) b->tp_y = (float*)device_alloc(rt, (size_t)max_batch * hidden * 4);
-        alloc_tc_scratch(rt, &b->tc, max_batch, hidden,
+        alloc_tc_scratch(rt, &b->tc, max_batch, (uint32_t)std::max<uint64_t>(qd, hidden),
                          (uint32_t)((3 * std::max<uint64_t>(qd, hidden) + 127) / 128));
     } catch (...) {
         cudaFree(b->q);
@@ -134,7 +134,7 @@ ab_swiglu_block* swiglu_block_new(ab_runtime* rt, uint32_t hidden, uint32_t inte
     try {
         b->hb = device_alloc(rt, (size_t)max_batch * intermediate * 4);
         if (tp) b->tp_y = (float*)device_alloc(rt, (size_t)max_batch * hidden * 4);
-        alloc_tc_scratch(rt, &b->tc, max_batch, hidden,
+        alloc_tc_scratch(rt, &b->tc, max_batch, std::max(hidden, intermediate),
                          std::max((intermediate + 63) / 64, (hidden + 127) / 128));
     } catch (...) {
         if (b->hb) cudaFree(b->hb);

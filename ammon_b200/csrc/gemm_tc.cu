@@ -14,8 +14,14 @@
 //    their 32 TMEM lanes with tcgen05.ld.
 //  - TMEM is allocated only after griddepcontrol.wait, so a successor launched early by
 //    programmatic dependent launch never holds TMEM that this kernel's later CTAs need.
-//  - Split-K partials go to an L2-resident fp32 workspace; the last CTA of a tile (atomic
-//    ticket) folds them in split order and applies the epilogue.
+//  - Split-K partials go to an L2-resident fp32 workspace; a second kernel folds them in
+//    split order and applies the epilogue.
+//  - fp32 weights take the same path on the tf32 tensor cores with three products per
+//    k-step (3xTF32): every value v is split exactly into hi = v with its low 13 mantissa
+//    bits cleared and lo = v - hi, and D += Wlo.Xhi + Whi.Xlo + Whi.Xhi keeps the error of
+//    each product near 2^-22 relative, inside the fp32 parity bar. Activations are split
+//    once per launch by the kernel that normalises them; weight tiles are split in shared
+//    memory after they land, so the weights stay plain fp32 tensors in HBM.
 //  - Every mbarrier wait is bounded (%globaltimer); a wait that runs out raises the device
 //    flag, and the CTA still releases its TMEM.
 #include <algorithm>
@@ -31,6 +37,8 @@ constexpr int kTcThreads = 128;
 constexpr int kTcBM = 128;
 constexpr int kTcBK = 64;  // bf16 elements per k-block: one 128-byte swizzled row
 constexpr int kTcMaxStages = 8;
+constexpr int kTfBK = 32;          // fp32 elements per k-block: one 128-byte swizzled row
+constexpr int kTfThreads = 192;    // producer warp, MMA warp, 4 split/epilogue warps
 
 // ---- tcgen05 wrappers -------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
@@ -56,6 +64,16 @@ __device__ __forceinline__ void tc_mma_bf16(uint32_t d, uint64_t a, uint64_t b, 
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m)
+        : "memory");
+}
+// D[tmem] (+)= A x B^T on the tf32 pipe (fp32 operands in shared memory, read as tf32).
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+    const uint32_t m = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m)
         : "memory");
 }
@@ -96,6 +114,20 @@ __host__ __device__ constexpr uint32_t tc_idesc_bf16(uint32_t M, uint32_t N) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// Instruction descriptor of kind::tf32: f32 accumulate, tf32 A and B, both K-major.
+__host__ __device__ constexpr uint32_t tc_idesc_tf32(uint32_t M, uint32_t N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// High part of the exact split v = hi + lo: v with its 13 low mantissa bits cleared (a
+// tf32 value). lo = v - hi is exact in fp32 and carries the cleared bits.
+__device__ __forceinline__ float tf32_hi(float v) {
+    return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+}
+
+// Named barrier of the 128 epilogue threads (the four warps that own the TMEM lanes).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 // ---- epilogue on a chunk of 16 batch columns held by the thread of TMEM lane `row` ------------
 template <int EPI>
 __device__ __forceinline__ void tc_epilogue_chunk(const GemmTcParams& p, uint32_t tile,
@@ -108,7 +140,7 @@ __device__ __forceinline__ void tc_epilogue_chunk(const GemmTcParams& p, uint32_
 #pragma unroll
             for (int j = 0; j < 16; j++) xch[j * 64 + (row - 64)] = v[j];
         }
-        __syncthreads();
+        epi_sync();
         if (row < 64) {
             const uint32_t u = tile * 64 + row;
 #pragma unroll
@@ -121,7 +153,7 @@ __device__ __forceinline__ void tc_epilogue_chunk(const GemmTcParams& p, uint32_
                 else ((bf16*)p.out)[o] = __float2bfloat16_rn(s * y1);
             }
         }
-        __syncthreads();
+        epi_sync();
         return;
     }
     float partner[16];
@@ -308,6 +340,201 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// fp32 weights on the tf32 pipe (3xTF32). Stage s holds [W | W lo | X hi | X lo], each a
+// K-major 128-byte-swizzled tile of 32 fp32 per row. Warp 0 (lane 0) loads W, X hi and
+// X lo by TMA; warps 2-5 split the landed W tile in place into hi and lo (fence to the
+// async proxy, then every thread arrives on split_bar[s]); warp 1 (lane 0) issues three
+// tf32 MMAs per 8-element k-step and commits the stage back to the producer. Warps 2-5
+// then own TMEM lanes 32 * (warp % 4) .. + 31 for the epilogue.
+template <int EPI>
+__global__ void __launch_bounds__(kTfThreads, 1)
+    gemm_tf32x3_kernel(const GemmTcParams p, const __grid_constant__ CUtensorMap ta0,
+                       const __grid_constant__ CUtensorMap ta1,
+                       const __grid_constant__ CUtensorMap ta2,
+                       const __grid_constant__ CUtensorMap tb_hi,
+                       const __grid_constant__ CUtensorMap tb_lo) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t split_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int sm_ok;
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t a_bytes = kTcBM * 128;
+    const uint32_t b_bytes = p.bn * 128;
+    const uint32_t stage_bytes = 2 * a_bytes + 2 * b_bytes;
+    float* xch = (float*)(smem + (size_t)p.stages * stage_bytes);  // [16][64]
+    const uint32_t tile = blockIdx.x, split = blockIdx.y;
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t kb0 = (uint32_t)((uint64_t)split * p.kblocks / p.ksplit);
+    const uint32_t kb1 = (uint32_t)((uint64_t)(split + 1) * p.kblocks / p.ksplit);
+    const uint32_t nk = kb1 - kb0;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < p.stages; s++) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&split_bar[s]), 128);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        mbar_init(smem_u32(&done_bar), 1);
+        fence_barrier_init();
+        sm_ok = 1;
+    }
+    pdl_wait();
+    if (warp == 0) tmem_alloc(smem_u32(&tmem_slot), p.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (threadIdx.x == 0) {
+        // TMA producer
+        for (uint32_t i = 0; i < nk; i++) {
+            const uint32_t s = i % p.stages;
+            if (i >= p.stages &&
+                !mbar_wait_bounded(smem_u32(&empty_bar[s]), ((i / p.stages) - 1) & 1)) {
+                sm_ok = 0;
+                break;
+            }
+            const int32_t kx = (int32_t)((kb0 + i) * kTfBK);
+            const uint32_t bar = smem_u32(&full_bar[s]);
+            const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
+            const uint32_t b = a + 2 * a_bytes;
+            mbar_arrive_expect_tx(bar, a_bytes + 2 * b_bytes);
+            if (p.interleave) {
+                tma_load_2d(a, &ta0, kx, (int32_t)(tile * 64), bar);
+                tma_load_2d(a + 64 * 128, &ta1, kx, (int32_t)(tile * 64), bar);
+            } else if (tile < p.seg_tiles[0]) {
+                tma_load_2d(a, &ta0, kx, (int32_t)(tile * kTcBM), bar);
+            } else if (tile < p.seg_tiles[0] + p.seg_tiles[1]) {
+                tma_load_2d(a, &ta1, kx, (int32_t)((tile - p.seg_tiles[0]) * kTcBM), bar);
+            } else {
+                tma_load_2d(a, &ta2, kx,
+                            (int32_t)((tile - p.seg_tiles[0] - p.seg_tiles[1]) * kTcBM), bar);
+            }
+            tma_load_2d(b, &tb_hi, kx, 0, bar);
+            tma_load_2d(b + b_bytes, &tb_lo, kx, 0, bar);
+        }
+    } else if (threadIdx.x == 32) {
+        // MMA issuer: small products first, then Whi.Xhi
+        const uint32_t idesc = tc_idesc_tf32(kTcBM, p.bn);
+        for (uint32_t i = 0; i < nk; i++) {
+            const uint32_t s = i % p.stages;
+            if (!mbar_wait_bounded(smem_u32(&split_bar[s]), (i / p.stages) & 1)) {
+                sm_ok = 0;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t whi = smem_u32(smem + (size_t)s * stage_bytes);
+            const uint32_t wlo = whi + a_bytes;
+            const uint32_t xhi = whi + 2 * a_bytes;
+            const uint32_t xlo = xhi + b_bytes;
+#pragma unroll
+            for (uint32_t k = 0; k < kTfBK / 8; k++) {
+                tc_mma_tf32(tmem, sw128_desc(wlo + 32 * k), sw128_desc(xhi + 32 * k), idesc,
+                            (i | k) != 0);
+                tc_mma_tf32(tmem, sw128_desc(whi + 32 * k), sw128_desc(xlo + 32 * k), idesc, 1);
+                tc_mma_tf32(tmem, sw128_desc(whi + 32 * k), sw128_desc(xhi + 32 * k), idesc, 1);
+            }
+            tc_commit(smem_u32(&empty_bar[s]));
+        }
+        tc_commit(smem_u32(&done_bar));
+    } else if (warp >= 2) {
+        // split the landed W tile: hi in place, lo beside it (same swizzled offsets)
+        const uint32_t t = threadIdx.x - 64;
+        for (uint32_t i = 0; i < nk; i++) {
+            const uint32_t s = i % p.stages;
+            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+                sm_ok = 0;
+                break;
+            }
+            float4* w = (float4*)(smem + (size_t)s * stage_bytes);
+            float4* wl = w + a_bytes / 16;
+#pragma unroll 4
+            for (uint32_t j = t; j < a_bytes / 16; j += 128) {
+                const float4 v = w[j];
+                const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z),
+                                             tf32_hi(v.w));
+                w[j] = h;
+                wl[j] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(smem_u32(&split_bar[s]));
+        }
+    }
+    const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0);
+    tc_fence_after();
+    const bool ok = __syncthreads_and(got && sm_ok != 0);
+    pdl_trigger();
+
+    if (ok) {
+        if (warp >= 2) {
+            const uint32_t quarter = warp & 3;
+            const uint32_t row = quarter * 32 + lane;  // TMEM lane = tile row
+            const uint32_t taddr = tmem + ((quarter * 32u) << 16);
+            if (p.ksplit == 1) {
+                for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + c0, v);
+                    tc_epilogue_chunk<EPI>(p, tile, row, c0, v, xch);
+                }
+            } else {
+                float* ws = p.ws + ((size_t)split * p.tiles + tile) * p.bn * kTcBM;
+                for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + c0, v);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) ws[(size_t)(c0 + j) * kTcBM + row] = v[j];
+                }
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        atomicOr(p.flags, kFlagWaitTimeout);
+        mbar_wait_bounded(smem_u32(&done_bar), 0);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, p.tmem_cols);
+    }
+}
+
+// Exact tf32 split of fp32 activation rows, optionally RMS-normalised first
+// (src/kernels.rs:75-101: o = w * (ss * x), ss = 1 / sqrt(mean(x^2) + eps)):
+// hi[r, k] = tf32_hi(o), lo[r, k] = o - hi[r, k]. One 256-thread block per row.
+template <bool NORM, typename WT>
+__global__ void __launch_bounds__(256)
+    split_rows_tf32_kernel(const float* __restrict__ x, uint32_t x_stride,
+                           const WT* __restrict__ w, float* __restrict__ hi,
+                           float* __restrict__ lo, uint32_t dim, float eps) {
+    pdl_wait();
+    const float* xr = x + (uint64_t)blockIdx.x * x_stride;
+    float scale = 1.0f;
+    if (NORM) {
+        __shared__ float red[8];
+        float ss = 0.0f;
+        for (uint32_t k = threadIdx.x; k < dim; k += 256) ss = fmaf(xr[k], xr[k], ss);
+        ss = warp_sum(ss);
+        if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+        __syncthreads();
+        float t = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) t += red[i];
+        scale = 1.0f / sqrtf(t / (float)dim + eps);
+    }
+    float* hr = hi + (uint64_t)blockIdx.x * dim;
+    float* lr = lo + (uint64_t)blockIdx.x * dim;
+    for (uint32_t k = threadIdx.x; k < dim; k += 256) {
+        const float v = NORM ? to_f32(w[k]) * (scale * xr[k]) : xr[k];
+        const float h = tf32_hi(v);
+        hr[k] = h;
+        lr[k] = v - h;
+    }
+    pdl_trigger();
+}
+
 // RMSNorm of fp32 rows into bf16 rows (the GEMM's activation operand): o = w * (ss * x),
 // ss = 1 / sqrt(mean(x^2) + eps) (src/kernels.rs:75-101). One 256-thread block per row.
 template <typename WT>
@@ -437,18 +664,21 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const GemmTcParams
     }
 }
 
-GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave) {
+GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave,
+                        bool f32) {
     GemmTcPlan pl = {};
     pl.bn = std::max(16u, (batch + 15) / 16 * 16);
     pl.tiles = interleave ? rows / 64 : (rows + kTcBM - 1) / kTcBM;
-    pl.kblocks = K / kTcBK;
-    const uint32_t stage_bytes = kTcBM * 128 + pl.bn * 128;
-    const uint32_t per_sm = pl.bn <= 128 ? 2 : 1;
+    pl.kblocks = K / (f32 ? kTfBK : kTcBK);
+    // bf16: [W | X]; fp32: [W | W lo | X hi | X lo], 128 bytes per tile row
+    const uint32_t stage_bytes = (kTcBM * 128 + pl.bn * 128) * (f32 ? 2 : 1);
+    const uint32_t per_sm = pl.bn <= 128 && 2 * stage_bytes <= 100u * 1024 ? 2 : 1;
     const uint32_t budget = (per_sm == 2 ? 100u : 200u) * 1024;
     pl.stages = std::max(2u, std::min((uint32_t)kTcMaxStages, budget / stage_bytes));
     const uint32_t target = (uint32_t)std::max(sms, 1) * per_sm;
     uint32_t ks = (target + pl.tiles / 2) / std::max(pl.tiles, 1u);
-    ks = std::min(ks, std::max(1u, pl.kblocks / 4));
+    // fp32 k-blocks carry three MMAs each: two of them per split still hide the fill
+    ks = std::min(ks, std::max(1u, pl.kblocks / (f32 ? 2 : 4)));
     pl.ksplit = std::max(1u, ks);
     pl.smem = (size_t)pl.stages * stage_bytes + 16 * 64 * 4 + 1024;
     uint32_t cols = 32;
@@ -467,15 +697,16 @@ void gemm_tc_scratch(uint32_t max_tiles, uint32_t max_batch, int sms, uint64_t* 
     *tickets = max_tiles;
 }
 
-void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t hidden,
+void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t max_k,
                       uint32_t max_tiles) {
     if (max_batch <= kGemvMaxBatch) return;
     rt->activate();
     GemmScratch t;
     try {
-        const size_t xb = (size_t)max_batch * hidden * 2;
-        cuda_check(cudaMalloc(&t.xn, xb), "cudaMalloc");
-        cuda_check(cudaMemset(t.xn, 0, xb), "cudaMemset");
+        // bf16 activation rows, or the fp32 hi and lo halves of the 3xTF32 path
+        t.xn_bytes = (uint64_t)max_batch * max_k * 8;
+        cuda_check(cudaMalloc(&t.xn, t.xn_bytes), "cudaMalloc");
+        cuda_check(cudaMemset(t.xn, 0, t.xn_bytes), "cudaMemset");
         gemm_tc_scratch(max_tiles, max_batch, rt->sm_count, &t.ws_floats, &t.tickets_n);
         cuda_check(cudaMalloc(&t.ws, t.ws_floats * 4), "cudaMalloc");
         cuda_check(cudaMalloc(&t.tickets, (size_t)t.tickets_n * 4), "cudaMalloc");
@@ -496,14 +727,15 @@ void free_tc_scratch(GemmScratch* g) {
 
 void attach_tc_scratch(GemvParams* p, const GemmScratch& g) {
     p->xn = g.xn;
+    p->xn_bytes = g.xn_bytes;
     p->ws = g.ws;
     p->ws_floats = g.ws_floats;
     p->tickets = g.tickets;
     p->tickets_n = g.tickets_n;
 }
 
-bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave) {
-    if (batch == 0 || batch > 256 || K == 0 || K % kTcBK) return false;
+bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave, bool f32) {
+    if (batch == 0 || batch > 256 || K == 0 || K % (f32 ? kTfBK : kTcBK)) return false;
     // a single stacked segment may end in a partial tile: TMA fills the missing rows with
     // zeros and the epilogues skip rows >= n_rows
     return interleave ? rows % 64 == 0 : rows > 0;
@@ -511,16 +743,26 @@ bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave) {
 
 template <int EPI>
 static void add_gemm_tc(ab_scheme* s, const char* label, const GemmTcParams& p,
-                        const CUtensorMap* maps, size_t smem) {
-    auto kern = gemm_tc_kernel<EPI>;
-    const CUtensorMap a0 = maps[0], a1 = maps[1], a2 = maps[2], b = maps[3];
+                        const CUtensorMap* maps, size_t smem, bool f32) {
+    const CUtensorMap a0 = maps[0], a1 = maps[1], a2 = maps[2], b = maps[3], blo = maps[4];
     dim3 grid(p.tiles, p.ksplit);
-    s->add(label, [=](cudaStream_t st) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        return launch(st, grid, dim3(kTcThreads), smem, true, kern, p, a0, a1, a2, b);
-    });
+    if (f32) {
+        auto kern = gemm_tf32x3_kernel<EPI>;
+        s->add(label, [=](cudaStream_t st) {
+            cudaError_t e = cudaFuncSetAttribute(
+                kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            return launch(st, grid, dim3(kTfThreads), smem, true, kern, p, a0, a1, a2, b, blo);
+        });
+    } else {
+        auto kern = gemm_tc_kernel<EPI>;
+        s->add(label, [=](cudaStream_t st) {
+            cudaError_t e = cudaFuncSetAttribute(
+                kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            return launch(st, grid, dim3(kTcThreads), smem, true, kern, p, a0, a1, a2, b);
+        });
+    }
     if (p.ksplit > 1) {
         auto fold = splitk_epilogue_kernel<EPI>;
         dim3 fgrid(p.tiles, (p.bn + 7) / 8);
@@ -530,14 +772,17 @@ static void add_gemm_tc(ab_scheme* s, const char* label, const GemmTcParams& p,
     }
 }
 
-void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void* const* segs,
-                    const uint32_t* seg_rows, int nseg, const void* x_bf16, uint32_t x_stride,
-                    int epi) {
+void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, int32_t wdtype,
+                    const void* const* segs, const uint32_t* seg_rows, int nseg, const void* x,
+                    const void* x_lo, uint32_t x_stride, int epi) {
+    const bool f32 = wdtype == AB_F32;
+    if (f32 != (x_lo != nullptr))
+        fail(AB_ERR_ARGUMENT, std::string(label) + ": fp32 GEMM needs the split activation");
     const int sms = s->rt ? s->rt->sm_count : 148;
     uint32_t rows = 0;
     for (int i = 0; i < nseg; i++) rows += seg_rows[i];
     if (p.interleave) rows = seg_rows[0];
-    const GemmTcPlan pl = gemm_tc_plan(rows, p.K, p.nb, sms, p.interleave != 0);
+    const GemmTcPlan pl = gemm_tc_plan(rows, p.K, p.nb, sms, p.interleave != 0, f32);
     p.bn = pl.bn;
     p.tiles = pl.tiles;
     p.kblocks = pl.kblocks;
@@ -546,21 +791,51 @@ void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void*
     p.tmem_cols = pl.tmem_cols;
     if (pl.ws_floats > p.ws_floats || (pl.ksplit > 1 && p.tickets_n < pl.tiles))
         fail(AB_ERR_ARGUMENT, std::string(label) + ": GEMM workspace too small");
-    CUtensorMap maps[4];
+    const int32_t dt = f32 ? AB_F32 : AB_BF16;
+    const uint32_t esz = f32 ? 4 : 2;
+    const uint32_t bk = f32 ? kTfBK : kTcBK;
+    CUtensorMap maps[5];
     const uint32_t box_rows = p.interleave ? 64 : kTcBM;
     for (int i = 0; i < 3; i++) {
         const int j = i < nseg ? i : 0;
         p.seg_tiles[i] = i < nseg && !p.interleave ? (seg_rows[i] + kTcBM - 1) / kTcBM : 0;
-        encode_tmap_2d(&maps[i], AB_BF16, segs[j], p.K, seg_rows[j], (uint64_t)p.K * 2, kTcBK,
+        encode_tmap_2d(&maps[i], dt, segs[j], p.K, seg_rows[j], (uint64_t)p.K * esz, bk,
                        box_rows, 128);
     }
-    encode_tmap_2d(&maps[3], AB_BF16, x_bf16, p.K, p.nb, (uint64_t)x_stride * 2, kTcBK, pl.bn, 128);
+    encode_tmap_2d(&maps[3], dt, x, p.K, p.nb, (uint64_t)x_stride * esz, bk, pl.bn, 128);
+    maps[4] = maps[3];
+    if (f32)
+        encode_tmap_2d(&maps[4], dt, x_lo, p.K, p.nb, (uint64_t)x_stride * esz, bk, pl.bn, 128);
     switch (epi) {
-        case kEpiStore: return add_gemm_tc<kEpiStore>(s, label, p, maps, pl.smem);
-        case kEpiQkv: return add_gemm_tc<kEpiQkv>(s, label, p, maps, pl.smem);
-        case kEpiSwiglu: return add_gemm_tc<kEpiSwiglu>(s, label, p, maps, pl.smem);
-        case kEpiResidual: return add_gemm_tc<kEpiResidual>(s, label, p, maps, pl.smem);
+        case kEpiStore: return add_gemm_tc<kEpiStore>(s, label, p, maps, pl.smem, f32);
+        case kEpiQkv: return add_gemm_tc<kEpiQkv>(s, label, p, maps, pl.smem, f32);
+        case kEpiSwiglu: return add_gemm_tc<kEpiSwiglu>(s, label, p, maps, pl.smem, f32);
+        case kEpiResidual: return add_gemm_tc<kEpiResidual>(s, label, p, maps, pl.smem, f32);
         default: fail(AB_ERR_ARGUMENT, "unsupported GEMM epilogue");
+    }
+}
+
+void record_split_rows_tf32(ab_scheme* s, const char* label, const float* x, uint32_t x_stride,
+                            const void* norm_w, int32_t w_dtype, float* hi, float* lo,
+                            uint32_t rows, uint32_t dim, float eps) {
+    if (!norm_w) {
+        s->add(label, [=](cudaStream_t st) {
+            return launch(st, dim3(rows), dim3(256), 0, true,
+                          split_rows_tf32_kernel<false, float>, x, x_stride,
+                          (const float*)nullptr, hi, lo, dim, eps);
+        });
+    } else if (w_dtype == AB_F32) {
+        const float* wp = (const float*)norm_w;
+        s->add(label, [=](cudaStream_t st) {
+            return launch(st, dim3(rows), dim3(256), 0, true, split_rows_tf32_kernel<true, float>,
+                          x, x_stride, wp, hi, lo, dim, eps);
+        });
+    } else {
+        const bf16* wp = (const bf16*)norm_w;
+        s->add(label, [=](cudaStream_t st) {
+            return launch(st, dim3(rows), dim3(256), 0, true, split_rows_tf32_kernel<true, bf16>,
+                          x, x_stride, wp, hi, lo, dim, eps);
+        });
     }
 }
 

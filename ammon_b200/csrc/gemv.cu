@@ -367,8 +367,9 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
     p.nchunks = (p.K + CH - 1) / CH;
     const uint32_t Kpad = p.nchunks * CH;
     const int sms = s->rt ? s->rt->sm_count : 148;
-    if (wdtype == AB_BF16 && batch > kGemvMaxBatch && p.ws != nullptr) {
+    if (batch > kGemvMaxBatch && p.ws != nullptr) {
         // a dense contraction: tensor-core tiles read each weight once for the whole batch
+        const bool f32 = wdtype == AB_F32;
         const bool inter = epi == kEpiSwiglu;
         int nseg = 0;
         bool segs_ok = true;
@@ -378,11 +379,26 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
         for (int i = 0; i < nseg; i++)
             if (!inter && nseg > 1 && p.seg_rows[i] % 128) segs_ok = false;
         const uint32_t rows = inter ? p.seg_rows[0] : p.n_rows;
-        const bool x_ok = pro == kProNorm ? p.xn != nullptr : p.x_dtype == AB_BF16;
-        if (segs_ok && x_ok && gemm_tc_fits(rows, p.K, batch, inter)) {
+        // fp32: the activation is split into tf32 halves in the scratch (normalised or not)
+        const bool x_ok =
+            f32 ? p.x_dtype == AB_F32 && p.xn != nullptr &&
+                      (uint64_t)batch * p.K * 8 <= p.xn_bytes
+                : pro == kProNorm ? p.xn != nullptr : p.x_dtype == AB_BF16;
+        if (segs_ok && x_ok && gemm_tc_fits(rows, p.K, batch, inter, f32)) {
             const void* xb = p.x;
+            const void* xlo = nullptr;
             uint32_t xs = p.x_stride;
-            if (pro == kProNorm) {
+            if (f32) {
+                float* hi = (float*)p.xn;
+                float* lo = hi + (uint64_t)batch * p.K;
+                record_split_rows_tf32(s, (std::string(label) + "_split").c_str(),
+                                       (const float*)p.x, p.x_stride,
+                                       pro == kProNorm ? p.norm_w : nullptr, p.norm_dtype, hi, lo,
+                                       batch, p.K, p.eps);
+                xb = hi;
+                xlo = lo;
+                xs = p.K;
+            } else if (pro == kProNorm) {
                 record_rmsnorm_rows_bf16(s, (std::string(label) + "_norm").c_str(),
                                          (const float*)p.x, p.norm_w, p.norm_dtype, p.xn, batch,
                                          p.K, p.eps);
@@ -414,7 +430,7 @@ void record_gemv(ab_scheme* s, const char* label, GemvParams p, int32_t wdtype, 
             g.cache_stride = p.cache_stride;
             g.step = p.step;
             g.flags = p.flags;
-            record_gemm_tc(s, label, g, p.seg, p.seg_rows, nseg, xb, xs, epi);
+            record_gemm_tc(s, label, g, wdtype, p.seg, p.seg_rows, nseg, xb, xlo, xs, epi);
             return;
         }
     }

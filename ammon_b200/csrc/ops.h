@@ -63,16 +63,18 @@ struct GemvParams {
     uint64_t cache_stride;  // elements between consecutive batch rows of the cache
     const Step* step;
     uint32_t* flags;
-    // scratch for the tensor-core path at batch > 4 (bf16 weights); null = GEMV only
-    void* xn;        // bf16 [batch, K]: the normalised activation (kProNorm)
+    // scratch for the tensor-core path at batch > 4; null = GEMV only
+    void* xn;        // the GEMM's activation operand: bf16 [batch, K] (normalised for
+                     // kProNorm), or for fp32 weights the tf32 hi and lo halves [2][batch, K]
+    uint64_t xn_bytes;
     float* ws;       // split-K partials
     uint64_t ws_floats;
     uint32_t* tickets;  // one per row tile, zero between launches
     uint32_t tickets_n;
 };
 
-// Largest batch the GEMV serves in one launch; above it bf16 weights go to the
-// tensor-core GEMM (gemm_tc.cu).
+// Largest batch the GEMV serves in one launch; above it the weights go to the tensor-core
+// GEMM (gemm_tc.cu): bf16 on the f16 pipe, fp32 as 3xTF32 on the tf32 pipe.
 constexpr uint32_t kGemvMaxBatch = 4;
 
 // Parameters of one tensor-core GEMM launch (gemm_tc.cu).
@@ -107,11 +109,17 @@ struct GemmTcPlan {
     uint64_t ws_floats;
 };
 
-GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave);
-bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave);
-void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, const void* const* segs,
-                    const uint32_t* seg_rows, int nseg, const void* x_bf16, uint32_t x_stride,
-                    int epi);
+GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave,
+                        bool f32);
+bool gemm_tc_fits(uint32_t rows, uint32_t K, uint32_t batch, bool interleave, bool f32);
+// x: bf16 activation rows (wdtype bf16), or the tf32 hi rows with x_lo the lo rows (fp32).
+void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, int32_t wdtype,
+                    const void* const* segs, const uint32_t* seg_rows, int nseg, const void* x,
+                    const void* x_lo, uint32_t x_stride, int epi);
+// hi/lo [rows, dim] = exact tf32 split of x (RMS-normalised with norm_w when non-null).
+void record_split_rows_tf32(ab_scheme* s, const char* label, const float* x, uint32_t x_stride,
+                            const void* norm_w, int32_t w_dtype, float* hi, float* lo,
+                            uint32_t rows, uint32_t dim, float eps);
 void record_rmsnorm_rows_bf16(ab_scheme* s, const char* label, const float* x, const void* w,
                               int32_t w_dtype, void* out, uint32_t rows, uint32_t dim, float eps);
 // Workspace floats and tickets that cover every tensor-core GEMM with up to `max_tiles`
@@ -119,17 +127,19 @@ void record_rmsnorm_rows_bf16(ab_scheme* s, const char* label, const float* x, c
 void gemm_tc_scratch(uint32_t max_tiles, uint32_t max_batch, int sms, uint64_t* ws_floats,
                      uint32_t* tickets);
 
-// Scratch of the tensor-core GEMM path owned by a module: the bf16 normalised
-// activation [max_batch, hidden], the split-K partials and one ticket per row tile.
-// Nothing is allocated when max_batch is within the GEMV's range.
+// Scratch of the tensor-core GEMM path owned by a module: the activation operand
+// (8 bytes per element of [max_batch, max_k]: bf16 rows or fp32 hi/lo halves), the
+// split-K partials and one ticket per row tile. Nothing is allocated when max_batch is
+// within the GEMV's range.
 struct GemmScratch {
     void* xn = nullptr;
+    uint64_t xn_bytes = 0;
     float* ws = nullptr;
     uint64_t ws_floats = 0;
     uint32_t* tickets = nullptr;
     uint32_t tickets_n = 0;
 };
-void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t hidden,
+void alloc_tc_scratch(Runtime* rt, GemmScratch* g, uint32_t max_batch, uint32_t max_k,
                       uint32_t max_tiles);
 void free_tc_scratch(GemmScratch* g);
 void attach_tc_scratch(GemvParams* p, const GemmScratch& g);

@@ -41,14 +41,15 @@ METRIC = "decode tokens/sec (batch 1 and 64) at 1/2/4/8 B200; per-kernel HBM GB/
 WORKLOADS = {
     "llama3-8b-bf16": dict(dim=4096, layers=32, heads=32, kv_heads=8, head_dim=128,
                            hidden=14336, vocab=128256, seq=8192, theta=500000.0, bf16=True,
-                           seed=3, prompt=128,
+                           seed=3, prompt=128, batch=1,
                            title="Llama-3-8B-shaped bf16 decode"),
     "llama-110m-f32": dict(dim=768, layers=12, heads=12, kv_heads=12, head_dim=64, hidden=2048,
                            vocab=32000, seq=1024, theta=10000.0, bf16=False, seed=1, prompt=16,
+                           batch=256, split_streams=True,
                            title="Llama-shaped 110M fp32 multi-stream decode"),
     "tiny-llama-f32": dict(dim=288, layers=6, heads=6, kv_heads=6, head_dim=48, hidden=768,
                            vocab=32000, seq=256, theta=10000.0, bf16=False, seed=0, prompt=8,
-                           title="Tiny llama2.c fp32 decode"),
+                           batch=1, title="Tiny llama2.c fp32 decode"),
 }
 
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -251,7 +252,9 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS))
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="streams per rank (default: the workload's; the 110M workload's 256 "
+                         "streams are split over the ranks)")
     ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
     ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
                     help="N > 1: tensor parallel (8B default) or independent replicas")
@@ -277,6 +280,14 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    split_streams = False
+    if not args.batch:
+        args.batch = w["batch"]
+        if w.get("split_streams") and world > 1 and args.parallel != "tp":
+            if args.batch % world:
+                raise SystemExit(f"{args.batch} streams do not split over {world} ranks")
+            args.batch //= world
+            split_streams = True
     if args.impl == "reference":
         run_reference(args, w, rank, world)
         return
@@ -407,13 +418,14 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if tp or split_streams else "weak",
+        "vs_baseline": None,
         "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
         "config": {"workload": w["title"], "batch": B, "seq_len": w["seq"],
                    "positions": f"{pos0 - args.steps - e2e_steps}.."
                                 f"{pos0 - e2e_steps - 1}",
-                   "parallelism": (f"tp{world}" if tp else f"replicas{world}") if world > 1
-                   else "single",
+                   "parallelism": (f"tp{world}" if tp else f"dp{world}" if split_streams
+                                   else f"replicas{world}") if world > 1 else "single",
                    "l2": "inputs larger than L2 (weights stream every step)"},
         "step_bytes": sb, "step_gbs": sb / (t / args.steps) / 1e9,
         "step_frac": sb / (t / args.steps) / 1e9 / peak,

@@ -216,6 +216,33 @@ def test_batched_bf16_model_on_tensor_cores(rt, orc, batch):
     assert "attn_qkv_rope_norm" in labels and "ffn_gate_up_swiglu_norm" in labels
 
 
+@pytest.mark.parametrize("batch", [5, 32, 256])
+def test_batched_fp32_model_on_tensor_cores(rt, orc, batch):
+    """Batches above 4 with fp32 weights run every projection as 3xTF32 on the tcgen05
+    tf32 pipe (exact hi/lo splits of weights and activations): each stream stays within
+    the fp32 bar of its own oracle decode and picks the oracle's greedy id. The vocab
+    ends in a partial 128-row tile and the K widths exercise split-K."""
+    cfg = dict(dim=256, layers=2, heads=4, kv_heads=4, head_dim=64, hidden=512, vocab=1000,
+               seq=16, theta=10000.0)
+    o, g = make_pair(rt, orc, batch=batch, seed=11, **cfg)
+    streams = sorted({0, 1, batch // 2, batch - 1})
+    refs = {b: orc.Model(cfg["dim"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
+                         cfg["head_dim"], cfg["hidden"], cfg["vocab"], cfg["seq"],
+                         theta=cfg["theta"], seed=11) for b in streams}
+    rng = np.random.default_rng(batch + 1)
+    toks = rng.integers(0, cfg["vocab"], size=(4, batch))
+    for pos in range(4):
+        logits, am = g.step_batch(toks[pos].tolist(), [pos] * batch, logits=True, argmax=True)
+        for b in streams:
+            want = refs[b].step(int(toks[pos, b]), pos)
+            assert rel(logits[b], want) < FP32_TOL, (batch, pos, b, rel(logits[b], want))
+            assert int(am[b]) == orc.sample_argmax(want), (batch, pos, b)
+        assert all(am[b] == int(np.argmax(logits[b])) for b in range(batch))
+    labels = g.scheme().node_labels()
+    assert "attn_qkv_rope_split" in labels and "attn_wo_residual_split" in labels
+    assert "final_norm_classifier_split" in labels
+
+
 def test_device_greedy_loop_matches_host_loop(rt, orc):
     """decode_device (argmax and the next DecodeStep on the device) emits the ids the
     reference loop (generate.rs:43-91 with host sample_argmax) emits."""
