@@ -96,6 +96,7 @@ SIGNATURES = {
     "ab_kernel_attention_partial": (C.c_int, [P, T, T, T, T, T]),
     "ab_kernel_attention_combine": (C.c_int, [P, T, T, T]),
     "ab_kernel_attention": (C.c_int, [P, T, T, T, T, T, T]),
+    "ab_kernel_attention_decode": (C.c_int, [P, T, T, T, T, T]),
     "ab_kernel_swiglu": (C.c_int, [P, T, T]),
     "ab_tensor_add_into": (C.c_int, [P, T, T, T]),
     "ab_tensor_matmul_into": (C.c_int, [P, T, T, T]),

@@ -409,12 +409,19 @@ __global__ void __launch_bounds__(kAttnThreads)
 }
 
 // ---- tensor-core kernel (bf16 K/V, head 64 or 128) --------------------------------------------
-// Same algorithm and TMA pipeline as above, with both products on mma.sync m16n8k16:
-//   S^T[64 pos x 8 heads] = K[64 x head] . Q^T[head x 8]   (each warp: 16 positions)
-//   O^T[head x 8]        += V^T[head x 64] . P^T[64 x 8]    (each warp: head/4 dims)
-// Q and P are split into bf16 high and low parts (two MMAs each), so scores and
-// weights keep close to fp32 precision; K and V are bf16 already. Operand fragments
-// come from the swizzled TMA tiles through ldmatrix (V transposed).
+// Each of the four warps owns 16 positions of every 64-position tile end to end, so warps
+// never wait for one another inside the loop:
+//   S[16 pos x 8 heads]   = K[16 x head] . Q^T[head x 8]        (mma.sync m16n8k16)
+//   online softmax per head over the warp's positions (its own running max and sum)
+//   O^T[head x 8 heads]  += V^T[head x 16 pos] . P^T[16 pos x 8] (P^T formed in registers by
+//                                                                 movmatrix.trans)
+// Q and P are split into bf16 high and low parts (two MMAs each), so scores and weights
+// keep close to fp32 precision; K and V are bf16 already. Operand fragments come from the
+// swizzled TMA tiles through ldmatrix (V transposed). Thread 0 refills a stage once all
+// four warps have released it (one arrival each on its empty barrier); the warps' partial
+// (max, sum, O) are merged through shared memory after the loop. Positions past the
+// current one inside the last tile are masked out of the softmax; they must hold finite
+// values (caches start zeroed), as their zero weights multiply them.
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -441,13 +448,21 @@ __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t* hi, uin
     *lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 template <int HD>
 struct AttnMmaLayout {
     static constexpr uint32_t kRowBytes = HD * 2;
-    static constexpr uint32_t kStage = 2 * kAttnTile * kRowBytes;
-    static constexpr uint32_t kP = kAttnStages * kStage;  // [2 parts][8 heads][64 pos] bf16
-    static constexpr uint32_t kO = kP + 2 * 8 * kAttnTile * 2;  // [8][HD] f32
-    static constexpr uint32_t kTail = kO + 8 * HD * 4;
+    static constexpr uint32_t kStage = 2 * kAttnTile * kRowBytes;  // K tile | V tile
+    static constexpr uint32_t kStages = HD == 128 ? 3 : 4;
+    static constexpr uint32_t kTail = kStages * kStage;  // then fold, split weights, ticket
+    static size_t smem(uint32_t G, uint32_t nsplit) {
+        return (size_t)kTail + (size_t)kAttnThreads * G * 4 + (size_t)nsplit * G * 4 + 16 + 1024;
+    }
 };
 
 template <typename OT, int G, int HD>
@@ -455,19 +470,18 @@ __global__ void __launch_bounds__(kAttnThreads)
     attn_decode_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                            const __grid_constant__ CUtensorMap vmap) {
     using LY = AttnMmaLayout<HD>;
+    constexpr uint32_t S = LY::kStages;
     constexpr uint32_t NBOX = LY::kRowBytes / 128;
-    constexpr int MT = HD / 64;  // 16-dim m-tiles per warp in P.V
+    constexpr int KS = HD / 16;  // k-steps of K.Q^T, m-tiles of V^T.P^T
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[kAttnStages];
-    __shared__ float red[4][8];
-    __shared__ float run_m[8], run_l[8], run_a[8];
+    __shared__ __align__(8) uint64_t full_bar[S];
+    __shared__ __align__(8) uint64_t empty_bar[S];
+    __shared__ float wm[4][8], wl[4][8], run_m[8], run_l[8];
+    __shared__ int sm_fail;
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const AttnTail T = attn_tail(LY::kTail, HD, G, p.nsplit);
-    bf16* pbuf = (bf16*)(smem + LY::kP);
-    float* obuf = (float*)(smem + LY::kO);
-    float* fold = (float*)(smem + T.fold_off);
-    float* wts = (float*)(smem + T.w_off);
-    int* sm_last = (int*)(smem + T.st_off);
+    float* fold = (float*)(smem + LY::kTail);  // [kAttnThreads][G]
+    float* wts = fold + kAttnThreads * G;      // [nsplit][G]
+    int* sm_last = (int*)(wts + p.nsplit * G);
 
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
@@ -481,20 +495,20 @@ __global__ void __launch_bounds__(kAttnThreads)
         return;
     }
     if (tid == 0) {
-        for (int s = 0; s < kAttnStages; s++) mbar_init(smem_u32(&full_bar[s]), 1);
+        for (uint32_t s = 0; s < S; s++) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 4);
+        }
         fence_barrier_init();
-    }
-    if (tid < 8) {
-        run_m[tid] = -INFINITY;
-        run_l[tid] = 0.0f;
+        sm_fail = 0;
     }
     // Q^T fragments (k = head dim, n = query head), pre-scaled, bf16 high + low parts
-    uint32_t qh[HD / 16][2], ql[HD / 16][2];
+    uint32_t qh[KS][2], ql[KS][2];
     {
         const float qscale = 1.0f / sqrtf((float)HD);
         const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * HD;
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ks++) {
+        for (int ks = 0; ks < KS; ks++) {
 #pragma unroll
             for (int h2 = 0; h2 < 2; h2++) {
                 const uint32_t d = ks * 16 + 2 * t + 8 * h2;
@@ -507,15 +521,12 @@ __global__ void __launch_bounds__(kAttnThreads)
             }
         }
     }
-    float o[MT][4];
-#pragma unroll
-    for (int m = 0; m < MT; m++) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.0f;
     __syncthreads();
 
     const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
     const int32_t ybase = (int32_t)(b * p.seq + start);
     auto issue = [&](uint32_t i) {
-        const uint32_t s = i % kAttnStages;
+        const uint32_t s = i % S;
         const uint32_t bar = smem_u32(&full_bar[s]);
         unsigned char* kst = smem + (size_t)s * LY::kStage;
         unsigned char* vst = kst + LY::kStage / 2;
@@ -528,157 +539,161 @@ __global__ void __launch_bounds__(kAttnThreads)
             tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
         }
     };
+    uint32_t issued = 0;  // meaningful in thread 0
     if (tid == 0)
-        for (uint32_t i = 0; i < ntiles && i < (uint32_t)kAttnStages; i++) issue(i);
+        for (; issued < ntiles && issued < S; issued++) issue(issued);
 
-    uint32_t failed_at = ntiles;
+    float o[KS][4];
+#pragma unroll
+    for (int m = 0; m < KS; m++) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.0f;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;  // heads 2t, 2t + 1
+    const uint32_t mi = lane / 8, r8 = lane % 8;
     for (uint32_t i = 0; i < ntiles; i++) {
-        const uint32_t s = i % kAttnStages;
-        const bool got = mbar_wait_bounded(smem_u32(&full_bar[s]), (i / kAttnStages) & 1);
-        if (!__syncthreads_and(got)) {
-            failed_at = i;
+        // thread 0 refills the stage of tile i - 1 once all four warps released it
+        if (tid == 0 && i >= 1 && issued < ntiles) {
+            const uint32_t r = i - 1;
+            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) issue(issued++);
+            else sm_fail = 1;
+        }
+        __syncwarp();
+        if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
+        const uint32_t s = i % S;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1))) {
+            sm_fail = 1;
             break;
         }
         const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
         const uint32_t kst = smem_u32(smem + (size_t)s * LY::kStage);
         const uint32_t vst = kst + LY::kStage / 2;
-        // S^T for positions 16*warp .. +15
-        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // S for positions 16 * warp + (g, g + 8), heads (2t, 2t + 1)
+        float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         {
             const uint32_t row = warp * 16 + (lane % 16);
 #pragma unroll
-            for (int ks = 0; ks < HD / 16; ks++) {
+            for (int ks = 0; ks < KS; ks++) {
                 const uint32_t colb = (ks % 4) * 32 + (lane / 16) * 16;
                 uint32_t a[4];
                 ldsm_x4(kst + swizzle_off<128>((ks / 4) * kAttnTile * 128 + row * 128 + colb), a);
-                mma_16816(sc, a, qh[ks][0], qh[ks][1]);
-                mma_16816(sc, a, ql[ks][0], ql[ks][1]);
+                mma_16816(sh, a, qh[ks][0], qh[ks][1]);
+                mma_16816(sl, a, ql[ks][0], ql[ks][1]);
             }
         }
-        const uint32_t p0 = warp * 16 + g, p1 = p0 + 8;
+        float sc[4] = {sh[0] + sl[0], sh[1] + sl[1], sh[2] + sl[2], sh[3] + sl[3]};
+        const uint32_t p0 = warp * 16 + g;
         if (p0 >= rows) sc[0] = sc[1] = -INFINITY;
-        if (p1 >= rows) sc[2] = sc[3] = -INFINITY;
-        // tile maximum per head (heads 2t, 2t+1 live in this thread)
-        float ma = fmaxf(sc[0], sc[2]), mb = fmaxf(sc[1], sc[3]);
+        if (p0 + 8 >= rows) sc[2] = sc[3] = -INFINITY;
+        float ta = fmaxf(sc[0], sc[2]), tb = fmaxf(sc[1], sc[3]);
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1) {
-            ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, off));
-            mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+            ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, off));
+            tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, off));
         }
-        if (g == 0) {
-            red[warp][2 * t] = ma;
-            red[warp][2 * t + 1] = mb;
-        }
-        __syncthreads();
-        if (tid < 8) {
-            const float tmax = fmaxf(fmaxf(red[0][tid], red[1][tid]), fmaxf(red[2][tid], red[3][tid]));
-            const float mnew = fmaxf(run_m[tid], tmax);
-            run_a[tid] = expf(run_m[tid] - mnew);
-            run_m[tid] = mnew;
-        }
-        __syncthreads();
-        const float m0 = run_m[2 * t], m1 = run_m[2 * t + 1];
-        const float e0 = expf(sc[0] - m0), e1 = expf(sc[1] - m1);
-        const float e2 = expf(sc[2] - m0), e3 = expf(sc[3] - m1);
-        float la = e0 + e2, lb = e1 + e3;
+        const float nA = fmaxf(mA, ta), nB = fmaxf(mB, tb);
+        // a warp whose positions were all masked so far keeps m = -inf and weight 0
+        const float aA = nA == -INFINITY ? 1.0f : expf(mA - nA);
+        const float aB = nB == -INFINITY ? 1.0f : expf(mB - nB);
+        const float e0 = nA == -INFINITY ? 0.0f : expf(sc[0] - nA);
+        const float e1 = nB == -INFINITY ? 0.0f : expf(sc[1] - nB);
+        const float e2 = nA == -INFINITY ? 0.0f : expf(sc[2] - nA);
+        const float e3 = nB == -INFINITY ? 0.0f : expf(sc[3] - nB);
+        mA = nA;
+        mB = nB;
+        lA = lA * aA + (e0 + e2);
+        lB = lB * aB + (e1 + e3);
 #pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            la += __shfl_xor_sync(0xffffffffu, la, off);
-            lb += __shfl_xor_sync(0xffffffffu, lb, off);
+        for (int m = 0; m < KS; m++) {
+            o[m][0] *= aA;
+            o[m][1] *= aB;
+            o[m][2] *= aA;
+            o[m][3] *= aB;
         }
-        // P^T (bf16 high / low) as [part][head][position]
-        {
-            uint32_t h01, l01, h23, l23;
-            split_bf16x2(e0, e1, &h01, &l01);  // (p0, heads 2t / 2t+1)
-            split_bf16x2(e2, e3, &h23, &l23);  // (p1, ...)
-            const __nv_bfloat162 H01 = *reinterpret_cast<__nv_bfloat162*>(&h01);
-            const __nv_bfloat162 L01 = *reinterpret_cast<__nv_bfloat162*>(&l01);
-            const __nv_bfloat162 H23 = *reinterpret_cast<__nv_bfloat162*>(&h23);
-            const __nv_bfloat162 L23 = *reinterpret_cast<__nv_bfloat162*>(&l23);
-            bf16* ph = pbuf;
-            bf16* pl = pbuf + 8 * kAttnTile;
-            ph[(2 * t) * kAttnTile + p0] = H01.x;
-            ph[(2 * t + 1) * kAttnTile + p0] = H01.y;
-            ph[(2 * t) * kAttnTile + p1] = H23.x;
-            ph[(2 * t + 1) * kAttnTile + p1] = H23.y;
-            pl[(2 * t) * kAttnTile + p0] = L01.x;
-            pl[(2 * t + 1) * kAttnTile + p0] = L01.y;
-            pl[(2 * t) * kAttnTile + p1] = L23.x;
-            pl[(2 * t + 1) * kAttnTile + p1] = L23.y;
-        }
-        __syncthreads();
-        if (g == 0) {
-            red[warp][2 * t] = la;
-            red[warp][2 * t + 1] = lb;
-        }
-        // O^T += V^T . P^T for dims [warp * HD/4, +HD/4)
-        {
-            const float a0 = run_a[2 * t], a1 = run_a[2 * t + 1];
+        // P^T fragments: the S accumulator holds (pos g / g + 8, heads 2t / 2t + 1); the
+        // transposed 8x8 blocks hold (head g, pos 2t / 2t + 1 and 8 + ...)
+        uint32_t h01, l01, h23, l23;
+        split_bf16x2(e0, e1, &h01, &l01);
+        split_bf16x2(e2, e3, &h23, &l23);
+        const uint32_t bh0 = movmatrix_trans(h01), bh1 = movmatrix_trans(h23);
+        const uint32_t bl0 = movmatrix_trans(l01), bl1 = movmatrix_trans(l23);
+        const uint32_t pos = warp * 16 + r8 + (mi >= 2 ? 8 : 0);
 #pragma unroll
-            for (int m = 0; m < MT; m++) {
-                o[m][0] *= a0;
-                o[m][1] *= a1;
-                o[m][2] *= a0;
-                o[m][3] *= a1;
-            }
-            const uint32_t* phw = reinterpret_cast<const uint32_t*>(pbuf);
-            const uint32_t* plw = reinterpret_cast<const uint32_t*>(pbuf + 8 * kAttnTile);
-            const uint32_t mi = lane / 8, r8 = lane % 8;
-#pragma unroll
-            for (int ks = 0; ks < kAttnTile / 16; ks++) {
-                const uint32_t bi = (g * kAttnTile + ks * 16 + 2 * t) / 2;
-                const uint32_t bh0 = phw[bi], bh1 = phw[bi + 4];
-                const uint32_t bl0 = plw[bi], bl1 = plw[bi + 4];
-                const uint32_t pos = ks * 16 + r8 + (mi >= 2 ? 8 : 0);
-#pragma unroll
-                for (int m = 0; m < MT; m++) {
-                    const uint32_t dim = warp * (HD / 4) + m * 16 + ((mi & 1) ? 8 : 0);
-                    const uint32_t byte = dim * 2;
-                    uint32_t a[4];
-                    ldsm_x4_t(vst + swizzle_off<128>((byte / 128) * kAttnTile * 128 + pos * 128 +
-                                                     byte % 128),
-                              a);
-                    mma_16816(o[m], a, bh0, bh1);
-                    mma_16816(o[m], a, bl0, bl1);
-                }
-            }
+        for (int m = 0; m < KS; m++) {
+            const uint32_t byte = (m * 16 + ((mi & 1) ? 8 : 0)) * 2;
+            uint32_t a[4];
+            ldsm_x4_t(vst + swizzle_off<128>((byte / 128) * kAttnTile * 128 + pos * 128 +
+                                             byte % 128),
+                      a);
+            mma_16816(o[m], a, bh0, bh1);
+            mma_16816(o[m], a, bl0, bl1);
         }
-        __syncthreads();
-        if (tid < 8)
-            run_l[tid] = run_l[tid] * run_a[tid] + red[0][tid] + red[1][tid] + red[2][tid] +
-                         red[3][tid];
-        if (tid == 0 && i + kAttnStages < ntiles) issue(i + kAttnStages);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
     }
-    if (failed_at < ntiles) {
+    __syncthreads();
+    if (sm_fail) {
+        // a bounded wait ran out: flag it, let the copies in flight land, and stop (only the
+        // last S issued tiles can still be in flight, each on the newest phase of its stage)
         if (tid == 0) {
             atomicOr(p.flags, kFlagWaitTimeout);
-            for (uint32_t i = failed_at; i < ntiles && i < failed_at + kAttnStages; i++)
-                mbar_wait_bounded(smem_u32(&full_bar[i % kAttnStages]), (i / kAttnStages) & 1);
+            for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
+                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1);
         }
         __syncthreads();
         pdl_trigger();
         return;
     }
     pdl_trigger();
-    // O^T fragments -> obuf[head][dim]
+    // merge the four warps: per-head max, rescaled sums and outputs (stage memory is free)
 #pragma unroll
-    for (int m = 0; m < MT; m++) {
-        const uint32_t d0 = warp * (HD / 4) + m * 16 + g;
+    for (int off = 4; off < 32; off <<= 1) {
+        lA += __shfl_xor_sync(0xffffffffu, lA, off);
+        lB += __shfl_xor_sync(0xffffffffu, lB, off);
+    }
+    if (g == 0) {
+        wm[warp][2 * t] = mA;
+        wm[warp][2 * t + 1] = mB;
+        wl[warp][2 * t] = lA;
+        wl[warp][2 * t + 1] = lB;
+    }
+    float* wo = (float*)smem;  // [4 warps][G][HD]
+#pragma unroll
+    for (int m = 0; m < KS; m++) {
+        const uint32_t d0 = m * 16 + g;
         if (2 * t < (uint32_t)G) {
-            obuf[(2 * t) * HD + d0] = o[m][0];
-            obuf[(2 * t) * HD + d0 + 8] = o[m][2];
+            wo[(warp * G + 2 * t) * HD + d0] = o[m][0];
+            wo[(warp * G + 2 * t) * HD + d0 + 8] = o[m][2];
         }
         if (2 * t + 1 < (uint32_t)G) {
-            obuf[(2 * t + 1) * HD + d0] = o[m][1];
-            obuf[(2 * t + 1) * HD + d0 + 8] = o[m][3];
+            wo[(warp * G + 2 * t + 1) * HD + d0] = o[m][1];
+            wo[(warp * G + 2 * t + 1) * HD + d0 + 8] = o[m][3];
         }
     }
     __syncthreads();
+    if (tid < (uint32_t)G) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w][tid]);
+        float L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; w++)
+            if (wm[w][tid] != -INFINITY) L += wl[w][tid] * expf(wm[w][tid] - M);
+        run_m[tid] = M;
+        run_l[tid] = L;
+    }
+    __syncthreads();
+    const uint32_t di = tid % HD;
     float acc[G];
 #pragma unroll
-    for (int h = 0; h < G; h++) acc[h] = tid < (uint32_t)HD ? obuf[h * HD + tid] : 0.0f;
-    attn_finish<OT, G>(p, acc, tid / HD, 1, tid % HD, fold, wts, run_m, run_l, sm_last, split,
-                       active, kvh, b, tid);
+    for (int h = 0; h < G; h++) {
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float mw = wm[w][h];
+            if (mw != -INFINITY) a += wo[(w * G + h) * HD + di] * expf(mw - run_m[h]);
+        }
+        acc[h] = a;
+    }
+    attn_finish<OT, G>(p, acc, tid / HD, 1, di, fold, wts, run_m, run_l, sm_last, split, active,
+                       kvh, b, tid);
 }
 
 // ---- plain-load kernel (head sizes the TMA boxes cannot tile) --------------------------------
@@ -835,8 +850,8 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
         const uint64_t rows = (uint64_t)p.batch * p.seq;
         encode_tmap_2d(&kmap, AB_BF16, p.kcache, inner, rows, inner * 2, 64, kAttnTile, 128);
         encode_tmap_2d(&vmap, AB_BF16, p.vcache, inner, rows, inner * 2, 64, kAttnTile, 128);
-        const uint32_t tail = p.head == 128 ? AttnMmaLayout<128>::kTail : AttnMmaLayout<64>::kTail;
-        const size_t smem = attn_tail(tail, p.head, G, p.nsplit).end + 1024;
+        const size_t smem = p.head == 128 ? AttnMmaLayout<128>::smem(G, p.nsplit)
+                                          : AttnMmaLayout<64>::smem(G, p.nsplit);
         if (smem > 220 * 1024) invalid("attention: shared-memory stage too large");
         if (p.head == 128) {
             auto kern = attn_decode_mma_kernel<OT, G, 128>;
@@ -955,38 +970,100 @@ static unsigned char* noalloc_scratch(int* device) {
 
 using namespace ab;
 
+// Validates the operands of the fused attention entry points and fills every AttnParams
+// field except the scratch (part_o, part_ml, counters, flags).
+static AttnParams attention_decode_operands(ab_tensor q, ab_tensor key_cache,
+                                            ab_tensor value_cache, ab_tensor out, ab_tensor step,
+                                            int sms) {
+    expect_data("q", q);
+    expect_data("key_cache", key_cache);
+    expect_data("value_cache", value_cache);
+    expect_data("out", out);
+    expect_dtype("q", q, AB_F32);
+    expect_rank_in("q", q, 2, 3);
+    const uint32_t batch = q.rank == 3 ? q.dims[0] : 1;
+    const uint32_t heads = q.dims[q.rank - 2], head = q.dims[q.rank - 1];
+    expect_float("key_cache", key_cache);
+    expect_dtype("value_cache", value_cache, key_cache.dtype);
+    const int cr = q.rank == 3 ? 4 : 3;
+    expect_rank("key_cache", key_cache, cr);
+    expect_rank("value_cache", value_cache, cr);
+    for (int a = 0; a < cr; a++)
+        if (value_cache.dims[a] != key_cache.dims[a])
+            invalid("parameter `value_cache`: dims must match key_cache " + shape_str(key_cache));
+    const int o = cr - 3;
+    if (cr == 4 && key_cache.dims[0] < batch) expect_dim("key_cache", key_cache, 0, "batch", batch);
+    const uint32_t seq = key_cache.dims[o], kv_heads = key_cache.dims[o + 1];
+    expect_dim("key_cache", key_cache, o + 2, "head", head);
+    expect_float("out", out);
+    if (numel(out) != (uint64_t)batch * heads * head)
+        invalid("parameter `out`: expected " + std::to_string((uint64_t)batch * heads * head) +
+                " elements ([batch, heads * head]), got " + shape_str(out));
+    expect_step(step, batch);
+    if (!attention_fusable(heads, kv_heads, head, key_cache.dtype))
+        invalid("attention: needs query_heads / kv_heads in {1, 2, 4, 8} and head * element "
+                "size a multiple of 16 bytes, head <= 128");
+    AttnParams p = {};
+    p.q = (const float*)q.data;
+    p.kcache = key_cache.data;
+    p.vcache = value_cache.data;
+    p.kv_dtype = key_cache.dtype;
+    p.cache_stride = (uint64_t)seq * kv_heads * head;
+    p.out = out.data;
+    p.out_dtype = out.dtype;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.head = head;
+    p.seq = seq;
+    p.batch = batch;
+    p.nsplit = attention_choose_splits(batch, kv_heads, seq, sms, 256);
+    // a (batch, kv head) group per SM or more: short contexts are not split
+    p.min_chunk = (uint64_t)batch * kv_heads >= (uint64_t)sms ? 256u : 0u;
+    p.step = (const Step*)step.data;
+    return p;
+}
+
+extern "C" int ab_kernel_attention_decode(ab_scheme* s, ab_tensor q, ab_tensor key_cache,
+                                          ab_tensor value_cache, ab_tensor out, ab_tensor step) {
+    return guard([&] {
+        if (!s) fail(AB_ERR_ARGUMENT, "null scheme");
+        if (!s->rt) fail(AB_ERR_ARGUMENT, "attention_decode: the scheme needs a runtime (it "
+                                          "allocates the split scratch)");
+        AttnParams p = attention_decode_operands(q, key_cache, value_cache, out, step,
+                                                 s->rt->sm_count);
+        uint64_t floats = 0, tickets = 0;
+        attention_scratch_size(p.batch, p.heads, p.head, p.nsplit, &floats, &tickets);
+        tickets = (uint64_t)p.batch * p.kv_heads;
+        s->rt->activate();
+        void* part = nullptr;
+        void* counters = nullptr;
+        cuda_check(cudaMalloc(&part, std::max<uint64_t>(floats, 1) * 4), "cudaMalloc");
+        if (cudaMalloc(&counters, tickets * 4) != cudaSuccess ||
+            cudaMemset(counters, 0, tickets * 4) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(part);
+            if (counters) cudaFree(counters);
+            fail(AB_ERR_CUDA, "attention_decode: scratch allocation failed");
+        }
+        s->owned.push_back(part);
+        s->owned.push_back(counters);
+        p.part_o = (float*)part;
+        p.part_ml = (float*)part + (uint64_t)p.batch * p.heads * p.nsplit * p.head;
+        p.counters = (uint32_t*)counters;
+        p.flags = s->rt->flags;
+        record_attention(s, "attn_decode", p);
+    });
+}
+
 extern "C" int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor key_cache,
                                            ab_tensor value_cache, ab_tensor out, ab_tensor step) {
     return guard([&] {
-        expect_data("q", q);
-        expect_data("key_cache", key_cache);
-        expect_data("value_cache", value_cache);
-        expect_data("out", out);
-        expect_dtype("q", q, AB_F32);
-        expect_rank_in("q", q, 2, 3);
-        const uint32_t batch = q.rank == 3 ? q.dims[0] : 1;
-        const uint32_t heads = q.dims[q.rank - 2], head = q.dims[q.rank - 1];
-        expect_float("key_cache", key_cache);
-        expect_dtype("value_cache", value_cache, key_cache.dtype);
-        const int cr = q.rank == 3 ? 4 : 3;
-        expect_rank("key_cache", key_cache, cr);
-        expect_rank("value_cache", value_cache, cr);
-        for (int a = 0; a < cr; a++)
-            if (value_cache.dims[a] != key_cache.dims[a])
-                invalid("parameter `value_cache`: dims must match key_cache " + shape_str(key_cache));
-        const int o = cr - 3;
-        if (cr == 4 && key_cache.dims[0] < batch)
-            expect_dim("key_cache", key_cache, 0, "batch", batch);
-        const uint32_t seq = key_cache.dims[o], kv_heads = key_cache.dims[o + 1];
-        expect_dim("key_cache", key_cache, o + 2, "head", head);
-        expect_float("out", out);
-        if (numel(out) != (uint64_t)batch * heads * head)
-            invalid("parameter `out`: expected " + std::to_string((uint64_t)batch * heads * head) +
-                    " elements ([batch, heads * head]), got " + shape_str(out));
-        expect_step(step, batch);
-        if (!attention_fusable(heads, kv_heads, head, key_cache.dtype))
-            invalid("attention: needs query_heads / kv_heads in {1, 2, 4, 8} and head * element "
-                    "size a multiple of 16 bytes, head <= 128");
+        int device = 0;
+        cuda_check(cudaGetDevice(&device), "query device");
+        int sms = 148;
+        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device),
+                   "query SM count");
+        AttnParams p = attention_decode_operands(q, key_cache, value_cache, out, step, sms);
 
         // this entry launches directly: refuse anything that is not device memory first
         for (const ab_tensor* t : {&q, &key_cache, &value_cache, &out, &step}) {
@@ -998,41 +1075,20 @@ extern "C" int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor 
                                       "device memory");
             }
         }
-        int device = 0;
         unsigned char* base = noalloc_scratch(&device);
-        int sms = 148;
-        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device),
-                   "query SM count");
-        const uint32_t nsplit = attention_choose_splits(batch, kv_heads, seq, sms, 256);
         uint64_t floats = 0, tickets = 0;
-        attention_scratch_size(batch, heads, head, nsplit, &floats, &tickets);
-        tickets = (uint64_t)batch * kv_heads;
+        attention_scratch_size(p.batch, p.heads, p.head, p.nsplit, &floats, &tickets);
+        tickets = (uint64_t)p.batch * p.kv_heads;
         if (floats > kNoAllocFloats || tickets > kNoAllocTickets)
             fail(AB_ERR_ARGUMENT,
                  "ab_attention_decode_noalloc: this shape needs " + std::to_string(floats * 4) +
                      " bytes of split partials and " + std::to_string(tickets) +
                      " tickets; the static scratch holds " + std::to_string(kNoAllocFloats * 4) +
                      " bytes and " + std::to_string(kNoAllocTickets) + " tickets");
-
-        AttnParams p = {};
-        p.q = (const float*)q.data;
-        p.kcache = key_cache.data;
-        p.vcache = value_cache.data;
-        p.kv_dtype = key_cache.dtype;
-        p.cache_stride = (uint64_t)seq * kv_heads * head;
-        p.out = out.data;
-        p.out_dtype = out.dtype;
-        p.heads = heads;
-        p.kv_heads = kv_heads;
-        p.head = head;
-        p.seq = seq;
-        p.batch = batch;
-        p.nsplit = nsplit;
         p.part_o = (float*)base;
-        p.part_ml = (float*)base + (uint64_t)batch * heads * nsplit * head;
+        p.part_ml = (float*)base + (uint64_t)p.batch * p.heads * p.nsplit * p.head;
         p.counters = (uint32_t*)(base + kNoAllocFloats * 4);
         p.flags = (uint32_t*)(base + kNoAllocFloats * 4 + (uint64_t)kNoAllocTickets * 4);
-        p.step = (const Step*)step.data;
 
         cudaStream_t st = (cudaStream_t)stream;
         // tickets must start at zero; the kernel resets them, but a failed earlier call

@@ -122,6 +122,9 @@ struct Scheme {
     bool use_graph = true;
     uint32_t records = 0;
     uint32_t replays = 0;
+    // device buffers that recorded nodes use and the scheme frees when it is destroyed
+    // (kernel entry points that need scratch of their own, e.g. ab_kernel_attention_decode)
+    std::vector<void*> owned;
     void add(const char* label, LaunchFn fn) {
         nodes.push_back(Node{label, std::move(fn)});
         dirty = true;

@@ -33,11 +33,17 @@ __global__ void embed_kernel(const TT* __restrict__ table, uint32_t vocab, uint3
     const TT* src = table + (uint64_t)token * dim;
     constexpr int V = 16 / sizeof(TT);
     if (vec) {
+        // 16-byte row vectors in, 16-byte vectors out (two for a bf16 -> f32 gather)
         for (uint32_t v = tid; v < dim / V; v += stride) {
-            uint4 raw = *reinterpret_cast<const uint4*>(src + (uint64_t)v * V);
-            const TT* e = reinterpret_cast<const TT*>(&raw);
-#pragma unroll
-            for (int j = 0; j < V; j++) dst[(uint64_t)v * V + j] = from_f32<XT>(to_f32(e[j]));
+            const uint4 raw = *reinterpret_cast<const uint4*>(src + (uint64_t)v * V);
+            if constexpr (sizeof(TT) == sizeof(XT)) {
+                *reinterpret_cast<uint4*>(dst + (uint64_t)v * V) = raw;
+            } else {
+                const TT* e = reinterpret_cast<const TT*>(&raw);
+                float4* d4 = reinterpret_cast<float4*>(dst + (uint64_t)v * V);
+                d4[0] = make_float4(to_f32(e[0]), to_f32(e[1]), to_f32(e[2]), to_f32(e[3]));
+                d4[1] = make_float4(to_f32(e[4]), to_f32(e[5]), to_f32(e[6]), to_f32(e[7]));
+            }
         }
     } else {
         for (uint32_t i = tid; i < dim; i += stride) dst[i] = from_f32<XT>(to_f32(src[i]));
@@ -64,19 +70,64 @@ __global__ void gemv_serial_kernel(const float* __restrict__ x, uint32_t n,
 }
 
 // ---- rmsnorm: src/kernels.rs:75-128 ----------------------------------------------------
-// One 256-thread block per row: strided partials per lane, a halving tree in shared
-// memory, then o = w * (ss * x) with ss = 1 / sqrt(mean + eps).
-template <typename WT, typename OT>
+// One 256-thread block per row: strided partials per lane (thread t sums elements t,
+// t + 256, ... in order), a halving tree in shared memory, then o = w * (ss * x) with
+// ss = 1 / sqrt(mean + eps). STAGED rows are first copied into shared memory with 16-byte
+// loads (which also makes the in-place form safe), and outputs go out 8 at a time; the
+// arithmetic and its order are the same in both forms.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* v) {
+    if constexpr (sizeof(T) == 2) {
+        const uint4 r = *reinterpret_cast<const uint4*>(p);
+        v[0] = bf16lo(r.x); v[1] = bf16hi(r.x); v[2] = bf16lo(r.y); v[3] = bf16hi(r.y);
+        v[4] = bf16lo(r.z); v[5] = bf16hi(r.z); v[6] = bf16lo(r.w); v[7] = bf16hi(r.w);
+    } else {
+        const float4 a = reinterpret_cast<const float4*>(p)[0];
+        const float4 b = reinterpret_cast<const float4*>(p)[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* v) {
+    if constexpr (sizeof(T) == 2) {
+        uint4 r;
+        __nv_bfloat162 h;
+        h = __floats2bfloat162_rn(v[0], v[1]); r.x = *reinterpret_cast<uint32_t*>(&h);
+        h = __floats2bfloat162_rn(v[2], v[3]); r.y = *reinterpret_cast<uint32_t*>(&h);
+        h = __floats2bfloat162_rn(v[4], v[5]); r.z = *reinterpret_cast<uint32_t*>(&h);
+        h = __floats2bfloat162_rn(v[6], v[7]); r.w = *reinterpret_cast<uint32_t*>(&h);
+        *reinterpret_cast<uint4*>(p) = r;
+    } else {
+        reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+template <typename XT, typename WT, typename OT, bool STAGED>
 __global__ void __launch_bounds__(256)
-    rmsnorm_ref_kernel(const float* __restrict__ x, const WT* __restrict__ w, OT* o, uint32_t size,
-                       float eps) {
+    rmsnorm_ref_kernel(const XT* x, const WT* __restrict__ w, OT* o, uint32_t size, float eps) {
     pdl_wait();
     __shared__ float lanes[256];
+    extern __shared__ float xs[];  // STAGED: the row as f32
     const uint32_t t = threadIdx.x;
-    const float* xr = x + (uint64_t)blockIdx.x * size;
+    const XT* xr = x + (uint64_t)blockIdx.x * size;
     OT* orow = o + (uint64_t)blockIdx.x * size;
+    if (STAGED) {
+        for (uint32_t v = t; v < size / 8; v += 256) {
+            float r[8];
+            load8(xr + (uint64_t)v * 8, r);
+            float4* d = reinterpret_cast<float4*>(xs + v * 8);
+            d[0] = make_float4(r[0], r[1], r[2], r[3]);
+            d[1] = make_float4(r[4], r[5], r[6], r[7]);
+        }
+        __syncthreads();
+    }
     float ss = 0.0f;
-    for (uint32_t j = t; j < size; j += 256) ss = __fadd_rn(ss, __fmul_rn(xr[j], xr[j]));
+    for (uint32_t j = t; j < size; j += 256) {
+        const float v = STAGED ? xs[j] : to_f32(xr[j]);
+        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
     lanes[t] = ss;
     __syncthreads();
     for (uint32_t s = 128; s > 0; s >>= 1) {
@@ -84,8 +135,21 @@ __global__ void __launch_bounds__(256)
         __syncthreads();
     }
     float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lanes[0], (float)size), eps)));
-    for (uint32_t j = t; j < size; j += 256)
-        orow[j] = from_f32<OT>(__fmul_rn(to_f32(w[j]), __fmul_rn(scale, xr[j])));
+    if (STAGED) {
+        for (uint32_t v = t; v < size / 8; v += 256) {
+            float wv[8], ov[8];
+            load8(w + (uint64_t)v * 8, wv);
+            const float4 xa = reinterpret_cast<const float4*>(xs + v * 8)[0];
+            const float4 xb = reinterpret_cast<const float4*>(xs + v * 8)[1];
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+            for (int k = 0; k < 8; k++) ov[k] = __fmul_rn(wv[k], __fmul_rn(scale, xv[k]));
+            store8(orow + (uint64_t)v * 8, ov);
+        }
+    } else {
+        for (uint32_t j = t; j < size; j += 256)
+            orow[j] = from_f32<OT>(__fmul_rn(to_f32(w[j]), __fmul_rn(scale, to_f32(xr[j]))));
+    }
     pdl_trigger();
 }
 
@@ -95,24 +159,69 @@ __device__ __forceinline__ void rotate(float a, float b, float c, float s, float
     *r1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
 }
 
-__global__ void rope_ref_kernel(float* q, uint32_t q_len, uint32_t head, float* k, uint32_t kv_dim,
-                                uint32_t seq, const Step* __restrict__ step, float theta,
-                                uint32_t* flags) {
+// One block per q row b (one token): row b rotates at step[b].position, and so does row
+// step[b].position of k (the row's own cache at k + b * k_stride, or one shared cache with
+// k_stride 0). A thread keeps one pair index j across heads when head / 2 divides 256, so
+// cos/sin are evaluated once per (row, j) instead of once per element pair.
+__global__ void __launch_bounds__(256)
+    rope_rows_kernel(float* q, uint32_t q_len, uint32_t head, float* k, uint32_t kv_dim,
+                     uint64_t k_stride, uint32_t seq, const Step* __restrict__ step, float theta,
+                     uint32_t* flags) {
     pdl_wait();
-    uint32_t i = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
-    if (i >= q_len) return;
-    uint32_t pos = step[0].position;
+    const uint32_t b = blockIdx.x;
+    const uint32_t pos = step[b].position;
     if (pos >= seq) {
-        if (i == 0) atomicOr(flags, kFlagPositionRange);
+        if (threadIdx.x == 0) atomicOr(flags, kFlagPositionRange);
         return;
     }
-    float c, s;
-    rope_cos_sin(i, head, pos, theta, &c, &s);
-    rotate(q[i], q[i + 1], c, s, &q[i], &q[i + 1]);
-    if (i < kv_dim) {
-        float* kr = k + (uint64_t)pos * kv_dim;
-        rotate(kr[i], kr[i + 1], c, s, &kr[i], &kr[i + 1]);
+    float* qr = q + (uint64_t)b * q_len;
+    float* kr = k + (uint64_t)b * k_stride + (uint64_t)pos * kv_dim;
+    if (q_len % 4 == 0 && kv_dim % 4 == 0 && ((uintptr_t)qr | (uintptr_t)kr) % 16 == 0) {
+        // two pairs per thread through 16-byte accesses
+        uint32_t last0 = 0xFFFFFFFFu, last1 = 0xFFFFFFFFu;
+        float c0 = 1.0f, s0 = 0.0f, c1 = 1.0f, s1 = 0.0f;
+        for (uint32_t i = threadIdx.x * 4; i < q_len; i += 1024) {
+            const uint32_t j0 = i % head, j1 = (i + 2) % head;
+            if (j0 != last0) {
+                rope_cos_sin(j0, head, pos, theta, &c0, &s0);
+                last0 = j0;
+            }
+            if (j1 != last1) {
+                rope_cos_sin(j1, head, pos, theta, &c1, &s1);
+                last1 = j1;
+            }
+            float4 v = *reinterpret_cast<float4*>(qr + i);
+            rotate(v.x, v.y, c0, s0, &v.x, &v.y);
+            rotate(v.z, v.w, c1, s1, &v.z, &v.w);
+            *reinterpret_cast<float4*>(qr + i) = v;
+            if (i < kv_dim) {
+                float4 u = *reinterpret_cast<float4*>(kr + i);
+                rotate(u.x, u.y, c0, s0, &u.x, &u.y);
+                rotate(u.z, u.w, c1, s1, &u.z, &u.w);
+                *reinterpret_cast<float4*>(kr + i) = u;
+            }
+        }
+        pdl_trigger();
+        return;
     }
+    uint32_t last = 0xFFFFFFFFu;
+    float c = 1.0f, s = 0.0f;
+    for (uint32_t i = threadIdx.x * 2; i < q_len; i += 512) {
+        const uint32_t j = i % head;
+        if (j != last) {
+            rope_cos_sin(j, head, pos, theta, &c, &s);
+            last = j;
+        }
+        float2 v = *reinterpret_cast<float2*>(qr + i);
+        rotate(v.x, v.y, c, s, &v.x, &v.y);
+        *reinterpret_cast<float2*>(qr + i) = v;
+        if (i < kv_dim) {
+            float2 u = *reinterpret_cast<float2*>(kr + i);
+            rotate(u.x, u.y, c, s, &u.x, &u.y);
+            *reinterpret_cast<float2*>(kr + i) = u;
+        }
+    }
+    pdl_trigger();
 }
 
 __global__ void rope_store_ref_kernel(float* q, uint32_t q_len, uint32_t head,
@@ -366,7 +475,8 @@ void record_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x) {
     if (table.dtype == AB_F32 && x.dtype == AB_BF16)
         invalid("parameter `x`: an f32 table gathers into an f32 x");
     const size_t esz = dtype_size(table.dtype);
-    const int vec = (dim % (16 / esz) == 0) && ((uintptr_t)table.data % 16 == 0);
+    const int vec = (dim % (16 / esz) == 0) && ((uintptr_t)table.data % 16 == 0) &&
+                    ((uintptr_t)x.data % 16 == 0);
     uint32_t* flags = flags_of(s);
     const Step* st = (const Step*)step.data;
     const unsigned chunks = std::max(1u, std::min(64u, (dim / (unsigned)(16 / esz) + 255) / 256));
@@ -400,7 +510,7 @@ void record_rmsnorm_ref(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor o
     expect_data("x", x);
     expect_data("weight", weight);
     expect_data("o", o);
-    expect_dtype("x", x, AB_F32);
+    expect_float("x", x);
     expect_float("weight", weight);
     expect_float("o", o);
     expect_rank_in("x", x, 1, 2);
@@ -410,22 +520,45 @@ void record_rmsnorm_ref(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor o
     expect_dim("weight", weight, 0, "dim", dim);
     if (numel(o) != numel(x))
         invalid("parameter `o`: dim `dim` must match x " + shape_str(x) + ", got " + shape_str(o));
-    if (o.data == x.data && o.dtype != AB_F32) invalid("parameter `o`: in-place norm is f32");
-    const float* xp = (const float*)x.data;
-    auto go = [&](auto wtag, auto otag) {
+    if (o.data == x.data && o.dtype != x.dtype)
+        invalid("parameter `o`: an in-place norm keeps x's dtype");
+    auto go = [&](auto xtag, auto wtag, auto otag) {
+        using X = decltype(xtag);
         using W = decltype(wtag);
         using O = decltype(otag);
+        const X* xp = (const X*)x.data;
         const W* wp = (const W*)weight.data;
         O* op = (O*)o.data;
-        s->add("rmsnorm", [=](cudaStream_t st) {
-            return launch(st, dim3(rows), dim3(256), 0, true, rmsnorm_ref_kernel<W, O>, xp, wp, op,
-                          dim, eps);
-        });
+        // rows of 8-element vectors on 16-byte boundaries are staged in shared memory
+        const bool staged = dim % 8 == 0 && (size_t)dim * 4 <= 160 * 1024 &&
+                            (uintptr_t)xp % 16 == 0 && (uintptr_t)wp % 16 == 0 &&
+                            (uintptr_t)op % 16 == 0;
+        if (staged) {
+            auto kern = rmsnorm_ref_kernel<X, W, O, true>;
+            const size_t smem = (size_t)dim * 4;
+            s->add("rmsnorm", [=](cudaStream_t st) {
+                if (smem > 48 * 1024) {
+                    cudaError_t e = cudaFuncSetAttribute(
+                        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                    if (e != cudaSuccess) return e;
+                }
+                return launch(st, dim3(rows), dim3(256), smem, true, kern, xp, wp, op, dim, eps);
+            });
+        } else {
+            s->add("rmsnorm", [=](cudaStream_t st) {
+                return launch(st, dim3(rows), dim3(256), 0, true,
+                              rmsnorm_ref_kernel<X, W, O, false>, xp, wp, op, dim, eps);
+            });
+        }
     };
-    if (weight.dtype == AB_F32 && o.dtype == AB_F32) go(float(), float());
-    else if (weight.dtype == AB_F32) go(float(), bf16());
-    else if (o.dtype == AB_F32) go(bf16(), float());
-    else go(bf16(), bf16());
+    auto by_w_o = [&](auto xtag) {
+        if (weight.dtype == AB_F32 && o.dtype == AB_F32) go(xtag, float(), float());
+        else if (weight.dtype == AB_F32) go(xtag, float(), bf16());
+        else if (o.dtype == AB_F32) go(xtag, bf16(), float());
+        else go(xtag, bf16(), bf16());
+    };
+    if (x.dtype == AB_F32) by_w_o(float());
+    else by_w_o(bf16());
 }
 
 }  // namespace ab
@@ -497,17 +630,30 @@ static void check_rope_shapes(ab_tensor q, ab_tensor k, const char* kname) {
 int ab_kernel_rope(ab_scheme* s, ab_tensor q, ab_tensor k, ab_tensor step, float theta) {
     return guard([&] {
         if (!s) fail(AB_ERR_ARGUMENT, "null scheme");
-        check_rope_shapes(q, k, "k");
-        expect_step(step, 1);
-        const uint32_t q_len = (uint32_t)numel(q), head = q.dims[1];
-        const uint32_t kv_dim = k.dims[1] * k.dims[2], seq = k.dims[0];
+        // q [heads, head] (one token) or [batch, heads, head] (one DecodeStep per row); k
+        // [seq, kv_heads, head] shared by the rows or [>= batch, seq, kv_heads, head]
+        expect_data("q", q);
+        expect_data("k", k);
+        expect_rank_in("q", q, 2, 3);
+        expect_rank_in("k", k, 3, 4);
+        expect_dtype("q", q, AB_F32);
+        expect_dtype("k", k, AB_F32);
+        const uint32_t batch = q.rank == 3 ? q.dims[0] : 1;
+        const uint32_t head = q.dims[q.rank - 1];
+        const int o = k.rank - 3;
+        expect_dim("k", k, o + 2, "head", head);
+        if (head % 2) invalid("parameter `q`: dim `head` must be even");
+        if (k.rank == 4 && k.dims[0] < batch) expect_dim("k", k, 0, "batch", batch);
+        expect_step(step, batch);
+        const uint32_t q_len = (uint32_t)(numel(q) / batch);
+        const uint32_t kv_dim = k.dims[o + 1] * k.dims[o + 2], seq = k.dims[o];
+        const uint64_t k_stride = k.rank == 4 ? (uint64_t)seq * kv_dim : 0;
         float *qp = (float*)q.data, *kp = (float*)k.data;
         const Step* st = (const Step*)step.data;
         uint32_t* flags = flags_of(s);
-        const unsigned grid = (q_len / 2 + 255) / 256;
         s->add("rope", [=](cudaStream_t stream) {
-            return launch(stream, dim3(std::max(1u, grid)), dim3(256), 0, true, rope_ref_kernel, qp,
-                          q_len, head, kp, kv_dim, seq, st, theta, flags);
+            return launch(stream, dim3(batch), dim3(256), 0, true, rope_rows_kernel, qp, q_len,
+                          head, kp, kv_dim, k_stride, seq, st, theta, flags);
         });
     });
 }

@@ -417,6 +417,7 @@ int ab_scheme_destroy(ab_scheme* s) {
             cudaStreamSynchronize(s->rt->stream);
         }
         s->release_graph();
+        for (void* b : s->owned) cudaFree(b);
         delete s;
     });
 }

@@ -105,6 +105,17 @@ class AttentionCombineKernel(_Kernel):
         return self._rec(scheme, partial, xb, step)
 
 
+class AttentionDecodeKernel(_Kernel):
+    """The fused flash-decoding replacement of AttentionPartialKernel + AttentionCombineKernel
+    (src/kernels.rs:228-410): one recorded kernel, split scratch owned by the scheme. q is
+    [heads, head] or [batch, heads, head]; the caches gain a leading batch dim with it."""
+
+    fn = "ab_kernel_attention_decode"
+
+    def record(self, scheme, label, q, key_cache, value_cache, out, step):
+        return self._rec(scheme, q, key_cache, value_cache, out, step)
+
+
 class AttentionKernel(_Kernel):
     fn = "ab_kernel_attention"
 

@@ -52,6 +52,15 @@ WORKLOADS = {
                            batch=1, title="Tiny llama2.c fp32 decode"),
 }
 
+# Kernel microbenchmarks (one JSON line each, GB/s against the measured HBM peak)
+MICRO = {
+    "ops": "Per-op microbench: RmsNorm rows {1,64,4096} x dim {4096,8192}, RoPE 32x128 at "
+           "positions 0-8191 (theta 500000), SwiGLU rows {1,64} x 14336, embedding gather "
+           "from 128256 x 4096; N(0,1) activations in f32 and bf16",
+    "attention": "Split attention decode: 32 query / 8 kv heads, head_dim 128, bf16 K/V, fp32 "
+                 "accumulation; context {4096,32768,131072} x batch {1,8,64}; N(0,1) seed 2",
+}
+
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -219,6 +228,225 @@ def cpu_sample(w, batch, positions, threads):
     return per_token, batch
 
 
+# ----------------------------------------------------------------------------- microbenchmarks
+class LaunchTimer:
+    """Median device time of a recorded scheme: each timed replay follows a write of a
+    buffer larger than L2 (so every launch reads from HBM), CUDA events on the runtime's
+    stream around the replay alone."""
+
+    def __init__(self, rt, flush_bytes=512 << 20):
+        import torch
+
+        self.rt = rt
+        self.torch = torch
+        self.ext = torch.cuda.ExternalStream(rt.stream)
+        self.flush = torch.empty(flush_bytes // 4, dtype=torch.float32, device="cuda")
+
+    def __call__(self, sch, iters, warmup=3):
+        torch = self.torch
+        for _ in range(warmup):
+            sch.submit()
+        pairs = []
+        for _ in range(iters):
+            with torch.cuda.stream(self.ext):
+                self.flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(self.ext)
+            sch.submit()
+            e1.record(self.ext)
+            pairs.append((e0, e1))
+        self.rt.synchronize()
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in pairs)
+
+
+def _micro_line(kind, cases, peak, peak_kind, clocks, cpu, extra=None):
+    # the HBM-scale cases (above 64 MB moved) summarise the line; small ones are latency
+    big = [c for c in cases if c["bytes"] >= (64 << 20)] or cases
+    agg = sum(c["bytes"] for c in big) / sum(c["us"] for c in big) / 1e3
+    top = max(cases, key=lambda c: c["bytes"])
+    line = {
+        "metric": f"per-kernel HBM GB/s vs peak ({kind} microbench)", "value": agg,
+        "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32+bf16" if kind == "ops" else "bf16",
+        "data": "synthetic", "config": {"workload": MICRO[kind],
+                                        "l2": "L2 flushed (512 MB write) before every launch"},
+        "roofline": {"kernel": top["op"], "bound": "hbm", "achieved": top["gbs"], "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": top["gbs"] / peak,
+                     "bytes_per_launch": top["bytes"], "launch_ms": top["us"] / 1e3,
+                     "traffic": None},
+        "cases": cases, "clocks": clocks, "gpu_launches": len(cases),
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    if extra:
+        line.update(extra)
+    return line
+
+
+def run_ops_micro(args):
+    import numpy as np
+    import torch
+
+    import ammon_b200 as ab
+    from ammon_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    rt = ab.create_runtime(0)
+    timer = LaunchTimer(rt)
+    peak, peak_kind = load_peaks()
+    cases = []
+
+    def add(op, dtype, shape, nbytes, sch, iters=20):
+        us = timer(sch, iters) * 1e3
+        cases.append({"op": op, "dtype": dtype, "shape": shape, "bytes": nbytes,
+                      "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
+                      "frac": round(nbytes / us / 1e3 / peak, 4)})
+
+    with ClockSampler(0) as clocks:
+        for dt, esz in ((ab.F32, 4), (ab.BF16, 2)):
+            name = "f32" if dt == ab.F32 else "bf16"
+            for dim in (4096, 8192):
+                w = ab.Tensor.zeros(rt, (dim,), dt).fill_normal(7, 1, 1.0, 0.01)
+                for rows in (1, 64, 4096):
+                    x = ab.Tensor.zeros(rt, (rows, dim), dt).fill_normal(7, 2)
+                    o = ab.Tensor.zeros(rt, (rows, dim), dt)
+                    s = rt.scheme()
+                    K.RmsnormKernel.prepare(rt).record(s, "rmsnorm", x, w, o)
+                    add("rmsnorm", name, [rows, dim], rows * dim * 2 * esz + dim * esz, s)
+                    s.close()
+            for rows in (1, 64):
+                hb = ab.Tensor.zeros(rt, (rows, 14336), dt).fill_normal(7, 3)
+                hb2 = ab.Tensor.zeros(rt, (rows, 14336), dt).fill_normal(7, 4)
+                s = rt.scheme()
+                K.SwigluKernel.prepare(rt).record(s, "swiglu", hb, hb2)
+                add("swiglu", name, [rows, 14336], rows * 14336 * 3 * esz, s)
+                s.close()
+            table = ab.Tensor.zeros(rt, (128256, 4096), dt).fill_normal(7, 5)
+            for n in (1, 64, 4096):
+                from oracle import oracle as orc
+
+                ids = orc.uniform_tokens(n, 7, 6, 0, 128256).tolist()
+                st = ab.DecodeStep.parcel(rt, n)
+                rt.deposit(st, [ab.DecodeStep(int(t), 0) for t in ids])
+                x = ab.Tensor.zeros(rt, (n, 4096), dt)
+                s = rt.scheme()
+                ab.Embedding(rt).record(s, table, st, x)
+                add("embed", name, [n, 4096], n * 4096 * 2 * esz, s)
+                s.close()
+                if n == 4096:
+                    got = x.read_f32() if dt == ab.BF16 else x.read()
+                    row = table.narrow(0, ids[-1], 1)
+                    want = row.read_f32() if dt == ab.BF16 else row.read()
+                    assert np.array_equal(got[-1], want.ravel()), "embed spot check"
+            table.free()
+        # RoPE: 8192 rows (one per position 0..8191) of q [32, 128] and the shared k cache
+        q = ab.Tensor.zeros(rt, (8192, 32, 128)).fill_normal(7, 7)
+        k = ab.Tensor.zeros(rt, (8192, 8, 128)).fill_normal(7, 8)
+        st = ab.DecodeStep.parcel(rt, 8192)
+        rt.deposit(st, [ab.DecodeStep(0, p) for p in range(8192)])
+        s = rt.scheme()
+        K.RopeKernel.prepare(rt).record(s, "rope", q, k, st, 500000.0)
+        add("rope", "f32", [8192, 32, 128], 8192 * (4096 + 1024) * 4 * 2, s)
+        s.close()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as orc
+
+        rows, dim = 64, 4096
+        xh = orc.normal(rows * dim, 7, 2, 0.0, 1.0).reshape(rows, dim)
+        wh = orc.normal(dim, 7, 1, 1.0, 0.01)
+        t0 = time.perf_counter()
+        reps = 50
+        for _ in range(reps):
+            for r in range(rows):
+                orc.rmsnorm(xh[r], wh)
+        dt_s = (time.perf_counter() - t0) / reps
+        cpu = {"value": (rows * dim * 8 + dim * 4) / dt_s / 1e9, "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": "oracle rmsnorm, 64 rows x 4096 f32, 50 repetitions"}
+    line = _micro_line("ops", cases, peak, peak_kind, clocks.summary(), cpu)
+    print(json.dumps(line), flush=True)
+    rt.close()
+
+
+def run_attention_micro(args):
+    import numpy as np
+    import torch
+
+    import ammon_b200 as ab
+    from ammon_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    rt = ab.create_runtime(0)
+    timer = LaunchTimer(rt)
+    peak, peak_kind = load_peaks()
+    H, KV, hd = 32, 8, 128
+    ctxs = [int(c) for c in args.contexts.split(",")]
+    batches = [int(b) for b in args.batches.split(",")]
+    rows_max = max(batches) * max(ctxs) * KV
+    # one K and one V buffer of [rows, 128] bf16 rows serve every case as [B, ctx, 8, 128]
+    kbuf = ab.Tensor.zeros(rt, (rows_max, hd), ab.BF16).fill_normal(2, 2)
+    vbuf = ab.Tensor.zeros(rt, (rows_max, hd), ab.BF16).fill_normal(2, 3)
+    cases = []
+    worst = 0.0
+    with ClockSampler(0) as clocks:
+        for ctx in ctxs:
+            for B in batches:
+                kc = kbuf.narrow(0, 0, B * ctx * KV).reshape((B, ctx, KV, hd))
+                vc = vbuf.narrow(0, 0, B * ctx * KV).reshape((B, ctx, KV, hd))
+                q = ab.Tensor.zeros(rt, (B, H, hd)).fill_normal(2, 1)
+                out = ab.Tensor.zeros(rt, (B, H * hd))
+                st = ab.DecodeStep.parcel(rt, B)
+                rt.deposit(st, [ab.DecodeStep(0, ctx - 1)] * B)
+                s = rt.scheme()
+                K.AttentionDecodeKernel.prepare(rt).record(s, "attn_decode", q, kc, vc, out, st)
+                nbytes = B * KV * ctx * hd * 2 * 2 + B * H * hd * 4 * 2
+                iters = 5 if nbytes > (8 << 30) else 20
+                us = timer(s, iters) * 1e3
+                # spot check: the last row's first kv group against float64
+                b = B - 1
+                kr = kbuf.narrow(0, b * ctx * KV, ctx * KV).read_f32().reshape(ctx, KV, hd)
+                vr = vbuf.narrow(0, b * ctx * KV, ctx * KV).read_f32().reshape(ctx, KV, hd)
+                qh = q.read()[b]
+                got = out.read()[b].reshape(H, hd)
+                g = H // KV
+                for h in range(g):
+                    sc = kr[:, 0].astype(np.float64) @ qh[h].astype(np.float64) / np.sqrt(hd)
+                    p = np.exp(sc - sc.max())
+                    want = (p / p.sum()) @ vr[:, 0].astype(np.float64)
+                    worst = max(worst, float(np.abs(got[h] - want).max() /
+                                             max(np.abs(want).max(), 1e-30)))
+                cases.append({"op": "attn_decode", "dtype": "bf16", "shape": [B, ctx],
+                              "bytes": nbytes, "us": round(us, 3),
+                              "gbs": round(nbytes / us / 1e3, 1),
+                              "frac": round(nbytes / us / 1e3 / peak, 4)})
+                s.close()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as orc
+
+        ctx = 4096
+        qh = orc.normal(H * hd, 2, 1, 0.0, 1.0).reshape(H, hd)
+        kh = orc.round_bf16(orc.normal(ctx * KV * hd, 2, 2, 0.0, 1.0)).reshape(ctx, KV, hd)
+        vh = orc.round_bf16(orc.normal(ctx * KV * hd, 2, 3, 0.0, 1.0)).reshape(ctx, KV, hd)
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            orc.attention(qh, kh, vh, ctx, ctx - 1)
+        dt_s = (time.perf_counter() - t0) / reps
+        cpu = {"value": KV * ctx * hd * 2 * 2 / dt_s / 1e9, "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": "oracle serial attention (the reference's "
+                                         "attention kernel), batch 1 x ctx 4096, bf16-rounded K/V "
+                                         "counted at 2 bytes per element"}
+    line = _micro_line("attention", cases, peak, peak_kind, clocks.summary(), cpu,
+                       {"parity": {"max_rel_err_vs_float64": worst, "tolerance": 1e-4}})
+    print(json.dumps(line), flush=True)
+    kbuf.free()
+    vbuf.free()
+    rt.close()
+
+
 def run_reference(args, w, rank, world):
     if rank != 0:
         return
@@ -251,7 +479,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS) +
+                    sorted(MICRO))
+    ap.add_argument("--contexts", default="4096,32768,131072", help="attention microbench")
+    ap.add_argument("--batches", default="1,8,64", help="attention microbench")
     ap.add_argument("--batch", type=int, default=0,
                     help="streams per rank (default: the workload's; the 110M workload's 256 "
                          "streams are split over the ranks)")
@@ -268,6 +499,15 @@ def main():
                     help="profiling aid: smaller KV cache (max context)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload in MICRO:
+        if int(os.environ.get("RANK", "0")) != 0:
+            return  # single-GPU kernel microbenchmarks: other ranks have nothing to do
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "kernel microbenchmarks "
+                              "report the oracle's CPU rate as cpu_baseline in the main arm"}))
+            return
+        (run_ops_micro if args.workload == "ops" else run_attention_micro)(args)
+        return
     w = dict(WORKLOADS[args.workload])
     if args.layers:
         w["layers"] = args.layers

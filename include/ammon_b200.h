@@ -127,10 +127,13 @@ int ab_scheme_node_label(const ab_scheme* s, uint32_t i, char* buf, uint32_t cap
 int ab_kernel_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x);
 /* gemv (src/kernels.rs:49-73): serial-order xout[pos, i] = sum_j w[i, j] x[j]. */
 int ab_kernel_gemv(ab_scheme* s, ab_tensor x, ab_tensor w, ab_tensor xout, ab_tensor step);
-/* rmsnorm / rmsnorm_inplace (src/kernels.rs:75-128): one row per block, eps 1e-5. */
+/* rmsnorm / rmsnorm_inplace (src/kernels.rs:75-128): one row per block, eps 1e-5. x is
+ * [dim] or [rows, dim], f32 or bf16; an in-place norm keeps x's dtype. */
 int ab_kernel_rmsnorm(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor o);
 int ab_kernel_rmsnorm_inplace(ab_scheme* s, ab_tensor x, ab_tensor weight);
-/* rope (src/kernels.rs:130-172): rotates q [heads, head] and row pos of k [seq, kv, head]. */
+/* rope (src/kernels.rs:130-172): rotates q [heads, head] and row pos of k [seq, kv, head].
+ * Batched form: q [batch, heads, head] with one DecodeStep per row; k is shared
+ * [seq, kv, head] or per row [>= batch, seq, kv, head]. */
 int ab_kernel_rope(ab_scheme* s, ab_tensor q, ab_tensor k, ab_tensor step, float theta);
 /* rope_store (src/kernels.rs:174-210). */
 int ab_kernel_rope_store(ab_scheme* s, ab_tensor q, ab_tensor k_proj, ab_tensor k,
@@ -142,6 +145,15 @@ int ab_kernel_cache_store(ab_scheme* s, ab_tensor src, ab_tensor dst, ab_tensor 
 int ab_kernel_attention_partial(ab_scheme* s, ab_tensor q, ab_tensor key_cache,
                                 ab_tensor value_cache, ab_tensor partial, ab_tensor step);
 int ab_kernel_attention_combine(ab_scheme* s, ab_tensor partial, ab_tensor xb, ab_tensor step);
+/* The fused replacement of attention_partial + attention_combine (src/kernels.rs:228-410):
+ * flash-decoding over positions [0, step.position] in one kernel (TMA-staged K/V tiles, GQA
+ * groups share their loads, the last split folds the partials). q f32 [heads, head] with
+ * caches [seq, kv_heads, head], or q [batch, heads, head] with caches [>= batch, seq,
+ * kv_heads, head] and one DecodeStep per row; out [batch, heads * head] f32 or bf16. Its
+ * split scratch is allocated here and owned by the scheme (freed by ab_scheme_destroy),
+ * so the scheme must have a runtime. */
+int ab_kernel_attention_decode(ab_scheme* s, ab_tensor q, ab_tensor key_cache,
+                               ab_tensor value_cache, ab_tensor out, ab_tensor step);
 /* attention (src/kernels.rs:412-460): serial scores into att [q_heads, seq]. */
 int ab_kernel_attention(ab_scheme* s, ab_tensor q, ab_tensor att, ab_tensor xb,
                         ab_tensor key_cache, ab_tensor value_cache, ab_tensor step);
