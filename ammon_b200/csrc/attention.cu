@@ -95,24 +95,6 @@ __host__ __device__ inline AttnLayout attn_layout(uint32_t head, uint32_t esz, u
     return L;
 }
 
-// TMA layout: kAttnStages x [K tile | V tile], each tile nbox boxes of [64 rows x SWZ
-// bytes] on a 1024-byte aligned base (the dynamic buffer carries 1 KB of slack).
-struct AttnTmaLayout {
-    uint32_t rowbytes, stage_bytes;
-    AttnTail t;
-    size_t total;
-};
-
-__host__ __device__ inline AttnTmaLayout attn_tma_layout(uint32_t head, uint32_t esz, uint32_t G,
-                                                         uint32_t nsplit) {
-    AttnTmaLayout L;
-    L.rowbytes = head * esz;
-    L.stage_bytes = 2u * kAttnTile * L.rowbytes;
-    L.t = attn_tail((size_t)kAttnStages * L.stage_bytes, head, G, nsplit);
-    L.total = L.t.end + 1024;
-    return L;
-}
-
 // Online-softmax update of one tile: scores sc[G][64] -> probabilities pt[64][PS],
 // running m/l and the rescale factor alpha per head. Warp w takes heads w, w + 4.
 template <int G>
@@ -230,15 +212,81 @@ __device__ __forceinline__ void attn_finish(const AttnParams& p, float* acc, uin
         sm_l[tid] = L;
     }
     __syncthreads();
-    for (uint32_t o = tid; o < G * hd; o += kAttnThreads) {
-        const uint32_t h = o / hd;
-        float v = 0.0f;
-#pragma unroll 4
-        for (uint32_t s = 0; s < active; s++) v += wts[s * G + h] * __ldcg(go + (size_t)s * G * hd + o);
-        const float L = sm_l[h];
-        ((OT*)p.out)[orow + o] = from_f32<OT>(L > 0.0f ? v / L : 0.0f);
+    // each thread folds all of its outputs at once with four independent sums apiece, so
+    // NO * 4 partial loads are in flight per step instead of one dependent chain
+    constexpr int NO = (G * 128 + kAttnThreads - 1) / kAttnThreads;
+    float v[NO][4];
+#pragma unroll
+    for (int k = 0; k < NO; k++) v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.0f;
+    uint32_t s = 0;
+    for (; s + 4 <= active; s += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+#pragma unroll
+            for (int k = 0; k < NO; k++) {
+                const uint32_t o = tid + k * kAttnThreads;
+                if (o < G * hd)
+                    v[k][u] += wts[(s + u) * G + o / hd] *
+                               __ldcg(go + (size_t)(s + u) * G * hd + o);
+            }
+        }
+    }
+    for (; s < active; s++) {
+#pragma unroll
+        for (int k = 0; k < NO; k++) {
+            const uint32_t o = tid + k * kAttnThreads;
+            if (o < G * hd) v[k][0] += wts[s * G + o / hd] * __ldcg(go + (size_t)s * G * hd + o);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < NO; k++) {
+        const uint32_t o = tid + k * kAttnThreads;
+        if (o < G * hd) {
+            const float L = sm_l[o / hd];
+            const float tot = (v[k][0] + v[k][1]) + (v[k][2] + v[k][3]);
+            ((OT*)p.out)[orow + o] = from_f32<OT>(L > 0.0f ? tot / L : 0.0f);
+        }
     }
     if (tid == 0) p.counters[grp] = 0;
+}
+
+// Merges the four warps' partial results of a CTA (per-head max wm, sum wl and unnormalised
+// output wo[warp][head][dim], all in shared memory) and hands the CTA's result to
+// attn_finish. Called by every thread after the warps wrote their parts.
+template <typename OT, int G>
+__device__ __forceinline__ void attn_merge_finish(const AttnParams& p, const float* wo,
+                                                  float (*wm)[8], float (*wl)[8], float* run_m,
+                                                  float* run_l, uint32_t hd, float* fold,
+                                                  float* wts, int* sm_last, uint32_t split,
+                                                  uint32_t active, uint32_t kvh, uint32_t b,
+                                                  uint32_t tid) {
+    __syncthreads();
+    if (tid < (uint32_t)G) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w][tid]);
+        float L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; w++)
+            if (wm[w][tid] != -INFINITY) L += wl[w][tid] * expf(wm[w][tid] - M);
+        run_m[tid] = M;
+        run_l[tid] = L;
+    }
+    __syncthreads();
+    const uint32_t di = tid % hd;
+    float acc[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float mw = wm[w][h];
+            if (mw != -INFINITY) a += wo[(w * G + h) * hd + di] * expf(mw - run_m[h]);
+        }
+        acc[h] = a;
+    }
+    attn_finish<OT, G>(p, acc, tid / hd, 1, di, fold, wts, run_m, run_l, sm_last, split, active,
+                       kvh, b, tid);
 }
 
 // The split's position range [start, end) and the number of splits holding positions.
@@ -257,35 +305,63 @@ __device__ __forceinline__ void attn_split_range(const AttnParams& p, uint32_t s
     *end = min(*start + chunk, total);
 }
 
-// ---- TMA kernel -----------------------------------------------------------------------------
+// ---- warp-independent SIMT kernel (f32 K/V; bf16 heads other than 64 and 128) ------------
+// The pipeline of the tensor-core kernel below with CUDA-core arithmetic: K/V tiles of 64
+// positions in a TMA ring (32/64/128-byte swizzle), each warp owning 16 positions of every
+// tile. For q.K lane l takes position l % 16 and half l / 16 of the head dims (the halves
+// meet in one shuffle); the warp's online softmax runs per head over its 16 positions; for
+// P.V lane l owns head dims l, l + 32, ... and each position's weights come by shuffle from
+// the lane that scored it. Warps release stages with one arrival each; thread 0 refills.
+constexpr uint32_t kWarpMaxStages = 4;
+
+struct AttnWarpLayout {
+    uint32_t stage_bytes, stages;
+    size_t q_off, fold_off, w_off, last_off, total;
+};
+
+__host__ __device__ inline AttnWarpLayout attn_warp_layout(uint32_t head, uint32_t esz, uint32_t G,
+                                                           uint32_t nsplit) {
+    AttnWarpLayout L;
+    L.stage_bytes = 2u * kAttnTile * head * esz;
+    uint32_t st = (100u * 1024) / L.stage_bytes;
+    L.stages = st < 2 ? 2 : st > kWarpMaxStages ? kWarpMaxStages : st;
+    size_t o = (size_t)L.stages * L.stage_bytes;
+    L.q_off = o;
+    o += (size_t)G * head * 4;
+    L.fold_off = o;
+    o += (size_t)kAttnThreads * G * 4;
+    L.w_off = o;
+    o += (size_t)nsplit * G * 4;
+    L.last_off = o;
+    o += 16;
+    L.total = o + 1024;
+    return L;
+}
+
 template <typename KT, typename OT, int G, int SWZ>
 __global__ void __launch_bounds__(kAttnThreads)
-    attn_decode_tma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
-                           const __grid_constant__ CUtensorMap vmap) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[kAttnStages];
-    constexpr int ESZ = sizeof(KT);
-    constexpr int VE = 16 / ESZ;
-    constexpr int PS = G < 4 ? 4 : G;
-    constexpr uint32_t CPB = SWZ / 16;   // 16-byte chunks per box row
+    attn_decode_warp_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap) {
+    constexpr uint32_t ESZ = sizeof(KT);
+    constexpr uint32_t VE = 16 / ESZ;     // elements per 16-byte chunk
     constexpr uint32_t BOXE = SWZ / ESZ;  // elements per box row
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kWarpMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kWarpMaxStages];
+    __shared__ float wm[4][8], wl[4][8], run_m[8], run_l[8];
+    __shared__ int sm_fail;
     const uint32_t hd = p.head;
-    const AttnTmaLayout L = attn_tma_layout(hd, ESZ, G, p.nsplit);
+    const AttnWarpLayout L = attn_warp_layout(hd, ESZ, G, p.nsplit);
+    const uint32_t S = L.stages;
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    float* qs = (float*)(smem + L.t.q_off);
-    float* sc = (float*)(smem + L.t.s_off);
-    float* pt = (float*)(smem + L.t.p_off);
-    float* st = (float*)(smem + L.t.st_off);
-    float* fold = (float*)(smem + L.t.fold_off);
-    float* wts = (float*)(smem + L.t.w_off);
-    float* sm_m = st;
-    float* sm_l = st + 8;
-    float* sm_a = st + 16;
-    int* sm_last = (int*)(st + 24);
+    float* qs = (float*)(smem + L.q_off);  // [G][hd], pre-scaled by 1/sqrt(hd)
+    float* fold = (float*)(smem + L.fold_off);
+    float* wts = (float*)(smem + L.w_off);
+    int* sm_last = (int*)(smem + L.last_off);
 
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-    const uint32_t nbox = L.rowbytes / SWZ;
+    const uint32_t nbox = hd * ESZ / SWZ;
 
     pdl_wait();
     uint32_t start, end, active;
@@ -295,27 +371,22 @@ __global__ void __launch_bounds__(kAttnThreads)
         return;
     }
     if (tid == 0) {
-        for (int s = 0; s < kAttnStages; s++) mbar_init(smem_u32(&full_bar[s]), 1);
+        for (uint32_t s = 0; s < S; s++) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 4);
+        }
         fence_barrier_init();
+        sm_fail = 0;
     }
     const float qscale = 1.0f / sqrtf((float)hd);
     const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * hd;
     for (uint32_t i = tid; i < G * hd; i += kAttnThreads) qs[i] = qsrc[i] * qscale;
-    if (tid < 8) {
-        sm_m[tid] = -INFINITY;
-        sm_l[tid] = 0.0f;
-    }
-    const uint32_t ways = kAttnThreads / hd;
-    const uint32_t way = tid / hd, di = tid % hd;
-    float acc[G];
-#pragma unroll
-    for (int h = 0; h < G; h++) acc[h] = 0.0f;
     __syncthreads();
 
     const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
     const int32_t ybase = (int32_t)(b * p.seq + start);
     auto issue = [&](uint32_t i) {
-        const uint32_t s = i % kAttnStages;
+        const uint32_t s = i % S;
         const uint32_t bar = smem_u32(&full_bar[s]);
         unsigned char* kst = smem + (size_t)s * L.stage_bytes;
         unsigned char* vst = kst + L.stage_bytes / 2;
@@ -327,85 +398,125 @@ __global__ void __launch_bounds__(kAttnThreads)
             tma_load_2d(smem_u32(vst + (size_t)j * kAttnTile * SWZ), &vmap, x, y, bar);
         }
     };
+    uint32_t issued = 0;  // meaningful in thread 0
     if (tid == 0)
-        for (uint32_t i = 0; i < ntiles && i < (uint32_t)kAttnStages; i++) issue(i);
+        for (; issued < ntiles && issued < S; issued++) issue(issued);
 
-    uint32_t failed_at = ntiles;
+    const uint32_t pl = lane % 16, half = lane / 16, hh = hd / 2;
+    float acc[G][4];
+    float m[G], lp[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+        m[h] = -INFINITY;
+        lp[h] = 0.0f;
+    }
     for (uint32_t i = 0; i < ntiles; i++) {
-        const uint32_t s = i % kAttnStages;
-        const bool got = mbar_wait_bounded(smem_u32(&full_bar[s]), (i / kAttnStages) & 1);
-        if (!__syncthreads_and(got)) {
-            failed_at = i;
+        if (tid == 0 && i >= 1 && issued < ntiles) {
+            const uint32_t r = i - 1;
+            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) issue(issued++);
+            else sm_fail = 1;
+        }
+        __syncwarp();
+        if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
+        const uint32_t s = i % S;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1))) {
+            sm_fail = 1;
             break;
         }
         const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
         const unsigned char* kst = smem + (size_t)s * L.stage_bytes;
         const unsigned char* vst = kst + L.stage_bytes / 2;
-        // scores: thread -> (position pp, head group hg)
-        {
-            const uint32_t pp = tid % kAttnTile, hg = tid / kAttnTile;
-            float d[G];
+        // q.K: position 16 * warp + pl over half `half` of the head dims
+        const uint32_t row = warp * 16 + pl;
+        float d[G];
 #pragma unroll
-            for (int h = 0; h < G; h++) d[h] = 0.0f;
-            if (hg < (uint32_t)G) {
-                for (uint32_t j = 0; j < nbox; j++) {
+        for (int h = 0; h < G; h++) d[h] = 0.0f;
+        for (uint32_t c = 0; c < hh / VE; c++) {
+            const uint32_t e0 = half * hh + c * VE;
+            const uint32_t byte = e0 * ESZ;
+            const uint32_t off =
+                swizzle_off<SWZ>((byte / SWZ) * kAttnTile * SWZ + row * SWZ + byte % SWZ);
+            float kf[VE];
+            unpack(*reinterpret_cast<const uint4*>(kst + off), kf, KT());
 #pragma unroll
-                    for (uint32_t c = 0; c < CPB; c++) {
-                        const uint32_t off =
-                            swizzle_off<SWZ>(j * kAttnTile * SWZ + pp * SWZ + c * 16);
-                        float kf[VE];
-                        unpack(*reinterpret_cast<const uint4*>(kst + off), kf, KT());
-                        const uint32_t e0 = j * BOXE + c * VE;
+            for (int h = 0; h < G; h++) {
+                const float* qh = qs + h * hd + e0;
 #pragma unroll
-                        for (int h = 0; h < G; h++) {
-                            if ((h % 2) != (int)hg && G > 1) continue;
-                            const float* qh = qs + h * hd + e0;
+                for (uint32_t e = 0; e < VE; e++) d[h] = fmaf(qh[e], kf[e], d[h]);
+            }
+        }
+        const bool valid = row < rows;
+        float e[G];
 #pragma unroll
-                            for (int e = 0; e < VE; e++) d[h] = fmaf(qh[e], kf[e], d[h]);
-                        }
-                    }
-                }
+        for (int h = 0; h < G; h++) {
+            // every lane takes part in the shuffle; invalid positions are masked after it
+            const float other = __shfl_xor_sync(0xffffffffu, d[h], 16);
+            const float sc = valid ? d[h] + other : -INFINITY;
+            float t = sc;
 #pragma unroll
-                for (int h = 0; h < G; h++) {
-                    if ((h % 2) != (int)hg && G > 1) continue;
-                    sc[h * kAttnTile + pp] = pp < rows ? d[h] : -INFINITY;
+            for (int off = 1; off < 16; off <<= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, off));
+            const float n = fmaxf(m[h], t);
+            const float alpha = n == -INFINITY ? 1.0f : expf(m[h] - n);
+            e[h] = n == -INFINITY ? 0.0f : expf(sc - n);
+            m[h] = n;
+            lp[h] = lp[h] * alpha + e[h];
+#pragma unroll
+            for (int k = 0; k < 4; k++) acc[h][k] *= alpha;
+        }
+        // P.V: lane owns dims lane + 32k; the weight of position q comes from lane q
+        for (uint32_t q = 0; q < 16; q++) {
+            const uint32_t vrow = warp * 16 + q;
+            float w[G];
+#pragma unroll
+            for (int h = 0; h < G; h++) w[h] = __shfl_sync(0xffffffffu, e[h], q);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t dd = lane + 32 * k;
+                if (dd < hd) {
+                    const uint32_t byte = dd * ESZ;
+                    const uint32_t off = swizzle_off<SWZ>((byte / SWZ) * kAttnTile * SWZ +
+                                                          vrow * SWZ + byte % SWZ);
+                    const float v = to_f32(*reinterpret_cast<const KT*>(vst + off));
+#pragma unroll
+                    for (int h = 0; h < G; h++) acc[h][k] = fmaf(w[h], v, acc[h][k]);
                 }
             }
         }
-        __syncthreads();
-        attn_softmax_tile<G>(sc, pt, sm_m, sm_l, sm_a, warp, lane);
-        __syncthreads();
-        // P.V: thread -> (dim di, way); ways split the tile's positions
-        if (way < ways) {
-#pragma unroll
-            for (int h = 0; h < G; h++) acc[h] *= sm_a[h];
-            const uint32_t byte = di * ESZ;
-            const uint32_t vcol = (byte / SWZ) * kAttnTile * SWZ + byte % SWZ;
-            for (uint32_t r = way; r < rows; r += ways) {
-                const float v =
-                    to_f32(*reinterpret_cast<const KT*>(vst + swizzle_off<SWZ>(vcol + r * SWZ)));
-                const float* pr = pt + r * PS;
-#pragma unroll
-                for (int h = 0; h < G; h++) acc[h] = fmaf(pr[h], v, acc[h]);
-            }
-        }
-        __syncthreads();
-        if (tid == 0 && i + kAttnStages < ntiles) issue(i + kAttnStages);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
     }
-    if (failed_at < ntiles) {
-        // a bounded wait ran out: flag it, let the copies in flight land, and stop
+    __syncthreads();
+    if (sm_fail) {
         if (tid == 0) {
             atomicOr(p.flags, kFlagWaitTimeout);
-            for (uint32_t i = failed_at; i < ntiles && i < failed_at + kAttnStages; i++)
-                mbar_wait_bounded(smem_u32(&full_bar[i % kAttnStages]), (i / kAttnStages) & 1);
+            for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
+                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1);
         }
         __syncthreads();
         pdl_trigger();
         return;
     }
     pdl_trigger();
-    attn_finish<OT, G>(p, acc, way, ways, di, fold, wts, sm_m, sm_l, sm_last, split, active, kvh,
-                       b, tid);
+    // per-warp sums over the 16 scoring lanes (lanes 16-31 hold copies)
+    float* wo = (float*)smem;  // [4 warps][G][hd] over the drained stages
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        float l = lane < 16 ? lp[h] : 0.0f;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (lane == 0) {
+            wm[warp][h] = m[h];
+            wl[warp][h] = l;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t dd = lane + 32 * k;
+            if (dd < hd) wo[(warp * G + h) * hd + dd] = acc[h][k];
+        }
+    }
+    attn_merge_finish<OT, G>(p, wo, wm, wl, run_m, run_l, hd, fold, wts, sm_last, split, active,
+                             kvh, b, tid);
 }
 
 // ---- tensor-core kernel (bf16 K/V, head 64 or 128) --------------------------------------------
@@ -667,33 +778,8 @@ __global__ void __launch_bounds__(kAttnThreads)
             wo[(warp * G + 2 * t + 1) * HD + d0 + 8] = o[m][3];
         }
     }
-    __syncthreads();
-    if (tid < (uint32_t)G) {
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w][tid]);
-        float L = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; w++)
-            if (wm[w][tid] != -INFINITY) L += wl[w][tid] * expf(wm[w][tid] - M);
-        run_m[tid] = M;
-        run_l[tid] = L;
-    }
-    __syncthreads();
-    const uint32_t di = tid % HD;
-    float acc[G];
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-        float a = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; w++) {
-            const float mw = wm[w][h];
-            if (mw != -INFINITY) a += wo[(w * G + h) * HD + di] * expf(mw - run_m[h]);
-        }
-        acc[h] = a;
-    }
-    attn_finish<OT, G>(p, acc, tid / HD, 1, di, fold, wts, run_m, run_l, sm_last, split, active,
-                       kvh, b, tid);
+    attn_merge_finish<OT, G>(p, wo, wm, wl, run_m, run_l, HD, fold, wts, sm_last, split, active,
+                             kvh, b, tid);
 }
 
 // ---- plain-load kernel (head sizes the TMA boxes cannot tile) --------------------------------
@@ -817,13 +903,39 @@ bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t
 
 uint32_t attention_choose_splits(uint32_t batch, uint32_t kv_heads, uint32_t seq, int sm_count,
                                  uint32_t max_splits) {
-    // about four CTAs per SM over the (batch, kv head, split) grid
-    const uint64_t target = (uint64_t)std::max(sm_count, 1) * 4;
+    // The kernels keep two CTAs per SM resident. Split the positions so the (batch, kv
+    // head, split) grid fills whole waves of those slots -- the first split count whose last
+    // wave is at least 90% full, else the fullest -- with at least four 64-position tiles
+    // per split. A grid with a group per slot or more is not split.
+    const uint64_t slots = (uint64_t)std::max(sm_count, 1) * 2;
     const uint64_t groups = std::max<uint64_t>(1, (uint64_t)batch * kv_heads);
-    uint64_t ns = (target + groups - 1) / groups;
-    ns = std::min<uint64_t>(ns, (seq + kAttnTile - 1) / kAttnTile);
-    ns = std::min<uint64_t>(ns, max_splits);
-    return (uint32_t)std::max<uint64_t>(ns, 1);
+    const uint64_t tiles = (seq + kAttnTile - 1) / kAttnTile;
+    const uint64_t cap = std::min<uint64_t>(std::max<uint32_t>(max_splits, 1),
+                                            std::max<uint64_t>(1, tiles / 4));
+    if (groups >= slots || cap <= 1) return 1;
+    uint64_t best = 1;
+    double best_fill = 0.0;
+    for (uint64_t ns = 1; ns <= cap; ns++) {
+        const uint64_t ctas = groups * ns;
+        const uint64_t waves = (ctas + slots - 1) / slots;
+        const double fill = (double)ctas / (double)(waves * slots);
+        if (fill >= 0.9) return (uint32_t)ns;
+        if (fill > best_fill) {
+            best_fill = fill;
+            best = ns;
+        }
+    }
+    return (uint32_t)best;
+}
+
+// Largest split count attention_choose_splits picks for any grid of up to `max_groups`
+// (batch, kv head) groups: the scratch bound of a block whose kv head count is not yet known.
+uint32_t attention_max_splits(uint32_t max_groups, uint32_t seq, int sm_count,
+                              uint32_t max_splits) {
+    uint32_t m = 1;
+    for (uint32_t g = 1; g <= max_groups; g++)
+        m = std::max(m, attention_choose_splits(g, 1, seq, sm_count, max_splits));
+    return m;
 }
 
 void attention_scratch_size(uint32_t batch, uint32_t heads, uint32_t head, uint32_t nsplit,
@@ -878,17 +990,17 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
                        swz / esz, kAttnTile, swz);
         encode_tmap_2d(&vmap, esz == 2 ? AB_BF16 : AB_F32, p.vcache, inner, rows, inner * esz,
                        swz / esz, kAttnTile, swz);
-        const size_t smem = attn_tma_layout(p.head, esz, G, p.nsplit).total;
+        const size_t smem = attn_warp_layout(p.head, esz, G, p.nsplit).total;
         if (smem > 220 * 1024) invalid("attention: shared-memory stage too large");
         if (swz == 128) {
-            auto kern = attn_decode_tma_kernel<KT, OT, G, 128>;
+            auto kern = attn_decode_warp_kernel<KT, OT, G, 128>;
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
                 return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
             });
         } else {
-            auto kern = attn_decode_tma_kernel<KT, OT, G, 64>;
+            auto kern = attn_decode_warp_kernel<KT, OT, G, 64>;
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
@@ -1017,8 +1129,8 @@ static AttnParams attention_decode_operands(ab_tensor q, ab_tensor key_cache,
     p.seq = seq;
     p.batch = batch;
     p.nsplit = attention_choose_splits(batch, kv_heads, seq, sms, 256);
-    // a (batch, kv head) group per SM or more: short contexts are not split
-    p.min_chunk = (uint64_t)batch * kv_heads >= (uint64_t)sms ? 256u : 0u;
+    // a split covers at least four tiles, whatever the position
+    p.min_chunk = 4 * kAttnTile;
     p.step = (const Step*)step.data;
     return p;
 }

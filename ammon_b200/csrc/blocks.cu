@@ -95,8 +95,8 @@ ab_attention_block* attention_block_new(ab_runtime* rt, uint32_t hidden, uint32_
     b->max_batch = max_batch;
     b->theta = rope_theta;
     b->tp = tp;
-    // worst case over kv_heads (1 kv head gives the most splits per group)
-    b->nsplit_max = attention_choose_splits(max_batch, 1, seq_len, rt->sm_count, 256);
+    // worst case over every kv head count the weights may bring (at most one per head)
+    b->nsplit_max = attention_max_splits(max_batch * heads, seq_len, rt->sm_count, 256);
     uint64_t floats = 0, counters = 0;
     attention_scratch_size(max_batch, heads, head, b->nsplit_max, &floats, &counters);
     const uint64_t qd = (uint64_t)heads * head;
@@ -379,11 +379,9 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         a.seq = blk->seq;
         a.batch = batch;
         a.nsplit = nsplit;
-        // with a (batch, kv head) group per SM or more, short contexts are not split: a
-        // split pays a partial write and a fold, and the groups already fill the GPU
-        a.min_chunk = (uint64_t)batch * kv_heads >= (uint64_t)(s->rt ? s->rt->sm_count : 148)
-                          ? 256u
-                          : 0u;
+        // a split covers at least four 64-position tiles: a split pays a partial write and
+        // a share of the fold, which shorter ones do not earn back
+        a.min_chunk = 256u;
         uint64_t floats = 0, counters = 0;
         attention_scratch_size(batch, heads, head, nsplit, &floats, &counters);
         a.part_o = blk->part;

@@ -33,16 +33,27 @@ __global__ void embed_kernel(const TT* __restrict__ table, uint32_t vocab, uint3
     const TT* src = table + (uint64_t)token * dim;
     constexpr int V = 16 / sizeof(TT);
     if (vec) {
-        // 16-byte row vectors in, 16-byte vectors out (two for a bf16 -> f32 gather)
-        for (uint32_t v = tid; v < dim / V; v += stride) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(src + (uint64_t)v * V);
-            if constexpr (sizeof(TT) == sizeof(XT)) {
-                *reinterpret_cast<uint4*>(dst + (uint64_t)v * V) = raw;
-            } else {
-                const TT* e = reinterpret_cast<const TT*>(&raw);
-                float4* d4 = reinterpret_cast<float4*>(dst + (uint64_t)v * V);
-                d4[0] = make_float4(to_f32(e[0]), to_f32(e[1]), to_f32(e[2]), to_f32(e[3]));
-                d4[1] = make_float4(to_f32(e[4]), to_f32(e[5]), to_f32(e[6]), to_f32(e[7]));
+        // 16-byte row vectors in, 16-byte vectors out (two for a bf16 -> f32 gather); four
+        // loads per thread in flight before the stores
+        const uint32_t nv = dim / V;
+        for (uint32_t v0 = tid; v0 < nv; v0 += 4 * stride) {
+            uint4 raw[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (v0 + u * stride < nv)
+                    raw[u] = *reinterpret_cast<const uint4*>(src + (uint64_t)(v0 + u * stride) * V);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t v = v0 + u * stride;
+                if (v >= nv) break;
+                if constexpr (sizeof(TT) == sizeof(XT)) {
+                    *reinterpret_cast<uint4*>(dst + (uint64_t)v * V) = raw[u];
+                } else {
+                    const TT* e = reinterpret_cast<const TT*>(&raw[u]);
+                    float4* d4 = reinterpret_cast<float4*>(dst + (uint64_t)v * V);
+                    d4[0] = make_float4(to_f32(e[0]), to_f32(e[1]), to_f32(e[2]), to_f32(e[3]));
+                    d4[1] = make_float4(to_f32(e[4]), to_f32(e[5]), to_f32(e[6]), to_f32(e[7]));
+                }
             }
         }
     } else {
@@ -114,12 +125,21 @@ __global__ void __launch_bounds__(256)
     const XT* xr = x + (uint64_t)blockIdx.x * size;
     OT* orow = o + (uint64_t)blockIdx.x * size;
     if (STAGED) {
-        for (uint32_t v = t; v < size / 8; v += 256) {
-            float r[8];
-            load8(xr + (uint64_t)v * 8, r);
-            float4* d = reinterpret_cast<float4*>(xs + v * 8);
-            d[0] = make_float4(r[0], r[1], r[2], r[3]);
-            d[1] = make_float4(r[4], r[5], r[6], r[7]);
+        // four 8-element vectors per thread in flight, then into shared memory
+        const uint32_t n = size / 8;
+        for (uint32_t v0 = t; v0 < n; v0 += 1024) {
+            float r[4][8];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (v0 + u * 256 < n) load8(xr + (uint64_t)(v0 + u * 256) * 8, r[u]);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (v0 + u * 256 < n) {
+                    float4* d = reinterpret_cast<float4*>(xs + (v0 + u * 256) * 8);
+                    d[0] = make_float4(r[u][0], r[u][1], r[u][2], r[u][3]);
+                    d[1] = make_float4(r[u][4], r[u][5], r[u][6], r[u][7]);
+                }
+            }
         }
         __syncthreads();
     }
@@ -136,6 +156,7 @@ __global__ void __launch_bounds__(256)
     }
     float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lanes[0], (float)size), eps)));
     if (STAGED) {
+#pragma unroll 4
         for (uint32_t v = t; v < size / 8; v += 256) {
             float wv[8], ov[8];
             load8(w + (uint64_t)v * 8, wv);
@@ -479,7 +500,8 @@ void record_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x) {
                     ((uintptr_t)x.data % 16 == 0);
     uint32_t* flags = flags_of(s);
     const Step* st = (const Step*)step.data;
-    const unsigned chunks = std::max(1u, std::min(64u, (dim / (unsigned)(16 / esz) + 255) / 256));
+    // each thread moves up to four 16-byte vectors of its row
+    const unsigned chunks = std::max(1u, std::min(64u, (dim / (unsigned)(16 / esz) + 1023) / 1024));
     dim3 grid(chunks, batch);
     if (table.dtype == AB_F32) {
         const float* tb = (const float*)table.data;

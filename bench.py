@@ -168,10 +168,11 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def layer_bytes(w, batch, shards=1):
+def layer_bytes(w, batch, shards=1, attn_pos=None):
     """Algorithmic bytes per launch of each fused kernel (weights once, activations and
     KV rows read/written), for the kernel labels the step graph records. With tensor
-    parallelism over `shards` ranks, one rank's share (the weights and K/V are split)."""
+    parallelism over `shards` ranks, one rank's share (the weights and K/V are split).
+    attn_pos: the position the attention launch decodes at (K/V rows 0..pos per stream)."""
     e = 2 if w["bf16"] else 4
     d, F, V = w["dim"], w["hidden"] // shards, w["vocab"] // shards
     qd = w["heads"] // shards * w["head_dim"]
@@ -183,6 +184,8 @@ def layer_bytes(w, batch, shards=1):
         "attn_wo_residual": d * qd * e + batch * (qd * e + 2 * d * 4),
         "final_norm_classifier": V * d * e + batch * (d * 4 + V * 4) + d * e,
     }
+    if attn_pos is not None:
+        out["attn_decode"] = batch * (2 * kvd * e * (attn_pos + 1) + qd * 4 + qd * e)
     out["attn_wo_partial"] = out["attn_wo_residual"]
     out["ffn_down_partial"] = out["ffn_down_residual"]
     return out
@@ -646,7 +649,8 @@ def main():
         c[1] += ms
     total_ms = sum(times)
     shards = world if tp else 1
-    lb = layer_bytes(w, B, shards)
+    # the timed nodes replay the last deposited steps: the e2e loop's final position
+    lb = layer_bytes(w, B, shards, attn_pos=pos0 + e2e_steps - 1)
     dom = max(per_label, key=lambda l: per_label[l][1])
     n_dom, ms_dom = per_label[dom]
     t_launch = ms_dom / n_dom / 1e3
