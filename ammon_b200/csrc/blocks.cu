@@ -410,12 +410,21 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
             record_attention(s, "attn_decode", a);
             if (blk->tp) {
                 // partial projection of this rank's heads; rank 0 adds the residual, and
-                // the all-reduce sums every rank's part straight into x
+                // the all-reduce sums every rank's part straight into x: over NVLink peer
+                // slots at GEMV batches, else through NCCL
                 o2.out = blk->tp_y;
                 o2.addend = comm_rank(blk->tp) == 0 ? (const float*)x.data : nullptr;
-                record_gemv(s, "attn_wo_partial", o2, wdt, batch, kProNone, kEpiStore);
-                record_allreduce_f32(s, "attn_allreduce", blk->tp, blk->tp_y, (float*)x.data,
-                                     (size_t)batch * hidden);
+                if (comm_has_peers(blk->tp) && batch <= kGemvMaxBatch) {
+                    const TpPush tgt = comm_push_target(blk->tp);
+                    o2.out = tgt.out;
+                    record_gemv(s, "attn_wo_partial", o2, wdt, batch, kProNone, kEpiStore);
+                    record_tp_reduce(s, "attn_allreduce", blk->tp, tgt, (float*)x.data,
+                                     batch * hidden);
+                } else {
+                    record_gemv(s, "attn_wo_partial", o2, wdt, batch, kProNone, kEpiStore);
+                    record_allreduce_f32(s, "attn_allreduce", blk->tp, blk->tp_y,
+                                         (float*)x.data, (size_t)batch * hidden);
+                }
             } else {
                 record_gemv(s, "attn_wo_residual", o2, wdt, batch, kProNone, kEpiResidual);
             }
@@ -509,9 +518,17 @@ int ab_swiglu_block_record(ab_swiglu_block* blk, ab_scheme* s, ab_tensor x,
             if (blk->tp) {
                 d.out = blk->tp_y;
                 d.addend = comm_rank(blk->tp) == 0 ? (const float*)x.data : nullptr;
-                record_gemv(s, "ffn_down_partial", d, wdt, batch, kProNone, kEpiStore);
-                record_allreduce_f32(s, "ffn_allreduce", blk->tp, blk->tp_y, (float*)x.data,
-                                     (size_t)batch * hidden);
+                if (comm_has_peers(blk->tp) && batch <= kGemvMaxBatch) {
+                    const TpPush tgt = comm_push_target(blk->tp);
+                    d.out = tgt.out;
+                    record_gemv(s, "ffn_down_partial", d, wdt, batch, kProNone, kEpiStore);
+                    record_tp_reduce(s, "ffn_allreduce", blk->tp, tgt, (float*)x.data,
+                                     batch * hidden);
+                } else {
+                    record_gemv(s, "ffn_down_partial", d, wdt, batch, kProNone, kEpiStore);
+                    record_allreduce_f32(s, "ffn_allreduce", blk->tp, blk->tp_y,
+                                         (float*)x.data, (size_t)batch * hidden);
+                }
             } else {
                 record_gemv(s, "ffn_down_residual", d, wdt, batch, kProNone, kEpiResidual);
             }

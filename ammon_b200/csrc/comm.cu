@@ -9,6 +9,10 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "tma.cuh"
 
 #include "internal.h"
 #include "ops.h"
@@ -67,12 +71,232 @@ struct ab_comm {
     ab::Runtime* rt = nullptr;
     ncclComm_t comm = nullptr;
     int32_t rank = 0, world = 1;
+    // NVLink peer exchange (comm_peers_setup): one device block per rank holding
+    // [flags: 2 parities x kTpMaxWorld u64][pad][send: 2 parities x max_elems f32],
+    // opened by every peer through CUDA IPC.
+    bool peers = false;
+    size_t max_elems = 0;
+    unsigned char* local = nullptr;
+    unsigned char* peer_base[ab::kTpMaxWorld] = {};
+    uint64_t* epoch = nullptr;   // device: bumped once per recorded step
+    uint32_t next_site = 0;      // all-reduce sites numbered in recording order
 };
 
 namespace ab {
 
 int comm_rank(const ab_comm* c) { return c ? c->rank : 0; }
 int comm_world(const ab_comm* c) { return c ? c->world : 1; }
+
+static constexpr size_t kTpFlagBytes = 2 * kTpMaxWorld * sizeof(uint64_t);
+static constexpr size_t kTpRecvOff = 256;
+
+static uint64_t* tp_flags(unsigned char* base, uint32_t parity) {
+    return (uint64_t*)base + (size_t)parity * kTpMaxWorld;
+}
+static float* tp_send(const ab_comm* c, unsigned char* base, uint32_t parity) {
+    return (float*)(base + kTpRecvOff) + (size_t)parity * c->max_elems;
+}
+
+// Blocking NCCL all-gather of host bytes through device staging (setup time only).
+static void allgather_host(ab_comm* c, const void* mine, void* all, size_t bytes) {
+    unsigned char* d = nullptr;
+    cuda_check(cudaMalloc(&d, bytes * (c->world + 1)), "cudaMalloc");
+    cudaError_t e = cudaMemcpy(d, mine, bytes, cudaMemcpyHostToDevice);
+    ncclResult_t r = ncclSuccess;
+    if (e == cudaSuccess) r = nccl().all_gather(d, d + bytes, bytes, ncclUint8, c->comm, c->rt->stream);
+    if (e == cudaSuccess && r == ncclSuccess) e = cudaStreamSynchronize(c->rt->stream);
+    if (e == cudaSuccess && r == ncclSuccess)
+        e = cudaMemcpy(all, d + bytes, bytes * c->world, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    nccl_check(r, "ncclAllGather");
+    cuda_check(e, "peer exchange");
+}
+
+bool comm_peers_setup(ab_comm* c, size_t max_elems) {
+    if (c->peers) {
+        if (max_elems > c->max_elems) fail(AB_ERR_ARGUMENT, "peer buffers set up smaller");
+        return true;
+    }
+    if (c->world < 2 || c->world > (int)kTpMaxWorld) return false;
+    const char* force = std::getenv("AMMON_B200_TP_NCCL");
+    bool want = !(force && force[0] == '1');
+    c->rt->activate();
+    c->max_elems = (max_elems + 63) / 64 * 64;
+    const size_t bytes = kTpRecvOff + 2 * c->max_elems * sizeof(float);
+    static_assert(kTpFlagBytes <= kTpRecvOff, "flag block");
+    cudaIpcMemHandle_t mine;
+    std::memset(&mine, 0, sizeof(mine));
+    int ok = 0;
+    if (want && cudaMalloc(&c->local, bytes) == cudaSuccess &&
+        cudaMemset(c->local, 0, bytes) == cudaSuccess &&
+        cudaMalloc(&c->epoch, sizeof(uint64_t)) == cudaSuccess &&
+        cudaMemset(c->epoch, 0, sizeof(uint64_t)) == cudaSuccess &&
+        cudaIpcGetMemHandle(&mine, c->local) == cudaSuccess)
+        ok = 1;
+    cudaGetLastError();
+    std::vector<cudaIpcMemHandle_t> all(c->world);
+    allgather_host(c, &mine, all.data(), sizeof(mine));
+    // every rank opens every peer's block; all must succeed or none use the path
+    for (int r = 0; r < c->world && ok; r++) {
+        if (r == c->rank) {
+            c->peer_base[r] = c->local;
+            continue;
+        }
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0;
+        } else {
+            c->peer_base[r] = (unsigned char*)ptr;
+        }
+    }
+    std::vector<int> oks(c->world);
+    allgather_host(c, &ok, oks.data(), sizeof(int));
+    bool every = true;
+    for (int v : oks) every = every && v == 1;
+    if (!every) {
+        comm_peers_release(c);
+        return false;
+    }
+    c->peers = true;
+    return true;
+}
+
+void comm_peers_release(ab_comm* c) {
+    for (int r = 0; r < (int)kTpMaxWorld; r++) {
+        if (c->peer_base[r] && r != c->rank) cudaIpcCloseMemHandle(c->peer_base[r]);
+        c->peer_base[r] = nullptr;
+    }
+    if (c->local) cudaFree(c->local);
+    if (c->epoch) cudaFree(c->epoch);
+    c->local = nullptr;
+    c->epoch = nullptr;
+    c->peers = false;
+}
+
+bool comm_has_peers(const ab_comm* c) { return c && c->peers; }
+void comm_begin_recording(ab_comm* c) {
+    if (c) c->next_site = 0;
+}
+
+__global__ void tp_epoch_kernel(uint64_t* epoch) {
+    pdl_wait();
+    *epoch += 1;
+    pdl_trigger();
+}
+
+void record_tp_epoch(ab_scheme* s, ab_comm* c) {
+    uint64_t* ep = c->epoch;
+    s->add("tp_epoch", [=](cudaStream_t st) {
+        return launch(st, dim3(1), dim3(1), 0, true, tp_epoch_kernel, ep);
+    });
+}
+
+TpPush comm_push_target(ab_comm* c) {
+    TpPush t = {};
+    t.site = c->next_site++;
+    t.out = tp_send(c, c->local, t.site & 1);
+    return t;
+}
+
+// Every rank's send slot of one parity and this rank's flag in every rank's flag block,
+// as this rank addresses them (its own, and the peers' through their IPC mappings).
+struct TpSources {
+    const float* src[kTpMaxWorld];
+    uint64_t* flag[kTpMaxWorld];
+};
+
+// Announces this rank's partial of the site (stored by the projection kernel before this
+// one in stream order, so it already sits in this GPU's memory where the peers read it),
+// waits until every rank announced its own, then sums the ranks' partials in rank order
+// into x, reading the peers' slots over NVLink (every rank adds the same values in the
+// same order, so the replicated x stays bit-identical).
+__global__ void __launch_bounds__(256) tp_reduce_kernel(const TpSources srcs,
+                                                        const uint64_t* flags,
+                                                        const uint64_t* epoch, uint32_t site,
+                                                        uint32_t world, float* x, uint32_t n,
+                                                        uint32_t* err) {
+    pdl_wait();
+    __shared__ int ok;
+    const uint64_t want = tp_signal_value(*epoch, site);
+    if (blockIdx.x == 0 && threadIdx.x < world) {
+        __threadfence_system();
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(srcs.flag[threadIdx.x]),
+                     "l"(want)
+                     : "memory");
+    }
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if (threadIdx.x < world) {
+        const uint64_t* f = flags + threadIdx.x;
+        uint64_t v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+        if (v < want) {
+            const uint64_t t0 = global_timer_ns();
+            while (true) {
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+                if (v >= want) break;
+                if (global_timer_ns() - t0 > 1000000000ull) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (!ok) {
+        if (threadIdx.x == 0) atomicOr(err, kFlagWaitTimeout);
+        return;
+    }
+    if (n % 4 == 0) {
+        // four elements per thread, every rank's load in flight before the sum
+        for (uint32_t i = (blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n;
+             i += gridDim.x * blockDim.x * 4) {
+            float4 v[kTpMaxWorld];
+#pragma unroll
+            for (uint32_t r = 0; r < kTpMaxWorld; r++)
+                if (r < world) v[r] = __ldcv(reinterpret_cast<const float4*>(srcs.src[r] + i));
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (uint32_t r = 0; r < kTpMaxWorld; r++) {
+                if (r < world) {
+                    acc.x += v[r].x;
+                    acc.y += v[r].y;
+                    acc.z += v[r].z;
+                    acc.w += v[r].w;
+                }
+            }
+            *reinterpret_cast<float4*>(x + i) = acc;
+        }
+    } else {
+        for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
+             i += gridDim.x * blockDim.x) {
+            float acc = 0.0f;
+            for (uint32_t r = 0; r < world; r++) acc += __ldcv(srcs.src[r] + i);
+            x[i] = acc;
+        }
+    }
+    pdl_trigger();
+}
+
+void record_tp_reduce(ab_scheme* s, const char* label, ab_comm* c, const TpPush& push,
+                      float* x, uint32_t n) {
+    const uint32_t parity = push.site & 1;
+    TpSources srcs = {};
+    for (int r = 0; r < c->world; r++) {
+        srcs.src[r] = tp_send(c, c->peer_base[r], parity);
+        srcs.flag[r] = tp_flags(c->peer_base[r], parity) + c->rank;
+    }
+    const uint64_t* flags = tp_flags(c->local, parity);
+    const uint64_t* ep = c->epoch;
+    const uint32_t site = push.site, world = (uint32_t)c->world;
+    uint32_t* err = c->rt->flags;
+    const unsigned grid = std::max(1u, std::min(32u, (n + 1023) / 1024));
+    s->add(label, [=](cudaStream_t st) {
+        return launch(st, dim3(grid), dim3(256), 0, true, tp_reduce_kernel, srcs, flags, ep, site,
+                      world, x, n, err);
+    });
+}
 
 // Records an in-place or out-of-place float sum over the communicator.
 void record_allreduce_f32(ab_scheme* s, const char* label, ab_comm* c, const float* send,
@@ -145,6 +369,16 @@ int ab_comm_destroy(ab_comm* c) {
         if (!c) return;
         c->rt->activate();
         cudaStreamSynchronize(c->rt->stream);
+        if (c->peers && c->comm) {
+            // every rank is done writing into its peers before any block goes away
+            int one = 1;
+            std::vector<int> all(c->world);
+            try {
+                allgather_host(c, &one, all.data(), sizeof(int));
+            } catch (...) {
+            }
+        }
+        comm_peers_release(c);
         if (c->comm) nccl().comm_destroy(c->comm);
         delete c;
     });

@@ -212,6 +212,11 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
         x.rank = 1;
         x.dims[0] = c.dim;
     }
+    if (m->comm && comm_has_peers(m->comm)) {
+        // a new epoch per replay names this step's peer flags; sites count from zero
+        comm_begin_recording(m->comm);
+        record_tp_epoch(s, m->comm);
+    }
     check(ab_embedding_record(s, m->embed, m->step, x));
     for (uint32_t l = 0; l < c.layers; l++) {
         ab_tensor key, value;
@@ -328,6 +333,9 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
             m->w3.push_back(alloc_t(rt, dt, {m->hidden_l, c.dim}));
         }
         check(ab_kvcache_create(rt, c.layers, c.seq, m->kv_l, c.head_dim, dt, c.batch, &m->cache));
+        // NVLink peer slots for the per-block row all-reduce (collective; falls back to
+        // NCCL on every rank when a peer cannot be opened)
+        if (comm && world > 1) comm_peers_setup(comm, (size_t)c.batch * c.dim);
         m->attn = attention_block_new(rt, c.dim, m->heads_l, c.head_dim, c.seq, c.batch,
                                       c.rope_theta, comm);
         m->ffn = swiglu_block_new(rt, c.dim, m->hidden_l, c.batch, comm);

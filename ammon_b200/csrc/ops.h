@@ -30,6 +30,19 @@ enum GemvEpi : int {
     kEpiResidual = 3,  // out[b, r] += y (f32 residual stream)
 };
 
+// Where a tensor-parallel projection leaves its partial for the row all-reduce of one
+// site: this rank's send slot (f32, read by the peers over NVLink) (comm.cu).
+constexpr uint32_t kTpMaxWorld = 8;
+struct TpPush {
+    float* out;
+    uint32_t site;
+};
+
+// Value a rank's flag holds once site `site` of step `epoch` was pushed.
+__host__ __device__ inline uint64_t tp_signal_value(uint64_t epoch, uint32_t site) {
+    return epoch * 1024 + site + 1;
+}
+
 // Parameters of one fused GEMV launch (plain old data; passed by value to the kernel).
 struct GemvParams {
     // Virtual weight matrix: up to three row-major [rows, K] segments stacked, or two
@@ -155,6 +168,21 @@ ab_swiglu_block* swiglu_block_new(ab_runtime* rt, uint32_t hidden, uint32_t inte
 // ---- tensor parallelism (comm.cu) ----
 int comm_rank(const ab_comm* c);
 int comm_world(const ab_comm* c);
+// NVLink peer exchange for the row all-reduce of the decode projections: every rank's
+// projection stores its partial in its own send slot; the reduce kernel that follows it
+// raises this rank's flag in each peer's flag block (peer pointers opened through CUDA
+// IPC), waits until every peer's flag for the site is up and sums the ranks' slots in rank
+// order, reading the peers' over NVLink. Slots alternate by site parity, so a rank running
+// ahead never overwrites a slot a peer has not read yet. comm_peers_setup is collective; it returns false (on
+// every rank) when any peer cannot be opened, and the NCCL all-reduce stays in use.
+bool comm_peers_setup(ab_comm* c, size_t max_elems);
+void comm_peers_release(ab_comm* c);
+bool comm_has_peers(const ab_comm* c);
+void comm_begin_recording(ab_comm* c);
+void record_tp_epoch(ab_scheme* s, ab_comm* c);
+TpPush comm_push_target(ab_comm* c);
+void record_tp_reduce(ab_scheme* s, const char* label, ab_comm* c, const TpPush& push,
+                      float* x, uint32_t n);
 void record_allreduce_f32(ab_scheme* s, const char* label, ab_comm* c, const float* send,
                           float* recv, size_t count);
 void record_allgather_bytes(ab_scheme* s, const char* label, ab_comm* c, const void* send,
