@@ -370,19 +370,6 @@ __global__ void __launch_bounds__(kAttnThreads)
         pdl_trigger();
         return;
     }
-    if (tid == 0) {
-        for (uint32_t s = 0; s < S; s++) {
-            mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), 4);
-        }
-        fence_barrier_init();
-        sm_fail = 0;
-    }
-    const float qscale = 1.0f / sqrtf((float)hd);
-    const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * hd;
-    for (uint32_t i = tid; i < G * hd; i += kAttnThreads) qs[i] = qsrc[i] * qscale;
-    __syncthreads();
-
     const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
     const int32_t ybase = (int32_t)(b * p.seq + start);
     auto issue = [&](uint32_t i) {
@@ -399,8 +386,20 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
     };
     uint32_t issued = 0;  // meaningful in thread 0
-    if (tid == 0)
+    if (tid == 0) {
+        for (uint32_t s = 0; s < S; s++) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 4);
+        }
+        fence_barrier_init();
+        sm_fail = 0;
+        // the first tiles are in flight while q is staged
         for (; issued < ntiles && issued < S; issued++) issue(issued);
+    }
+    const float qscale = 1.0f / sqrtf((float)hd);
+    const float* qsrc = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G) * hd;
+    for (uint32_t i = tid; i < G * hd; i += kAttnThreads) qs[i] = qsrc[i] * qscale;
+    __syncthreads();
 
     const uint32_t pl = lane % 16, half = lane / 16, hh = hd / 2;
     float acc[G][4];
@@ -605,6 +604,23 @@ __global__ void __launch_bounds__(kAttnThreads)
         pdl_trigger();
         return;
     }
+    const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
+    const int32_t ybase = (int32_t)(b * p.seq + start);
+    auto issue = [&](uint32_t i) {
+        const uint32_t s = i % S;
+        const uint32_t bar = smem_u32(&full_bar[s]);
+        unsigned char* kst = smem + (size_t)s * LY::kStage;
+        unsigned char* vst = kst + LY::kStage / 2;
+        mbar_arrive_expect_tx(bar, LY::kStage);
+        const int32_t y = ybase + (int32_t)(i * kAttnTile);
+#pragma unroll
+        for (uint32_t j = 0; j < NBOX; j++) {
+            const int32_t x = (int32_t)(kvh * HD + j * 64);
+            tma_load_2d(smem_u32(kst + j * kAttnTile * 128), &kmap, x, y, bar);
+            tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
+        }
+    };
+    uint32_t issued = 0;  // meaningful in thread 0
     if (tid == 0) {
         for (uint32_t s = 0; s < S; s++) {
             mbar_init(smem_u32(&full_bar[s]), 1);
@@ -612,6 +628,8 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
         fence_barrier_init();
         sm_fail = 0;
+        // the first tiles are in flight while the Q fragments load
+        for (; issued < ntiles && issued < S; issued++) issue(issued);
     }
     // Q^T fragments (k = head dim, n = query head), pre-scaled, bf16 high + low parts
     uint32_t qh[KS][2], ql[KS][2];
@@ -633,26 +651,6 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
     }
     __syncthreads();
-
-    const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
-    const int32_t ybase = (int32_t)(b * p.seq + start);
-    auto issue = [&](uint32_t i) {
-        const uint32_t s = i % S;
-        const uint32_t bar = smem_u32(&full_bar[s]);
-        unsigned char* kst = smem + (size_t)s * LY::kStage;
-        unsigned char* vst = kst + LY::kStage / 2;
-        mbar_arrive_expect_tx(bar, LY::kStage);
-        const int32_t y = ybase + (int32_t)(i * kAttnTile);
-#pragma unroll
-        for (uint32_t j = 0; j < NBOX; j++) {
-            const int32_t x = (int32_t)(kvh * HD + j * 64);
-            tma_load_2d(smem_u32(kst + j * kAttnTile * 128), &kmap, x, y, bar);
-            tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
-        }
-    };
-    uint32_t issued = 0;  // meaningful in thread 0
-    if (tid == 0)
-        for (; issued < ntiles && issued < S; issued++) issue(issued);
 
     float o[KS][4];
 #pragma unroll
@@ -928,6 +926,19 @@ uint32_t attention_choose_splits(uint32_t batch, uint32_t kv_heads, uint32_t seq
     return (uint32_t)best;
 }
 
+// Smallest split, in positions (a multiple of the 64-position tile): 256 by default;
+// AMMON_B200_ATTN_MIN_CHUNK overrides it (a tuning parameter: the results do not change).
+uint32_t attention_min_chunk() {
+    static const uint32_t v = [] {
+        const char* e = std::getenv("AMMON_B200_ATTN_MIN_CHUNK");
+        long n = e ? std::atol(e) : 256;
+        if (n < kAttnTile) n = kAttnTile;
+        if (n > 1 << 20) n = 1 << 20;
+        return (uint32_t)(n / kAttnTile * kAttnTile);
+    }();
+    return v;
+}
+
 // Largest split count attention_choose_splits picks for any grid of up to `max_groups`
 // (batch, kv head) groups: the scratch bound of a block whose kv head count is not yet known.
 uint32_t attention_max_splits(uint32_t max_groups, uint32_t seq, int sm_count,
@@ -1129,8 +1140,7 @@ static AttnParams attention_decode_operands(ab_tensor q, ab_tensor key_cache,
     p.seq = seq;
     p.batch = batch;
     p.nsplit = attention_choose_splits(batch, kv_heads, seq, sms, 256);
-    // a split covers at least four tiles, whatever the position
-    p.min_chunk = 4 * kAttnTile;
+    p.min_chunk = attention_min_chunk();
     p.step = (const Step*)step.data;
     return p;
 }

@@ -379,9 +379,9 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         a.seq = blk->seq;
         a.batch = batch;
         a.nsplit = nsplit;
-        // a split covers at least four 64-position tiles: a split pays a partial write and
-        // a share of the fold, which shorter ones do not earn back
-        a.min_chunk = 256u;
+        // a split covers several 64-position tiles: a split pays a partial write and a
+        // share of the fold, which shorter ones do not earn back
+        a.min_chunk = attention_min_chunk();
         uint64_t floats = 0, counters = 0;
         attention_scratch_size(batch, heads, head, nsplit, &floats, &counters);
         a.part_o = blk->part;

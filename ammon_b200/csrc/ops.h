@@ -224,6 +224,7 @@ void attention_scratch_size(uint32_t batch, uint32_t heads, uint32_t head, uint3
                             uint64_t* floats, uint64_t* counters);
 uint32_t attention_choose_splits(uint32_t batch, uint32_t kv_heads, uint32_t seq, int sm_count,
                                  uint32_t max_splits);
+uint32_t attention_min_chunk();
 uint32_t attention_max_splits(uint32_t max_groups, uint32_t seq, int sm_count,
                               uint32_t max_splits);
 bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t kv_dtype);
