@@ -10,6 +10,8 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 CFG = dict(dim=128, layers=2, heads=4, kv_heads=2, head_dim=32, hidden=256, vocab=96, seq=32)
+# divisible over 4 and 8 ranks (heads, kv heads, FFN columns, vocab rows)
+CFG8 = dict(dim=256, layers=2, heads=16, kv_heads=8, head_dim=32, hidden=512, vocab=256, seq=32)
 TOKENS = [5, 90, 12, 12, 44, 3]
 
 
@@ -19,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, bf16, batch, out):
+def _worker(rank, world, port, bf16, batch, out, cfg=None):
     import datetime
 
     import torch
@@ -28,6 +30,7 @@ def _worker(rank, world, port, bf16, batch, out):
     import ammon_b200 as ab
     from oracle import oracle as orc
 
+    cfg_d = cfg or CFG
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
@@ -41,11 +44,11 @@ def _worker(rank, world, port, bf16, batch, out):
             uid.copy_(torch.frombuffer(bytearray(ab.Comm.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         comm = ab.Comm(rt, bytes(uid.cpu().numpy().tobytes()), rank, world)
-        cfg = ab.LlamaConfig(**CFG, batch=batch, rope_theta=500000.0,
+        cfg = ab.LlamaConfig(**cfg_d, batch=batch, rope_theta=500000.0,
                              dtype=ab.BF16 if bf16 else ab.F32)
         model = ab.LlamaModel(rt, cfg, comm)
         model.init_synthetic(17, 0.02)
-        ref = orc.Model(**CFG, theta=500000.0, bf16=bf16, seed=17)
+        ref = orc.Model(**cfg_d, theta=500000.0, bf16=bf16, seed=17)
         worst, same = 0.0, True
         for pos, tok in enumerate(TOKENS):
             logits, am = model.step_batch([tok] * batch, [pos] * batch, logits=True, argmax=True)
@@ -66,16 +69,17 @@ def _worker(rank, world, port, bf16, batch, out):
         dist.destroy_process_group()
 
 
-def _run(bf16, batch):
+def _run(bf16, batch, world=2, cfg=None):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, bf16, batch, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -84,7 +88,7 @@ def _run(bf16, batch):
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    return [q.get(timeout=5) for _ in range(2)]
+    return [q.get(timeout=5) for _ in range(world)]
 
 
 def test_tensor_parallel_fp32_matches_oracle():
@@ -96,4 +100,16 @@ def test_tensor_parallel_fp32_matches_oracle():
 def test_tensor_parallel_bf16_batched_matches_oracle():
     for rank, worst, same, agree in _run(True, 6):
         assert worst < 2e-2, (rank, worst)
+        assert same and agree
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tensor_parallel_wide_matches_oracle(world):
+    """Four or eight ranks (one kv head per rank at eight): the peer all-reduce with more
+    sources, at batch 1 (NVLink peer slots) and batch 6 (NCCL)."""
+    for rank, worst, same, agree in _run(False, 1, world, CFG8):
+        assert worst < 1e-5, (world, rank, worst)
+        assert same and agree
+    for rank, worst, same, agree in _run(True, 6, world, CFG8):
+        assert worst < 2e-2, (world, rank, worst)
         assert same and agree
