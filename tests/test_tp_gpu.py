@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 CFG = dict(dim=128, layers=2, heads=4, kv_heads=2, head_dim=32, hidden=256, vocab=96, seq=32)
 # divisible over 4 and 8 ranks (heads, kv heads, FFN columns, vocab rows)
-CFG8 = dict(dim=256, layers=2, heads=16, kv_heads=8, head_dim=32, hidden=512, vocab=256, seq=32)
+CFG8 = dict(dim=512, layers=2, heads=16, kv_heads=8, head_dim=32, hidden=1024, vocab=256, seq=32)
 TOKENS = [5, 90, 12, 12, 44, 3]
 
 
