@@ -53,6 +53,7 @@ struct GemvParams {
     uint32_t units;   // output pairs = ceil(n_rows / 2) (or rows of w1 for SwiGLU)
     uint32_t K;
     uint32_t nchunks;  // ceil(K / (32 * elements per 16 bytes))
+    uint32_t prefetch_chunks;  // 512-byte chunks of each first weight row prefetched into L2
     uint32_t nb;       // live batch rows in this launch
     // activations [nb, K]
     const void* x;
