@@ -565,6 +565,8 @@ __global__ void __launch_bounds__(256)
 // Grid (tiles, ceil(bn / 8)), 256 threads = 8 columns x 32 row quads.
 template <int EPI>
 __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const GemmTcParams p) {
+    // the GEMM lets this kernel launch before its epilogue stored the partials: wait for it
+    pdl_wait();
     const uint32_t tile = blockIdx.x;
     const uint32_t col = blockIdx.y * 8 + threadIdx.x / 32;
     const uint32_t quad = threadIdx.x % 32;
