@@ -323,7 +323,8 @@ __host__ __device__ inline AttnWarpLayout attn_warp_layout(uint32_t head, uint32
                                                            uint32_t nsplit) {
     AttnWarpLayout L;
     L.stage_bytes = 2u * kAttnTile * head * esz;
-    uint32_t st = (100u * 1024) / L.stage_bytes;
+    // about 64 KB of stages: three CTAs per SM at f32 head 64, whose splits are short
+    uint32_t st = (64u * 1024) / L.stage_bytes;
     L.stages = st < 2 ? 2 : st > kWarpMaxStages ? kWarpMaxStages : st;
     size_t o = (size_t)L.stages * L.stage_bytes;
     L.q_off = o;
@@ -341,7 +342,9 @@ __host__ __device__ inline AttnWarpLayout attn_warp_layout(uint32_t head, uint32
 template <typename KT, typename OT, int G, int SWZ>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_decode_warp_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
-                            const __grid_constant__ CUtensorMap vmap) {
+                            const __grid_constant__ CUtensorMap vmap,
+                            const __grid_constant__ CUtensorMap kmap16,
+                            const __grid_constant__ CUtensorMap vmap16) {
     constexpr uint32_t ESZ = sizeof(KT);
     constexpr uint32_t VE = 16 / ESZ;     // elements per 16-byte chunk
     constexpr uint32_t BOXE = SWZ / ESZ;  // elements per box row
@@ -377,12 +380,27 @@ __global__ void __launch_bounds__(kAttnThreads)
         const uint32_t bar = smem_u32(&full_bar[s]);
         unsigned char* kst = smem + (size_t)s * L.stage_bytes;
         unsigned char* vst = kst + L.stage_bytes / 2;
-        mbar_arrive_expect_tx(bar, L.stage_bytes);
         const int32_t y = ybase + (int32_t)(i * kAttnTile);
-        for (uint32_t j = 0; j < nbox; j++) {
-            const int32_t x = (int32_t)(kvh * hd + j * BOXE);
-            tma_load_2d(smem_u32(kst + (size_t)j * kAttnTile * SWZ), &kmap, x, y, bar);
-            tma_load_2d(smem_u32(vst + (size_t)j * kAttnTile * SWZ), &vmap, x, y, bar);
+        const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
+        if (rows == kAttnTile) {
+            mbar_arrive_expect_tx(bar, L.stage_bytes);
+            for (uint32_t j = 0; j < nbox; j++) {
+                const int32_t x = (int32_t)(kvh * hd + j * BOXE);
+                tma_load_2d(smem_u32(kst + (size_t)j * kAttnTile * SWZ), &kmap, x, y, bar);
+                tma_load_2d(smem_u32(vst + (size_t)j * kAttnTile * SWZ), &vmap, x, y, bar);
+            }
+        } else {
+            // the split's last tile: only the 16-row groups that hold positions
+            const uint32_t groups = (rows + 15) / 16;
+            mbar_arrive_expect_tx(bar, groups * 16 * 2 * hd * ESZ);
+            for (uint32_t q = 0; q < groups; q++) {
+                for (uint32_t j = 0; j < nbox; j++) {
+                    const int32_t x = (int32_t)(kvh * hd + j * BOXE);
+                    const size_t off = (size_t)j * kAttnTile * SWZ + (size_t)q * 16 * SWZ;
+                    tma_load_2d(smem_u32(kst + off), &kmap16, x, y + 16 * q, bar);
+                    tma_load_2d(smem_u32(vst + off), &vmap16, x, y + 16 * q, bar);
+                }
+            }
         }
     };
     uint32_t issued = 0;  // meaningful in thread 0
@@ -426,59 +444,62 @@ __global__ void __launch_bounds__(kAttnThreads)
         const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
         const unsigned char* kst = smem + (size_t)s * L.stage_bytes;
         const unsigned char* vst = kst + L.stage_bytes / 2;
-        // q.K: position 16 * warp + pl over half `half` of the head dims
-        const uint32_t row = warp * 16 + pl;
-        float d[G];
+        // a warp whose 16 positions all lie past the split's end has nothing in this tile
+        if (warp * 16 < rows) {
+            // q.K: position 16 * warp + pl over half `half` of the head dims
+            const uint32_t row = warp * 16 + pl;
+            float d[G];
 #pragma unroll
-        for (int h = 0; h < G; h++) d[h] = 0.0f;
-        for (uint32_t c = 0; c < hh / VE; c++) {
-            const uint32_t e0 = half * hh + c * VE;
-            const uint32_t byte = e0 * ESZ;
-            const uint32_t off =
-                swizzle_off<SWZ>((byte / SWZ) * kAttnTile * SWZ + row * SWZ + byte % SWZ);
-            float kf[VE];
-            unpack(*reinterpret_cast<const uint4*>(kst + off), kf, KT());
+            for (int h = 0; h < G; h++) d[h] = 0.0f;
+            for (uint32_t c = 0; c < hh / VE; c++) {
+                const uint32_t e0 = half * hh + c * VE;
+                const uint32_t byte = e0 * ESZ;
+                const uint32_t off =
+                    swizzle_off<SWZ>((byte / SWZ) * kAttnTile * SWZ + row * SWZ + byte % SWZ);
+                float kf[VE];
+                unpack(*reinterpret_cast<const uint4*>(kst + off), kf, KT());
+#pragma unroll
+                for (int h = 0; h < G; h++) {
+                    const float* qh = qs + h * hd + e0;
+#pragma unroll
+                    for (uint32_t e = 0; e < VE; e++) d[h] = fmaf(qh[e], kf[e], d[h]);
+                }
+            }
+            const bool valid = row < rows;
+            float e[G];
 #pragma unroll
             for (int h = 0; h < G; h++) {
-                const float* qh = qs + h * hd + e0;
+                // every lane takes part in the shuffle; invalid positions are masked after it
+                const float other = __shfl_xor_sync(0xffffffffu, d[h], 16);
+                const float sc = valid ? d[h] + other : -INFINITY;
+                float t = sc;
 #pragma unroll
-                for (uint32_t e = 0; e < VE; e++) d[h] = fmaf(qh[e], kf[e], d[h]);
+                for (int off = 1; off < 16; off <<= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, off));
+                const float n = fmaxf(m[h], t);
+                const float alpha = n == -INFINITY ? 1.0f : expf(m[h] - n);
+                e[h] = n == -INFINITY ? 0.0f : expf(sc - n);
+                m[h] = n;
+                lp[h] = lp[h] * alpha + e[h];
+#pragma unroll
+                for (int k = 0; k < 4; k++) acc[h][k] *= alpha;
             }
-        }
-        const bool valid = row < rows;
-        float e[G];
+            // P.V: lane owns dims lane + 32k; the weight of position q comes from lane q
+            for (uint32_t q = 0; q < 16; q++) {
+                const uint32_t vrow = warp * 16 + q;
+                float w[G];
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-            // every lane takes part in the shuffle; invalid positions are masked after it
-            const float other = __shfl_xor_sync(0xffffffffu, d[h], 16);
-            const float sc = valid ? d[h] + other : -INFINITY;
-            float t = sc;
+                for (int h = 0; h < G; h++) w[h] = __shfl_sync(0xffffffffu, e[h], q);
 #pragma unroll
-            for (int off = 1; off < 16; off <<= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, off));
-            const float n = fmaxf(m[h], t);
-            const float alpha = n == -INFINITY ? 1.0f : expf(m[h] - n);
-            e[h] = n == -INFINITY ? 0.0f : expf(sc - n);
-            m[h] = n;
-            lp[h] = lp[h] * alpha + e[h];
+                for (int k = 0; k < 4; k++) {
+                    const uint32_t dd = lane + 32 * k;
+                    if (dd < hd) {
+                        const uint32_t byte = dd * ESZ;
+                        const uint32_t off = swizzle_off<SWZ>((byte / SWZ) * kAttnTile * SWZ +
+                                                              vrow * SWZ + byte % SWZ);
+                        const float v = to_f32(*reinterpret_cast<const KT*>(vst + off));
 #pragma unroll
-            for (int k = 0; k < 4; k++) acc[h][k] *= alpha;
-        }
-        // P.V: lane owns dims lane + 32k; the weight of position q comes from lane q
-        for (uint32_t q = 0; q < 16; q++) {
-            const uint32_t vrow = warp * 16 + q;
-            float w[G];
-#pragma unroll
-            for (int h = 0; h < G; h++) w[h] = __shfl_sync(0xffffffffu, e[h], q);
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const uint32_t dd = lane + 32 * k;
-                if (dd < hd) {
-                    const uint32_t byte = dd * ESZ;
-                    const uint32_t off = swizzle_off<SWZ>((byte / SWZ) * kAttnTile * SWZ +
-                                                          vrow * SWZ + byte % SWZ);
-                    const float v = to_f32(*reinterpret_cast<const KT*>(vst + off));
-#pragma unroll
-                    for (int h = 0; h < G; h++) acc[h][k] = fmaf(w[h], v, acc[h][k]);
+                        for (int h = 0; h < G; h++) acc[h][k] = fmaf(w[h], v, acc[h][k]);
+                    }
                 }
             }
         }
@@ -578,7 +599,9 @@ struct AttnMmaLayout {
 template <typename OT, int G, int HD>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_decode_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
-                           const __grid_constant__ CUtensorMap vmap) {
+                           const __grid_constant__ CUtensorMap vmap,
+                           const __grid_constant__ CUtensorMap kmap16,
+                           const __grid_constant__ CUtensorMap vmap16) {
     using LY = AttnMmaLayout<HD>;
     constexpr uint32_t S = LY::kStages;
     constexpr uint32_t NBOX = LY::kRowBytes / 128;
@@ -611,13 +634,29 @@ __global__ void __launch_bounds__(kAttnThreads)
         const uint32_t bar = smem_u32(&full_bar[s]);
         unsigned char* kst = smem + (size_t)s * LY::kStage;
         unsigned char* vst = kst + LY::kStage / 2;
-        mbar_arrive_expect_tx(bar, LY::kStage);
         const int32_t y = ybase + (int32_t)(i * kAttnTile);
+        const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
+        if (rows == kAttnTile) {
+            mbar_arrive_expect_tx(bar, LY::kStage);
 #pragma unroll
-        for (uint32_t j = 0; j < NBOX; j++) {
-            const int32_t x = (int32_t)(kvh * HD + j * 64);
-            tma_load_2d(smem_u32(kst + j * kAttnTile * 128), &kmap, x, y, bar);
-            tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
+            for (uint32_t j = 0; j < NBOX; j++) {
+                const int32_t x = (int32_t)(kvh * HD + j * 64);
+                tma_load_2d(smem_u32(kst + j * kAttnTile * 128), &kmap, x, y, bar);
+                tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
+            }
+        } else {
+            // the split's last tile: only the 16-row groups that hold positions
+            const uint32_t groups = (rows + 15) / 16;
+            mbar_arrive_expect_tx(bar, groups * 16 * 2 * LY::kRowBytes);
+            for (uint32_t q = 0; q < groups; q++) {
+#pragma unroll
+                for (uint32_t j = 0; j < NBOX; j++) {
+                    const int32_t x = (int32_t)(kvh * HD + j * 64);
+                    const uint32_t off = j * kAttnTile * 128 + q * 16 * 128;
+                    tma_load_2d(smem_u32(kst + off), &kmap16, x, y + 16 * q, bar);
+                    tma_load_2d(smem_u32(vst + off), &vmap16, x, y + 16 * q, bar);
+                }
+            }
         }
     };
     uint32_t issued = 0;  // meaningful in thread 0
@@ -674,65 +713,68 @@ __global__ void __launch_bounds__(kAttnThreads)
         const uint32_t rows = min((uint32_t)kAttnTile, end - (start + i * kAttnTile));
         const uint32_t kst = smem_u32(smem + (size_t)s * LY::kStage);
         const uint32_t vst = kst + LY::kStage / 2;
-        // S for positions 16 * warp + (g, g + 8), heads (2t, 2t + 1)
-        float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        {
-            const uint32_t row = warp * 16 + (lane % 16);
+        // a warp whose 16 positions all lie past the split's end has nothing in this tile
+        if (warp * 16 < rows) {
+            // S for positions 16 * warp + (g, g + 8), heads (2t, 2t + 1)
+            float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            {
+                const uint32_t row = warp * 16 + (lane % 16);
 #pragma unroll
-            for (int ks = 0; ks < KS; ks++) {
-                const uint32_t colb = (ks % 4) * 32 + (lane / 16) * 16;
-                uint32_t a[4];
-                ldsm_x4(kst + swizzle_off<128>((ks / 4) * kAttnTile * 128 + row * 128 + colb), a);
-                mma_16816(sh, a, qh[ks][0], qh[ks][1]);
-                mma_16816(sl, a, ql[ks][0], ql[ks][1]);
+                for (int ks = 0; ks < KS; ks++) {
+                    const uint32_t colb = (ks % 4) * 32 + (lane / 16) * 16;
+                    uint32_t a[4];
+                    ldsm_x4(kst + swizzle_off<128>((ks / 4) * kAttnTile * 128 + row * 128 + colb), a);
+                    mma_16816(sh, a, qh[ks][0], qh[ks][1]);
+                    mma_16816(sl, a, ql[ks][0], ql[ks][1]);
+                }
             }
-        }
-        float sc[4] = {sh[0] + sl[0], sh[1] + sl[1], sh[2] + sl[2], sh[3] + sl[3]};
-        const uint32_t p0 = warp * 16 + g;
-        if (p0 >= rows) sc[0] = sc[1] = -INFINITY;
-        if (p0 + 8 >= rows) sc[2] = sc[3] = -INFINITY;
-        float ta = fmaxf(sc[0], sc[2]), tb = fmaxf(sc[1], sc[3]);
+            float sc[4] = {sh[0] + sl[0], sh[1] + sl[1], sh[2] + sl[2], sh[3] + sl[3]};
+            const uint32_t p0 = warp * 16 + g;
+            if (p0 >= rows) sc[0] = sc[1] = -INFINITY;
+            if (p0 + 8 >= rows) sc[2] = sc[3] = -INFINITY;
+            float ta = fmaxf(sc[0], sc[2]), tb = fmaxf(sc[1], sc[3]);
 #pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, off));
-            tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, off));
-        }
-        const float nA = fmaxf(mA, ta), nB = fmaxf(mB, tb);
-        // a warp whose positions were all masked so far keeps m = -inf and weight 0
-        const float aA = nA == -INFINITY ? 1.0f : expf(mA - nA);
-        const float aB = nB == -INFINITY ? 1.0f : expf(mB - nB);
-        const float e0 = nA == -INFINITY ? 0.0f : expf(sc[0] - nA);
-        const float e1 = nB == -INFINITY ? 0.0f : expf(sc[1] - nB);
-        const float e2 = nA == -INFINITY ? 0.0f : expf(sc[2] - nA);
-        const float e3 = nB == -INFINITY ? 0.0f : expf(sc[3] - nB);
-        mA = nA;
-        mB = nB;
-        lA = lA * aA + (e0 + e2);
-        lB = lB * aB + (e1 + e3);
+            for (int off = 4; off < 32; off <<= 1) {
+                ta = fmaxf(ta, __shfl_xor_sync(0xffffffffu, ta, off));
+                tb = fmaxf(tb, __shfl_xor_sync(0xffffffffu, tb, off));
+            }
+            const float nA = fmaxf(mA, ta), nB = fmaxf(mB, tb);
+            // a warp whose positions were all masked so far keeps m = -inf and weight 0
+            const float aA = nA == -INFINITY ? 1.0f : expf(mA - nA);
+            const float aB = nB == -INFINITY ? 1.0f : expf(mB - nB);
+            const float e0 = nA == -INFINITY ? 0.0f : expf(sc[0] - nA);
+            const float e1 = nB == -INFINITY ? 0.0f : expf(sc[1] - nB);
+            const float e2 = nA == -INFINITY ? 0.0f : expf(sc[2] - nA);
+            const float e3 = nB == -INFINITY ? 0.0f : expf(sc[3] - nB);
+            mA = nA;
+            mB = nB;
+            lA = lA * aA + (e0 + e2);
+            lB = lB * aB + (e1 + e3);
 #pragma unroll
-        for (int m = 0; m < KS; m++) {
-            o[m][0] *= aA;
-            o[m][1] *= aB;
-            o[m][2] *= aA;
-            o[m][3] *= aB;
-        }
-        // P^T fragments: the S accumulator holds (pos g / g + 8, heads 2t / 2t + 1); the
-        // transposed 8x8 blocks hold (head g, pos 2t / 2t + 1 and 8 + ...)
-        uint32_t h01, l01, h23, l23;
-        split_bf16x2(e0, e1, &h01, &l01);
-        split_bf16x2(e2, e3, &h23, &l23);
-        const uint32_t bh0 = movmatrix_trans(h01), bh1 = movmatrix_trans(h23);
-        const uint32_t bl0 = movmatrix_trans(l01), bl1 = movmatrix_trans(l23);
-        const uint32_t pos = warp * 16 + r8 + (mi >= 2 ? 8 : 0);
+            for (int m = 0; m < KS; m++) {
+                o[m][0] *= aA;
+                o[m][1] *= aB;
+                o[m][2] *= aA;
+                o[m][3] *= aB;
+            }
+            // P^T fragments: the S accumulator holds (pos g / g + 8, heads 2t / 2t + 1); the
+            // transposed 8x8 blocks hold (head g, pos 2t / 2t + 1 and 8 + ...)
+            uint32_t h01, l01, h23, l23;
+            split_bf16x2(e0, e1, &h01, &l01);
+            split_bf16x2(e2, e3, &h23, &l23);
+            const uint32_t bh0 = movmatrix_trans(h01), bh1 = movmatrix_trans(h23);
+            const uint32_t bl0 = movmatrix_trans(l01), bl1 = movmatrix_trans(l23);
+            const uint32_t pos = warp * 16 + r8 + (mi >= 2 ? 8 : 0);
 #pragma unroll
-        for (int m = 0; m < KS; m++) {
-            const uint32_t byte = (m * 16 + ((mi & 1) ? 8 : 0)) * 2;
-            uint32_t a[4];
-            ldsm_x4_t(vst + swizzle_off<128>((byte / 128) * kAttnTile * 128 + pos * 128 +
-                                             byte % 128),
-                      a);
-            mma_16816(o[m], a, bh0, bh1);
-            mma_16816(o[m], a, bl0, bl1);
+            for (int m = 0; m < KS; m++) {
+                const uint32_t byte = (m * 16 + ((mi & 1) ? 8 : 0)) * 2;
+                uint32_t a[4];
+                ldsm_x4_t(vst + swizzle_off<128>((byte / 128) * kAttnTile * 128 + pos * 128 +
+                                                 byte % 128),
+                          a);
+                mma_16816(o[m], a, bh0, bh1);
+                mma_16816(o[m], a, bl0, bl1);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
@@ -973,6 +1015,9 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
         const uint64_t rows = (uint64_t)p.batch * p.seq;
         encode_tmap_2d(&kmap, AB_BF16, p.kcache, inner, rows, inner * 2, 64, kAttnTile, 128);
         encode_tmap_2d(&vmap, AB_BF16, p.vcache, inner, rows, inner * 2, 64, kAttnTile, 128);
+        CUtensorMap kmap16, vmap16;  // 16-row boxes for a split's partial last tile
+        encode_tmap_2d(&kmap16, AB_BF16, p.kcache, inner, rows, inner * 2, 64, 16, 128);
+        encode_tmap_2d(&vmap16, AB_BF16, p.vcache, inner, rows, inner * 2, 64, 16, 128);
         const size_t smem = p.head == 128 ? AttnMmaLayout<128>::smem(G, p.nsplit)
                                           : AttnMmaLayout<64>::smem(G, p.nsplit);
         if (smem > 220 * 1024) invalid("attention: shared-memory stage too large");
@@ -981,14 +1026,16 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
-                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap, kmap16,
+                              vmap16);
             });
         } else {
             auto kern = attn_decode_mma_kernel<OT, G, 64>;
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
-                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap, kmap16,
+                              vmap16);
             });
         }
         return;
@@ -1001,6 +1048,11 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
                        swz / esz, kAttnTile, swz);
         encode_tmap_2d(&vmap, esz == 2 ? AB_BF16 : AB_F32, p.vcache, inner, rows, inner * esz,
                        swz / esz, kAttnTile, swz);
+        CUtensorMap kmap16, vmap16;  // 16-row boxes for a split's partial last tile
+        encode_tmap_2d(&kmap16, esz == 2 ? AB_BF16 : AB_F32, p.kcache, inner, rows, inner * esz,
+                       swz / esz, 16, swz);
+        encode_tmap_2d(&vmap16, esz == 2 ? AB_BF16 : AB_F32, p.vcache, inner, rows, inner * esz,
+                       swz / esz, 16, swz);
         const size_t smem = attn_warp_layout(p.head, esz, G, p.nsplit).total;
         if (smem > 220 * 1024) invalid("attention: shared-memory stage too large");
         if (swz == 128) {
@@ -1008,14 +1060,16 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
-                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap, kmap16,
+                              vmap16);
             });
         } else {
             auto kern = attn_decode_warp_kernel<KT, OT, G, 64>;
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
-                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+                return launch(st, grid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap, kmap16,
+                              vmap16);
             });
         }
         return;

@@ -111,15 +111,24 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def profile_traffic(kernel, workload):
-    """Per-launch DRAM bytes of `kernel` from a committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
-    try:
-        for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].strip().split()[0])
-    except OSError:
-        pass
+def profile_traffic(kernel, workload, algorithmic=None):
+    """Per-launch DRAM bytes of `kernel` from a committed ncu summary of this workload
+    (profiles/<kernel>*<workload>*.md, a `traffic_bytes_per_launch:` entry). When the summary
+    also states the capture's `algorithmic_bytes_per_launch:` (position-dependent launches,
+    e.g. attention), the traffic is scaled to this launch's algorithmic bytes."""
+    import glob
+    import re
+
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", f"{kernel}*{workload}*.md"))):
+        text = open(path).read()
+        m = re.search(r"traffic_bytes_per_launch:\s*\|?\s*([0-9.]+)", text)
+        if not m:
+            continue
+        traffic = float(m.group(1))
+        a = re.search(r"algorithmic_bytes_per_launch:\s*\|?\s*([0-9.]+)", text)
+        if a and algorithmic:
+            traffic *= algorithmic / float(a.group(1))
+        return traffic
     return None
 
 
@@ -677,7 +686,7 @@ def main():
                      "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,
                      "bytes_per_launch": lb.get(dom), "launch_ms": t_launch * 1e3,
-                     "traffic": profile_traffic(dom, args.workload)},
+                     "traffic": profile_traffic(dom, args.workload, lb.get(dom))},
         "kernels": {l: {"launches": c[0], "ms": round(c[1], 4),
                         "share": round(c[1] / total_ms, 4),
                         "gbs": round(lb[l] * c[0] / (c[1] / 1e3) / 1e9, 1) if l in lb else None}
