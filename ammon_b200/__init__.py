@@ -14,6 +14,7 @@ fallback: without the library, or without a GPU, calls raise.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 from typing import Iterable, List, Optional, Sequence
 
@@ -574,6 +575,39 @@ class LlamaModel:
         self.comm = comm
         self._logits = np.zeros((cfg.batch, cfg.vocab), np.float32)
         self._argmax = np.zeros(cfg.batch, np.int32)
+
+    @classmethod
+    def from_llama2c(cls, rt: Runtime, path: str, dtype: int = AB_F32, batch: int = 1,
+                     rope_theta: float = DEFAULT_ROPE_THETA,
+                     comm: Optional[Comm] = None) -> "LlamaModel":
+        """A model with the weights of a llama2.c checkpoint (run.c layout; the reference
+        leaves checkpoints to architecture crates, README.md:5,21). With ``comm`` every rank
+        loads its own shard from the same file."""
+        c = _abi.LlamaConfig_t()
+        h = C.c_void_p()
+        _check(_abi.lib().ab_llama_load_llama2c(
+            rt.handle, os.fsencode(path), dtype, batch, rope_theta,
+            comm.handle if comm is not None else None, C.byref(c), C.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        self.rt = rt
+        self.cfg = LlamaConfig(c.dim, c.layers, c.heads, c.kv_heads, c.head_dim, c.hidden,
+                               c.vocab, c.seq, c.batch, c.rope_theta, c.norm_eps, c.dtype)
+        self.comm = comm
+        self._logits = np.zeros((c.batch, c.vocab), np.float32)
+        self._argmax = np.zeros(c.batch, np.int32)
+        return self
+
+    @staticmethod
+    def llama2c_config(path: str, batch: int = 1, dtype: int = AB_F32,
+                       rope_theta: float = DEFAULT_ROPE_THETA) -> "LlamaConfig":
+        """The model shape a llama2.c checkpoint holds (header and file size checked; no
+        GPU needed)."""
+        c = _abi.LlamaConfig_t()
+        _check(_abi.lib().ab_llama2c_config(os.fsencode(path), batch, dtype, rope_theta,
+                                            C.byref(c)))
+        return LlamaConfig(c.dim, c.layers, c.heads, c.kv_heads, c.head_dim, c.hidden,
+                           c.vocab, c.seq, c.batch, c.rope_theta, c.norm_eps, c.dtype)
 
     @property
     def handle(self):

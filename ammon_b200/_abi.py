@@ -138,6 +138,10 @@ SIGNATURES = {
     "ab_comm_destroy": (C.c_int, [P]),
     "ab_comm_last_error": (C.c_char_p, []),
     "ab_llama_create_tp": (C.c_int, [P, C.POINTER(LlamaConfig_t), P, PP]),
+    "ab_llama2c_config": (C.c_int, [C.c_char_p, C.c_uint32, C.c_int32, C.c_float,
+                                    C.POINTER(LlamaConfig_t)]),
+    "ab_llama_load_llama2c": (C.c_int, [P, C.c_char_p, C.c_int32, C.c_uint32, C.c_float, P,
+                                        C.POINTER(LlamaConfig_t), PP]),
 }
 
 COMM_ID_BYTES = 128

@@ -322,6 +322,19 @@ const char* ab_comm_last_error(void);
 int ab_llama_create_tp(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm,
                        ab_llama** out);
 
+/* llama2.c checkpoint (no counterpart in the reference, which leaves checkpoints to
+ * architecture crates, README.md:5,21): seven int32 (dim, hidden_dim, n_layers, n_heads,
+ * n_kv_heads, vocab_size -- negative for a classifier of its own --, seq_len) then the fp32
+ * tensors of llama2.c's run.c layout. ab_llama2c_config reads and size-checks the header
+ * only (no GPU needed); ab_llama_load_llama2c creates the model (this rank's shard when
+ * comm is not NULL), converts the weights to `dtype` (AB_F32 or AB_BF16) and uploads them.
+ * cfg_out may be NULL. */
+int ab_llama2c_config(const char* path, uint32_t batch, int32_t dtype, float rope_theta,
+                      ab_llama_config* cfg);
+int ab_llama_load_llama2c(ab_runtime* rt, const char* path, int32_t dtype, uint32_t batch,
+                          float rope_theta, ab_comm* comm, ab_llama_config* cfg_out,
+                          ab_llama** out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

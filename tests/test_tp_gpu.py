@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, bf16, batch, out, cfg=None):
+def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None):
     import datetime
 
     import torch
@@ -46,8 +46,11 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None):
         comm = ab.Comm(rt, bytes(uid.cpu().numpy().tobytes()), rank, world)
         cfg = ab.LlamaConfig(**cfg_d, batch=batch, rope_theta=500000.0,
                              dtype=ab.BF16 if bf16 else ab.F32)
-        model = ab.LlamaModel(rt, cfg, comm)
-        model.init_synthetic(17, 0.02)
+        if ckpt:  # every rank loads its own shard of one llama2.c file
+            model = ab.LlamaModel.from_llama2c(rt, ckpt, cfg.dtype, batch, 500000.0, comm)
+        else:
+            model = ab.LlamaModel(rt, cfg, comm)
+            model.init_synthetic(17, 0.02)
         ref = orc.Model(**cfg_d, theta=500000.0, bf16=bf16, seed=17)
         worst, same = 0.0, True
         for pos, tok in enumerate(TOKENS):
@@ -69,7 +72,7 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None):
         dist.destroy_process_group()
 
 
-def _run(bf16, batch, world=2, cfg=None):
+def _run(bf16, batch, world=2, cfg=None, ckpt=None):
     import torch
     import torch.multiprocessing as mp
 
@@ -78,7 +81,7 @@ def _run(bf16, batch, world=2, cfg=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg, ckpt))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -112,4 +115,17 @@ def test_tensor_parallel_wide_matches_oracle(world):
         assert same and agree
     for rank, worst, same, agree in _run(True, 6, world, CFG8):
         assert worst < 2e-2, (world, rank, worst)
+        assert same and agree
+
+
+def test_tensor_parallel_llama2c_shards_match_oracle(tmp_path):
+    """Each rank slices its rows / columns out of one llama2.c checkpoint written with the
+    oracle's fp32 weights; the sharded decode matches the oracle's single-device model."""
+    from oracle import oracle as orc
+    from test_checkpoint import write_llama2c
+
+    path = str(tmp_path / "tp.bin")
+    write_llama2c(path, orc.Model(**CFG, theta=500000.0, seed=17).weight, CFG)
+    for rank, worst, same, agree in _run(False, 1, ckpt=path):
+        assert worst < 1e-5, (rank, worst)
         assert same and agree
