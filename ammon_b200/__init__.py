@@ -649,6 +649,42 @@ class LlamaModel:
         logits, _ = self.step_batch([token], [pos])
         return logits[0]
 
+    def prefill(self, tokens: Sequence[int], pos0: int = 0, stream: int = 0,
+                logits: bool = True):
+        """Runs prompt `tokens` of cache stream `stream` at positions pos0.. as batched
+        passes (each weight read once per pass); returns (last token's logits or None, its
+        greedy id). The cache ends as one step per token leaves it (src/generate.rs:60-66)."""
+        toks = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(self.cfg.vocab, np.float32) if logits else None
+        am = C.c_int32()
+        _check(_abi.lib().ab_llama_prefill(
+            self._h, int(stream), toks.ctypes.data_as(C.POINTER(C.c_int32)), toks.size,
+            int(pos0), out.ctypes.data_as(C.POINTER(C.c_float)) if logits else None,
+            C.byref(am)))
+        return out, int(am.value)
+
+    def set_prefill_rows(self, rows: int):
+        """Rows per prefill pass (1..256; 0 = the default 256)."""
+        _check(_abi.lib().ab_llama_prefill_rows(self._h, int(rows)))
+
+    def generate(self, prompt: Sequence[int], max_new_tokens: int,
+                 stop_on: Optional[int] = None) -> GenerateTokenOutput:
+        """generate_tokens (src/generate.rs:43-91) with the prompt prefilled in batched passes
+        and each new token picked by the device argmax (batch-1 model)."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        cap = max(int(max_new_tokens), 1)
+        out = np.zeros(cap, np.int32)
+        n = C.c_uint32()
+        tps = C.c_double()
+        _check(_abi.lib().ab_llama_generate_tokens(
+            self._h, prompt.ctypes.data_as(C.POINTER(C.c_int32)), prompt.size,
+            int(max_new_tokens), 0 if stop_on is None else 1,
+            0 if stop_on is None else int(stop_on), out.ctypes.data_as(C.POINTER(C.c_int32)),
+            cap, C.byref(n), C.byref(tps)))
+        return GenerateTokenOutput(tokens=out[:min(n.value, cap)].tolist(),
+                                   prompt_tokens=int(prompt.size),
+                                   tokens_per_second=float(tps.value))
+
     def decode_device(self, tokens: Sequence[int], positions: Sequence[int], steps: int,
                       want_tokens: bool = True):
         """Greedy decode of `steps` tokens entirely on the device, starting from one

@@ -126,6 +126,12 @@ SIGNATURES = {
                                 C.POINTER(i32)]),
     "ab_llama_decode_device": (C.c_int, [P, C.POINTER(DecodeStep_t), u32, u32,
                                          C.POINTER(i32)]),
+    "ab_llama_prefill": (C.c_int, [P, u32, C.POINTER(i32), u32, u32, C.POINTER(f32),
+                                   C.POINTER(i32)]),
+    "ab_llama_prefill_rows": (C.c_int, [P, u32]),
+    "ab_llama_generate_tokens": (C.c_int, [P, C.POINTER(i32), u32, u32, i32, i32,
+                                           C.POINTER(i32), u32, C.POINTER(u32),
+                                           C.POINTER(C.c_double)]),
     "ab_llama_scheme": (C.c_int, [P, PP]),
     "ab_llama_logits": (C.c_int, [P, C.POINTER(T)]),
     "ab_llama_reset": (C.c_int, [P]),

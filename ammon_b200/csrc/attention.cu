@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         return;
     }
     const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
-    const int32_t ybase = (int32_t)(b * p.seq + start);
+    const int32_t ybase = (int32_t)(b * p.cache_rows + start);
     auto issue = [&](uint32_t i) {
         const uint32_t s = i % S;
         const uint32_t bar = smem_u32(&full_bar[s]);
@@ -628,7 +628,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         return;
     }
     const uint32_t ntiles = (end - start + kAttnTile - 1) / kAttnTile;
-    const int32_t ybase = (int32_t)(b * p.seq + start);
+    const int32_t ybase = (int32_t)(b * p.cache_rows + start);
     auto issue = [&](uint32_t i) {
         const uint32_t s = i % S;
         const uint32_t bar = smem_u32(&full_bar[s]);
@@ -1012,7 +1012,7 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
         // bf16 K/V: both products on the tensor cores
         CUtensorMap kmap, vmap;
         const uint64_t inner = (uint64_t)p.kv_heads * p.head;
-        const uint64_t rows = (uint64_t)p.batch * p.seq;
+        const uint64_t rows = (uint64_t)(p.batch - 1) * p.cache_rows + p.seq;
         encode_tmap_2d(&kmap, AB_BF16, p.kcache, inner, rows, inner * 2, 64, kAttnTile, 128);
         encode_tmap_2d(&vmap, AB_BF16, p.vcache, inner, rows, inner * 2, 64, kAttnTile, 128);
         CUtensorMap kmap16, vmap16;  // 16-row boxes for a split's partial last tile
@@ -1043,7 +1043,7 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
     if (swz) {
         CUtensorMap kmap, vmap;
         const uint64_t inner = (uint64_t)p.kv_heads * p.head;
-        const uint64_t rows = (uint64_t)p.batch * p.seq;
+        const uint64_t rows = (uint64_t)(p.batch - 1) * p.cache_rows + p.seq;
         encode_tmap_2d(&kmap, esz == 2 ? AB_BF16 : AB_F32, p.kcache, inner, rows, inner * esz,
                        swz / esz, kAttnTile, swz);
         encode_tmap_2d(&vmap, esz == 2 ? AB_BF16 : AB_F32, p.vcache, inner, rows, inner * esz,
@@ -1098,6 +1098,13 @@ static void dispatch_g(ab_scheme* s, const char* label, const AttnParams& p) {
 void record_attention(ab_scheme* s, const char* label, AttnParams p) {
     if (!attention_fusable(p.heads, p.kv_heads, p.head, p.kv_dtype))
         invalid("attention: shape not supported by the fused kernel");
+    // the tiled loads address the cache as [(batch - 1) * cache_rows + seq] rows of
+    // kv_heads * head elements: cache_rows is seq for a cache per batch row, 0 when every
+    // row reads the same cache (consecutive positions of one sequence)
+    const uint64_t row = (uint64_t)p.kv_heads * p.head;
+    if (p.cache_stride % row || p.cache_stride / row > p.seq)
+        invalid("attention: the cache stride must be 0 or a whole number of positions <= seq");
+    p.cache_rows = (uint32_t)(p.cache_stride / row);
     if (p.kv_dtype == AB_BF16) {
         if (p.out_dtype == AB_BF16) dispatch_g<bf16, bf16>(s, label, p);
         else dispatch_g<bf16, float>(s, label, p);

@@ -299,12 +299,14 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         if (head > 128) invalid("attention: head size " + std::to_string(head) + " exceeds 128");
         if (kvd % head) invalid("attention: kv width must be a whole number of heads");
         const uint32_t kv_heads = kvd / head;
-        // cache views: [seq, kv, head] (batch 1) or [B, seq, kv, head]
+        // cache views: [B, seq, kv, head] (a cache per batch row) or [seq, kv, head] (one
+        // cache every row reads and appends to: at batch 1, or the consecutive positions of
+        // one sequence -- a prompt -- whose rows must then carry distinct positions)
         expect_data("key", key);
         expect_data("value", value);
         expect_float("key", key);
         expect_dtype("value", value, key.dtype);
-        const int cr = batch == 1 && key.rank == 3 ? 3 : 4;
+        const int cr = key.rank == 3 ? 3 : 4;
         expect_rank("key", key, cr);
         expect_rank("value", value, cr);
         const int o = cr - 3;
@@ -326,7 +328,7 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
             invalid("attention: fused path needs query_heads / kv_heads in {1, 2, 4, 8} and "
                     "head * element size a multiple of 16 bytes");
 
-        const uint64_t cache_stride = (uint64_t)blk->seq * kvd;
+        const uint64_t cache_stride = cr == 3 ? 0 : (uint64_t)blk->seq * kvd;
         const Step* st = (const Step*)step.data;
         uint32_t* flags = s->rt ? s->rt->flags : nullptr;
         const int32_t act = wdt;  // activation dtype feeding the projections

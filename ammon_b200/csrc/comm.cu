@@ -281,6 +281,10 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpSources srcs,
 
 void record_tp_reduce(ab_scheme* s, const char* label, ab_comm* c, const TpPush& push,
                       float* x, uint32_t n) {
+    if (n > c->max_elems)
+        fail(AB_ERR_ARGUMENT, "peer all-reduce of " + std::to_string(n) +
+                                  " elements exceeds the send slots set up for " +
+                                  std::to_string(c->max_elems));
     const uint32_t parity = push.site & 1;
     TpSources srcs = {};
     for (int r = 0; r < c->world; r++) {

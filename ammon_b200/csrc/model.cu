@@ -9,7 +9,9 @@
 // Under tensor parallelism (ab_llama_create_tp) every rank holds a shard: its query and kv
 // heads, its SwiGLU columns and its slice of the vocabulary; the residual stream and the
 // embedding table are replicated. The greedy pick merges every rank's best (value, id).
+#include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -155,6 +157,25 @@ struct ab_llama {
     int32_t* h_argmax = nullptr;
     ab_decode_step* h_steps = nullptr;
     std::vector<float> vt_logits;  // host logits handed out through the vtable
+    // Batched prefill: up to pf_rows prompt positions of one cache stream run as the rows
+    // of one pass (set up on the first prefill). Passes are recorded per (stream, rows,
+    // whether the classifier runs) and the most recently used few are kept.
+    struct PrefillScheme {
+        uint32_t stream, rows;
+        bool head;
+        ab_scheme* s;
+        uint64_t used;
+    };
+    uint32_t pf_rows = 0;
+    uint32_t pf_rows_wanted = 0;  // 0: the default
+    ab_attention_block* pf_attn = nullptr;
+    ab_swiglu_block* pf_ffn = nullptr;
+    ab_tensor pf_x = {}, pf_step = {}, pf_logits = {}, pf_argmax = {};
+    ab_tensor pf_logits_all = {}, pf_pairs = {}, pf_pairs_all = {};
+    std::vector<PrefillScheme> pf_schemes;
+    uint64_t pf_clock = 0;
+    ab_decode_step* h_pf_steps = nullptr;  // pinned [seq]
+    float* h_pf_logits = nullptr;          // pinned [vocab]
 };
 
 namespace {
@@ -176,6 +197,23 @@ void check(int status) {
     if (status != AB_OK) fail(status, ab_last_error());
 }
 
+void free_prefill(ab_llama* m) {
+    for (auto& e : m->pf_schemes) ab_scheme_destroy(e.s);
+    m->pf_schemes.clear();
+    if (m->pf_attn) ab_attention_block_destroy(m->pf_attn);
+    if (m->pf_ffn) ab_swiglu_block_destroy(m->pf_ffn);
+    m->pf_attn = nullptr;
+    m->pf_ffn = nullptr;
+    for (ab_tensor* t : {&m->pf_x, &m->pf_step, &m->pf_logits, &m->pf_argmax, &m->pf_logits_all,
+                         &m->pf_pairs, &m->pf_pairs_all})
+        free_t(*t);
+    if (m->h_pf_steps) cudaFreeHost(m->h_pf_steps);
+    if (m->h_pf_logits) cudaFreeHost(m->h_pf_logits);
+    m->h_pf_steps = nullptr;
+    m->h_pf_logits = nullptr;
+    m->pf_rows = 0;
+}
+
 void destroy_model(ab_llama* m) {
     if (!m) return;
     Runtime* rt = m->rt;
@@ -183,6 +221,7 @@ void destroy_model(ab_llama* m) {
         rt->activate();
         cudaStreamSynchronize(rt->stream);
     }
+    free_prefill(m);
     if (m->scheme) ab_scheme_destroy(m->scheme);
     if (m->loop_scheme) ab_scheme_destroy(m->loop_scheme);
     free_tc_scratch(&m->cls_tc);
@@ -201,60 +240,93 @@ void destroy_model(ab_llama* m) {
     delete m;
 }
 
-// Records the full decode step into `s`: with the device sample feedback (the device
-// loop) or, under tensor parallelism, with the logits gathered from every rank.
-void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
-    s->nodes.clear();
-    s->dirty = true;
-    const auto& c = m->c;
-    ab_tensor x = m->x;
-    if (c.batch == 1) {
-        x.rank = 1;
-        x.dims[0] = c.dim;
+// One cache stream's view [seq, kv_heads, head] of a layer's cache.
+ab_tensor stream_view(ab_tensor t, uint32_t stream) {
+    if (t.rank == 4) {
+        const uint64_t per = (uint64_t)t.dims[1] * t.dims[2] * t.dims[3];
+        t.data = (char*)t.data + stream * per * dtype_size(t.dtype);
+        t.rank = 3;
+        t.dims[0] = t.dims[1];
+        t.dims[1] = t.dims[2];
+        t.dims[2] = t.dims[3];
+        t.dims[3] = 0;
     }
+    return t;
+}
+
+// The embedding and every layer over the rows of x with the DecodeSteps of `step`. Each row
+// appends to and attends over its own cache stream, or, with stream >= 0, every row is a
+// position of that one stream (a prompt's consecutive positions).
+void record_layers(ab_llama* m, ab_scheme* s, ab_tensor x, ab_tensor step,
+                   ab_attention_block* attn, ab_swiglu_block* ffn, int64_t stream) {
+    const auto& c = m->c;
     if (m->comm && comm_has_peers(m->comm)) {
         // a new epoch per replay names this step's peer flags; sites count from zero
         comm_begin_recording(m->comm);
         record_tp_epoch(s, m->comm);
     }
-    check(ab_embedding_record(s, m->embed, m->step, x));
+    check(ab_embedding_record(s, m->embed, step, x));
     for (uint32_t l = 0; l < c.layers; l++) {
         ab_tensor key, value;
         check(ab_kvcache_layer(m->cache, l, &key, &value));
+        if (stream >= 0) {
+            key = stream_view(key, (uint32_t)stream);
+            value = stream_view(value, (uint32_t)stream);
+        }
         ab_attention_weights aw = {m->rms_att[l], m->wq[l], m->wk[l], m->wv[l], m->wo[l]};
-        check(ab_attention_block_record(m->attn, s, x, &aw, key, value, m->step));
+        check(ab_attention_block_record(attn, s, x, &aw, key, value, step));
         ab_swiglu_weights fw = {m->rms_ffn[l], m->w1[l], m->w3[l], m->w2[l]};
-        check(ab_swiglu_block_record(m->ffn, s, x, &fw));
+        check(ab_swiglu_block_record(ffn, s, x, &fw));
     }
-    // final RmsNorm fused into the classifier's prologue (this rank's vocabulary rows)
+}
+
+// Where the classifier and the greedy pick of `rows` residual rows leave their results:
+// logits [rows, vocab_l] and argmax [rows]; under tensor parallelism the ranks' (value, id)
+// candidates go through pairs / pairs_all and, when gathered, the logits into logits_all
+// [world, rows, vocab_l].
+struct HeadOut {
+    const float* x;
+    uint32_t rows;
+    float* logits;
+    int32_t* argmax;
+    ArgPair* pairs;
+    ArgPair* pairs_all;
+    void* logits_all;
+    const GemmScratch* tc;
+};
+
+// Final RmsNorm fused into the classifier's prologue (this rank's vocabulary rows), then the
+// device argmax (merged over the ranks under tensor parallelism).
+void record_head(ab_llama* m, ab_scheme* s, const HeadOut& h, bool gather_logits) {
+    const auto& c = m->c;
     GemvParams g = {};
     g.seg[0] = m->wcls.data;
     g.seg_rows[0] = m->vocab_l;
     g.n_rows = m->vocab_l;
     g.units = (m->vocab_l + 1) / 2;
     g.K = c.dim;
-    g.x = m->x.data;
+    g.x = h.x;
     g.x_dtype = AB_F32;
     g.x_stride = c.dim;
     g.norm_w = m->rms_final.data;
     g.norm_dtype = m->rms_final.dtype;
     g.eps = c.norm_eps;
-    g.out = m->logits.data;
+    g.out = h.logits;
     g.out_dtype = AB_F32;
     g.out_stride = m->vocab_l;
-    attach_tc_scratch(&g, m->cls_tc);
-    record_gemv(s, "final_norm_classifier", g, c.dtype, c.batch, kProNorm, kEpiStore);
-    const float* lg = (const float*)m->logits.data;
-    int32_t* am = (int32_t*)m->argmax.data;
-    const uint32_t batch = c.batch;
+    if (h.tc) attach_tc_scratch(&g, *h.tc);
+    record_gemv(s, "final_norm_classifier", g, c.dtype, h.rows, kProNorm, kEpiStore);
+    const float* lg = h.logits;
+    int32_t* am = h.argmax;
+    const uint32_t batch = h.rows;
     if (m->world == 1) {
         const uint32_t vocab = c.vocab;
         s->add("argmax", [=](cudaStream_t st) {
             return launch(st, dim3(batch), dim3(1024), 0, true, argmax_kernel, lg, vocab, am);
         });
     } else {
-        ArgPair* pr = (ArgPair*)m->pairs.data;
-        ArgPair* pa = (ArgPair*)m->pairs_all.data;
+        ArgPair* pr = h.pairs;
+        ArgPair* pa = h.pairs_all;
         const uint32_t vl = m->vocab_l, off = (uint32_t)m->rank * m->vocab_l;
         const uint32_t world = (uint32_t)m->world;
         s->add("argmax", [=](cudaStream_t st) {
@@ -266,9 +338,30 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
                           (const ArgPair*)pa, world, batch, am);
         });
         if (gather_logits)
-            record_allgather_bytes(s, "logits_allgather", m->comm, lg, m->logits_all.data,
+            record_allgather_bytes(s, "logits_allgather", m->comm, lg, h.logits_all,
                                    (size_t)batch * m->vocab_l * 4);
     }
+}
+
+// Records the full decode step into `s`: with the device sample feedback (the device
+// loop) or, under tensor parallelism, with the logits gathered from every rank.
+void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
+    s->nodes.clear();
+    s->dirty = true;
+    const auto& c = m->c;
+    ab_tensor x = m->x;
+    if (c.batch == 1) {
+        x.rank = 1;
+        x.dims[0] = c.dim;
+    }
+    record_layers(m, s, x, m->step, m->attn, m->ffn, -1);
+    const uint32_t batch = c.batch;
+    int32_t* am = (int32_t*)m->argmax.data;
+    record_head(m, s,
+                {(const float*)m->x.data, batch, (float*)m->logits.data, am,
+                 (ArgPair*)m->pairs.data, (ArgPair*)m->pairs_all.data, m->logits_all.data,
+                 &m->cls_tc},
+                gather_logits);
     if (feedback) {
         Step* stp = (Step*)m->step.data;
         int32_t* hist = (int32_t*)m->history.data;
@@ -279,6 +372,102 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
                           stp, hist, batch, seq, flags);
         });
     }
+}
+
+// Records one prefill pass of `rows` positions of cache stream `stream`; with `head` the
+// last row's logits and greedy id follow (the logits gathered over the ranks).
+void record_prefill(ab_llama* m, ab_scheme* s, uint32_t stream, uint32_t rows, bool head) {
+    s->nodes.clear();
+    s->dirty = true;
+    const auto& c = m->c;
+    ab_tensor x = m->pf_x;
+    if (rows == 1) {
+        x.rank = 1;
+        x.dims[0] = c.dim;
+    } else {
+        x.dims[0] = rows;
+    }
+    record_layers(m, s, x, m->pf_step, m->pf_attn, m->pf_ffn, stream);
+    if (head)
+        record_head(m, s,
+                    {(const float*)m->pf_x.data + (uint64_t)(rows - 1) * c.dim, 1,
+                     (float*)m->pf_logits.data, (int32_t*)m->pf_argmax.data,
+                     (ArgPair*)m->pf_pairs.data, (ArgPair*)m->pf_pairs_all.data,
+                     m->pf_logits_all.data, nullptr},
+                    true);
+}
+
+// Rows per prefill pass: 256 (the tensor-core GEMM's widest batch) unless the model or
+// AMMON_B200_PREFILL_ROWS asks for fewer; never more than seq_len.
+uint32_t prefill_rows(const ab_llama* m) {
+    long r = 256;
+    if (m->pf_rows_wanted) {
+        r = m->pf_rows_wanted;
+    } else if (const char* e = std::getenv("AMMON_B200_PREFILL_ROWS")) {
+        r = std::atol(e);
+    }
+    r = std::max(1L, std::min(r, 256L));
+    return (uint32_t)std::min<long>(r, m->c.seq);
+}
+
+void setup_prefill(ab_llama* m) {
+    const uint32_t rows = prefill_rows(m);
+    if (m->pf_rows == rows) return;
+    free_prefill(m);
+    const auto& c = m->c;
+    ab_runtime* rt = static_cast<ab_runtime*>(m->rt);
+    try {
+        m->pf_attn = attention_block_new(rt, c.dim, m->heads_l, c.head_dim, c.seq, rows,
+                                         c.rope_theta, m->comm);
+        m->pf_ffn = swiglu_block_new(rt, c.dim, m->hidden_l, rows, m->comm);
+        m->pf_x = alloc_t(rt, AB_F32, {rows, c.dim});
+        m->pf_logits = alloc_t(rt, AB_F32, {1, m->vocab_l});
+        m->pf_argmax = alloc_t(rt, AB_U32, {1});
+        if (m->world > 1) {
+            m->pf_logits_all = alloc_t(rt, AB_F32, {(uint32_t)m->world, 1, m->vocab_l});
+            m->pf_pairs = alloc_t(rt, AB_U32, {1, 2});
+            m->pf_pairs_all = alloc_t(rt, AB_U32, {(uint32_t)m->world, 1, 2});
+        }
+        check(ab_step_parcel(rt, rows, &m->pf_step));
+        cuda_check(cudaMallocHost(&m->h_pf_steps, (size_t)c.seq * sizeof(ab_decode_step)),
+                   "pinned prefill steps");
+        cuda_check(cudaMallocHost(&m->h_pf_logits, (size_t)c.vocab * 4), "pinned logits");
+    } catch (...) {
+        free_prefill(m);
+        throw;
+    }
+    m->pf_rows = rows;
+}
+
+// The recorded pass for (stream, rows, head), recording it on first use; the least
+// recently used pass is dropped beyond kPrefillSchemes.
+constexpr size_t kPrefillSchemes = 8;
+ab_scheme* prefill_scheme(ab_llama* m, uint32_t stream, uint32_t rows, bool head) {
+    m->pf_clock++;
+    for (auto& e : m->pf_schemes)
+        if (e.stream == stream && e.rows == rows && e.head == head) {
+            e.used = m->pf_clock;
+            return e.s;
+        }
+    if (m->pf_schemes.size() >= kPrefillSchemes) {
+        auto lru = std::min_element(
+            m->pf_schemes.begin(), m->pf_schemes.end(),
+            [](const ab_llama::PrefillScheme& a, const ab_llama::PrefillScheme& b) {
+                return a.used < b.used;
+            });
+        ab_scheme_destroy(lru->s);
+        m->pf_schemes.erase(lru);
+    }
+    ab_scheme* s = nullptr;
+    check(ab_scheme_create(static_cast<ab_runtime*>(m->rt), &s));
+    try {
+        record_prefill(m, s, stream, rows, head);
+    } catch (...) {
+        ab_scheme_destroy(s);
+        throw;
+    }
+    m->pf_schemes.push_back({stream, rows, head, s, m->pf_clock});
+    return s;
 }
 
 int vt_step(void* self, uint32_t token, uint32_t pos, const float** logits) {
@@ -333,9 +522,11 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
             m->w3.push_back(alloc_t(rt, dt, {m->hidden_l, c.dim}));
         }
         check(ab_kvcache_create(rt, c.layers, c.seq, m->kv_l, c.head_dim, dt, c.batch, &m->cache));
-        // NVLink peer slots for the per-block row all-reduce (collective; falls back to
-        // NCCL on every rank when a peer cannot be opened)
-        if (comm && world > 1) comm_peers_setup(comm, (size_t)c.batch * c.dim);
+        // NVLink peer slots for the per-block row all-reduce of up to the GEMV's batch rows,
+        // prefill passes included (collective; falls back to NCCL on every rank when a peer
+        // cannot be opened)
+        if (comm && world > 1)
+            comm_peers_setup(comm, (size_t)std::max(c.batch, kGemvMaxBatch) * c.dim);
         m->attn = attention_block_new(rt, c.dim, m->heads_l, c.head_dim, c.seq, c.batch,
                                       c.rope_theta, comm);
         m->ffn = swiglu_block_new(rt, c.dim, m->hidden_l, c.batch, comm);
@@ -590,6 +781,154 @@ int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n,
         }
         cuda_check(cudaStreamSynchronize(rt->stream), "decode synchronize");
         rt->check_flags();
+    });
+}
+
+int ab_llama_prefill_rows(ab_llama* m, uint32_t rows) {
+    return guard([&] {
+        if (!m) fail(AB_ERR_ARGUMENT, "null model");
+        if (rows > 256) fail(AB_ERR_ARGUMENT, "prefill passes take at most 256 rows");
+        m->pf_rows_wanted = rows;
+    });
+}
+
+}  // extern "C"
+
+namespace {
+
+// Runs positions [pos0, pos0 + n) of cache stream `stream` through prefill passes; the last
+// pass ends with the classifier and the greedy pick of its last row when `head`.
+void run_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n, uint32_t pos0,
+                 bool head) {
+    const auto& c = m->c;
+    Runtime* rt = m->rt;
+    rt->activate();
+    setup_prefill(m);
+    const uint32_t R = m->pf_rows;
+    // pinned steps for the whole prompt: each pass's copy reads its own slice
+    cuda_check(cudaStreamSynchronize(rt->stream), "prefill synchronize");
+    for (uint32_t i = 0; i < n; i++) m->h_pf_steps[i] = {(uint32_t)tokens[i], pos0 + i};
+    for (uint32_t done = 0; done < n;) {
+        const uint32_t rows = std::min(R, n - done);
+        const bool last = done + rows == n;
+        ab_scheme* s = prefill_scheme(m, stream, rows, head && last);
+        cuda_check(cudaMemcpyAsync(m->pf_step.data, m->h_pf_steps + done,
+                                   sizeof(ab_decode_step) * rows, cudaMemcpyHostToDevice,
+                                   rt->stream),
+                   "deposit prefill steps");
+        check(ab_scheme_submit(s));
+        done += rows;
+    }
+    (void)c;
+}
+
+void check_prompt(const ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n,
+                  uint32_t pos0) {
+    const auto& c = m->c;
+    if (stream >= c.batch)
+        fail(AB_ERR_ARGUMENT, "stream " + std::to_string(stream) + " out of range for batch " +
+                                  std::to_string(c.batch));
+    if (n == 0) fail(AB_ERR_ARGUMENT, "expected at least one prompt token");
+    if ((uint64_t)pos0 + n > c.seq)
+        fail(AB_ERR_ARGUMENT, "positions " + std::to_string(pos0) + " + " + std::to_string(n) +
+                                  " tokens pass max_seq_len " + std::to_string(c.seq));
+    for (uint32_t i = 0; i < n; i++)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= c.vocab)
+            fail(AB_ERR_ARGUMENT, "token " + std::to_string(tokens[i]) +
+                                      " out of range for vocab " + std::to_string(c.vocab));
+}
+
+// Reads back the prefill's last-row logits ([vocab], gathered over the ranks) and greedy id.
+void read_prefill_head(ab_llama* m, float* logits_host, int32_t* argmax_host) {
+    Runtime* rt = m->rt;
+    const size_t vl = m->vocab_l;
+    if (logits_host) {
+        const void* src = m->world > 1 ? m->pf_logits_all.data : m->pf_logits.data;
+        // gathered as [rank][1][vocab slice]: already the vocabulary order
+        cuda_check(cudaMemcpyAsync(m->h_pf_logits, src, (size_t)m->world * vl * 4,
+                                   cudaMemcpyDeviceToHost, rt->stream),
+                   "prefill logits readback");
+    }
+    int32_t am = 0;
+    if (argmax_host)
+        cuda_check(cudaMemcpyAsync(&am, m->pf_argmax.data, 4, cudaMemcpyDeviceToHost, rt->stream),
+                   "prefill argmax readback");
+    cuda_check(cudaStreamSynchronize(rt->stream), "prefill synchronize");
+    rt->check_flags();
+    if (logits_host) std::memcpy(logits_host, m->h_pf_logits, (size_t)m->c.vocab * 4);
+    if (argmax_host) *argmax_host = am;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ab_llama_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n,
+                     uint32_t pos0, float* logits_host, int32_t* argmax_host) {
+    return guard([&] {
+        if (!m || !tokens) fail(AB_ERR_ARGUMENT, "null argument");
+        check_prompt(m, stream, tokens, n, pos0);
+        run_prefill(m, stream, tokens, n, pos0, true);
+        read_prefill_head(m, logits_host, argmax_host);
+    });
+}
+
+int ab_llama_generate_tokens(ab_llama* m, const int32_t* prompt, uint32_t prompt_len,
+                             uint32_t max_new_tokens, int32_t has_stop, int32_t stop_on,
+                             int32_t* out_tokens, uint32_t cap, uint32_t* out_len,
+                             double* tokens_per_second) {
+    return guard([&] {
+        if (!m) fail(AB_ERR_ARGUMENT, "null model");
+        if (m->c.batch != 1) fail(AB_ERR_ARGUMENT, "generate_tokens needs a batch-1 model");
+        if (!prompt || prompt_len == 0) fail(AB_ERR_ARGUMENT, "expected at least one prompt token");
+        const auto& c = m->c;
+        // generate_tokens (src/generate.rs:43-91) steps through positions 0 .. limit - 1:
+        // prompt tokens are forced ids until the prompt runs out, then greedy picks; a next
+        // id equal to the stop id ends it before it is emitted.
+        const uint32_t cap_steps = std::min(max_new_tokens, c.seq);
+        const uint32_t limit = cap_steps > 0 ? cap_steps - 1 : 0;
+        const uint32_t S = std::min(prompt_len, limit);  // prompt positions stepped through
+        uint32_t k_stop = 0;  // first forced id equal to the stop id (0: none)
+        for (uint32_t k = 1; has_stop && k <= S && k < prompt_len; k++)
+            if (prompt[k] == stop_on) {
+                k_stop = k;
+                break;
+            }
+        const uint32_t P = k_stop ? k_stop : S;
+        const bool sample = !k_stop && S == prompt_len;  // the last prompt step picks the next id
+        uint32_t n = 0;
+        auto emit = [&](int32_t t) {
+            if (out_tokens && n < cap) out_tokens[n] = t;
+            n++;
+        };
+        double elapsed = 0.0;
+        uint32_t decoded = 0;
+        if (P > 0) {
+            check_prompt(m, 0, prompt, P, 0);
+            run_prefill(m, 0, prompt, P, 0, sample);
+            const uint32_t last_forced = k_stop ? k_stop - 1 : std::min(P, prompt_len - 1);
+            for (uint32_t k = 1; k <= last_forced; k++) emit(prompt[k]);
+            if (sample) {
+                int32_t next = 0;
+                read_prefill_head(m, nullptr, &next);
+                const auto start = std::chrono::steady_clock::now();
+                for (uint32_t pos = P;; pos++) {
+                    if (has_stop && next == stop_on) break;
+                    emit(next);
+                    if (pos >= limit) break;
+                    ab_decode_step st = {(uint32_t)next, pos};
+                    check(ab_llama_step(m, &st, 1, nullptr, &next));
+                    decoded++;
+                }
+                elapsed = std::chrono::duration<double>(std::chrono::steady_clock::now() - start)
+                              .count();
+            }
+            m->rt->activate();
+            cuda_check(cudaStreamSynchronize(m->rt->stream), "generate synchronize");
+            m->rt->check_flags();
+        }
+        if (out_len) *out_len = n;
+        if (tokens_per_second) *tokens_per_second = elapsed > 0.0 ? decoded / elapsed : 0.0;
     });
 }
 

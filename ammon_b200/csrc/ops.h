@@ -207,7 +207,8 @@ struct AttnParams {
     const void* kcache;  // [B, S, KV, hd]
     const void* vcache;
     int32_t kv_dtype;
-    uint64_t cache_stride;  // elements between batch rows of the cache
+    uint64_t cache_stride;  // elements between batch rows of the cache (0: rows share one)
+    uint32_t cache_rows;    // the same in positions (set by record_attention)
     void* out;              // [B, H * hd]
     int32_t out_dtype;
     uint32_t heads, kv_heads, head, seq, batch;

@@ -196,7 +196,10 @@ int ab_attention_block_create(ab_runtime* rt, uint32_t hidden, uint32_t query_he
                               ab_attention_block** out);
 /* CausalAttentionBlock::record (src/modules.rs:232-260; op order src/blocks.rs:178-259):
  * RMSNorm, Q/K/V, RoPE with the K/V append at step.position, split attention, output
- * projection and residual add into x. */
+ * projection and residual add into x. key/value are [B, seq, kv_heads, head] (a cache per
+ * row of x) or [seq, kv_heads, head]: one cache that every row appends to and attends over,
+ * so rows of x with distinct positions are consecutive tokens of one sequence (a prompt
+ * prefilled in one pass; each row attends over positions 0 .. its own). */
 int ab_attention_block_record(ab_attention_block* b, ab_scheme* s, ab_tensor x,
                               const ab_attention_weights* w, ab_tensor key, ab_tensor value,
                               ab_tensor step);
@@ -285,6 +288,26 @@ int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* l
  * advancing and raises AB_ERR_DEVICE at the end. */
 int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n, uint32_t steps,
                            int32_t* tokens_out);
+/* Batched prefill of one cache stream (batch row `stream`): the n tokens at positions
+ * pos0 .. pos0 + n - 1 run as the rows of passes of up to R rows, so each weight is read once
+ * per pass instead of once per token, where generate_tokens feeds a prompt one DecodeStep at
+ * a time (src/generate.rs:60-66). The K/V cache ends as that loop leaves it (within the
+ * arithmetic's rounding). logits_host (may be NULL) receives the last token's [vocab] logits,
+ * argmax_host (may be NULL) its greedy id. R is 256 unless set by ab_llama_prefill_rows (or
+ * AMMON_B200_PREFILL_ROWS) and at most seq_len. Under tensor parallelism every rank makes the
+ * same call. */
+int ab_llama_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n,
+                     uint32_t pos0, float* logits_host, int32_t* argmax_host);
+/* Rows per prefill pass (1..256; 0 = the default); takes effect at the next prefill. */
+int ab_llama_prefill_rows(ab_llama* m, uint32_t rows);
+/* generate_tokens (src/generate.rs:43-91) on a batch-1 model, same arguments and results as
+ * ab_generate_tokens, with the prompt run by ab_llama_prefill and each generated token by one
+ * step with the device argmax (4 bytes read back). tokens_per_second counts the generated
+ * tokens after the first (the prompt's pick) over the time from that pick on. */
+int ab_llama_generate_tokens(ab_llama* m, const int32_t* prompt, uint32_t prompt_len,
+                             uint32_t max_new_tokens, int32_t has_stop, int32_t stop_on,
+                             int32_t* out_tokens, uint32_t cap, uint32_t* out_len,
+                             double* tokens_per_second);
 /* The model's step scheme (recorded on first use), for profiling. */
 int ab_llama_scheme(ab_llama* m, ab_scheme** out);
 /* Device logits [batch, vocab] of the last step. */

@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None):
+def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=False):
     import datetime
 
     import torch
@@ -53,6 +53,26 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None):
             model.init_synthetic(17, 0.02)
         ref = orc.Model(**cfg_d, theta=500000.0, bf16=bf16, seed=17)
         worst, same = 0.0, True
+        if prefill:
+            # the prompt in one pass of 6 rows (NCCL all-reduce), then in passes of 2 (peer
+            # all-reduce) over the same positions; then decode continues from the cache
+            for want_pos, tok in enumerate(TOKENS):
+                want = ref.step(tok, want_pos)
+            for rows in (0, 2):
+                model.set_prefill_rows(rows)
+                logits, am = model.prefill(TOKENS)
+                worst = max(worst, float(np.abs(logits - want).max() / np.abs(want).max()))
+                same &= am == int(np.argmax(logits)) == orc.sample_argmax(want)
+            tok, start = am, len(TOKENS)
+            for pos in range(start, start + 3):
+                logits, am = model.step_batch([tok] * batch, [pos] * batch, logits=True,
+                                              argmax=True)
+                want = ref.step(tok, pos)
+                worst = max(worst, float(np.abs(logits[0] - want).max() / np.abs(want).max()))
+                same &= int(am[0]) == orc.sample_argmax(want)
+                tok = int(am[0])
+            out.put((rank, worst, same, True))
+            return
         for pos, tok in enumerate(TOKENS):
             logits, am = model.step_batch([tok] * batch, [pos] * batch, logits=True, argmax=True)
             want = ref.step(tok, pos)
@@ -72,7 +92,7 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None):
         dist.destroy_process_group()
 
 
-def _run(bf16, batch, world=2, cfg=None, ckpt=None):
+def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False):
     import torch
     import torch.multiprocessing as mp
 
@@ -81,7 +101,8 @@ def _run(bf16, batch, world=2, cfg=None, ckpt=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg, ckpt))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg, ckpt,
+                                                    prefill))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -129,3 +150,12 @@ def test_tensor_parallel_llama2c_shards_match_oracle(tmp_path):
     for rank, worst, same, agree in _run(False, 1, ckpt=path):
         assert worst < 1e-5, (rank, worst)
         assert same and agree
+
+
+def test_tensor_parallel_prefill_matches_oracle():
+    """Sharded prefill passes (row all-reduces through NCCL at 6 rows, over the NVLink peer
+    slots at 2) leave every rank with the oracle's last-token logits and a cache the decode
+    continues from."""
+    for rank, worst, same, _ in _run(False, 1, prefill=True):
+        assert worst < 1e-5, (rank, worst)
+        assert same
