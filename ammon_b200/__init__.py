@@ -663,6 +663,24 @@ class LlamaModel:
             C.byref(am)))
         return out, int(am.value)
 
+    def prefill_scheme(self, rows: int, stream: int = 0, head: bool = True) -> "Scheme":
+        """The recorded prefill pass of `rows` positions (profiling; owned by the model)."""
+        h = C.c_void_p()
+        _check(_abi.lib().ab_llama_prefill_scheme(self._h, int(stream), int(rows),
+                                                  1 if head else 0, C.byref(h)))
+        s = Scheme.__new__(Scheme)
+        s._h = h
+        s.rt = self.rt
+        s._keep = [self]
+        s.close = lambda: None
+        return s
+
+    def prefill_launches(self) -> int:
+        """Graph nodes (kernels and collectives) the last prefill launched."""
+        n = C.c_uint32()
+        _check(_abi.lib().ab_llama_prefill_launches(self._h, C.byref(n)))
+        return int(n.value)
+
     def set_prefill_rows(self, rows: int):
         """Rows per prefill pass (1..256; 0 = the default 256)."""
         _check(_abi.lib().ab_llama_prefill_rows(self._h, int(rows)))

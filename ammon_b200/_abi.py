@@ -129,6 +129,8 @@ SIGNATURES = {
     "ab_llama_prefill": (C.c_int, [P, u32, C.POINTER(i32), u32, u32, C.POINTER(f32),
                                    C.POINTER(i32)]),
     "ab_llama_prefill_rows": (C.c_int, [P, u32]),
+    "ab_llama_prefill_launches": (C.c_int, [P, C.POINTER(u32)]),
+    "ab_llama_prefill_scheme": (C.c_int, [P, u32, u32, i32, PP]),
     "ab_llama_generate_tokens": (C.c_int, [P, C.POINTER(i32), u32, u32, i32, i32,
                                            C.POINTER(i32), u32, C.POINTER(u32),
                                            C.POINTER(C.c_double)]),

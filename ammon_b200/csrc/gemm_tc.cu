@@ -25,6 +25,7 @@
 //  - Every mbarrier wait is bounded (%globaltimer); a wait that runs out raises the device
 //    flag, and the CTA still releases its TMEM.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -236,6 +237,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t kb0 = (uint32_t)((uint64_t)split * p.kblocks / p.ksplit);
     const uint32_t kb1 = (uint32_t)((uint64_t)(split + 1) * p.kblocks / p.ksplit);
     const uint32_t nk = kb1 - kb0;
+    // each tile walks its k-blocks from its own starting block, so the CTAs of a launch
+    // read different activation blocks at any moment instead of all the same L2 lines
+    const uint32_t rot = nk ? (tile * p.krot) % nk : 0;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < p.stages; s++) {
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 sm_ok = 0;
                 break;
             }
-            const int32_t kx = (int32_t)((kb0 + i) * kTcBK);
+            const int32_t kx = (int32_t)((kb0 + (i + rot) % nk) * kTcBK);
             const uint32_t bar = smem_u32(&full_bar[s]);
             const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
             mbar_arrive_expect_tx(bar, stage_bytes);
@@ -370,6 +374,9 @@ __global__ void __launch_bounds__(kTfThreads, 1)
     const uint32_t kb0 = (uint32_t)((uint64_t)split * p.kblocks / p.ksplit);
     const uint32_t kb1 = (uint32_t)((uint64_t)(split + 1) * p.kblocks / p.ksplit);
     const uint32_t nk = kb1 - kb0;
+    // each tile walks its k-blocks from its own starting block, so the CTAs of a launch
+    // read different activation blocks at any moment instead of all the same L2 lines
+    const uint32_t rot = nk ? (tile * p.krot) % nk : 0;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < p.stages; s++) {
@@ -397,7 +404,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
                 sm_ok = 0;
                 break;
             }
-            const int32_t kx = (int32_t)((kb0 + i) * kTfBK);
+            const int32_t kx = (int32_t)((kb0 + (i + rot) % nk) * kTfBK);
             const uint32_t bar = smem_u32(&full_bar[s]);
             const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
             const uint32_t b = a + 2 * a_bytes;
@@ -674,17 +681,39 @@ GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool
     pl.kblocks = K / (f32 ? kTfBK : kTcBK);
     // bf16: [W | X]; fp32: [W | W lo | X hi | X lo], 128 bytes per tile row
     const uint32_t stage_bytes = (kTcBM * 128 + pl.bn * 128) * (f32 ? 2 : 1);
-    const uint32_t per_sm = pl.bn <= 128 && 2 * stage_bytes <= 100u * 1024 ? 2 : 1;
-    const uint32_t budget = (per_sm == 2 ? 100u : 200u) * 1024;
-    pl.stages = std::max(2u, std::min((uint32_t)kTcMaxStages, budget / stage_bytes));
+    // two resident CTAs per SM where two stages each fit: one CTA's fill, epilogue and
+    // tail overlap the other's main loop, which measured faster than one CTA with a deeper
+    // ring at every batch width (128-row passes: 2 x 3 stages; 256: 2 x 2)
+    uint32_t per_sm = 2;
+    // tuning parameters (the results do not change): CTAs per SM and a stage cap
+    if (const char* e = std::getenv("AMMON_B200_GEMM_PER_SM")) {
+        const long v = std::atol(e);
+        if (v >= 1 && v <= 4) per_sm = (uint32_t)v;
+    }
+    uint32_t max_stages = kTcMaxStages;
+    if (const char* e = std::getenv("AMMON_B200_GEMM_STAGES")) {
+        const long v = std::atol(e);
+        if (v >= 2 && v <= kTcMaxStages) max_stages = (uint32_t)v;
+    }
+    // resident CTAs share 227 KB of shared memory (each also holds the 4 KB exchange buffer
+    // and 1 KB of alignment slack) and the 512 TMEM columns
+    uint32_t cols = 32;
+    while (cols < pl.bn) cols <<= 1;
+    while (per_sm > 1 && (per_sm * cols > 512 ||
+                          per_sm * (2 * stage_bytes + 6u * 1024) > 226u * 1024))
+        per_sm--;
+    const uint32_t budget = per_sm == 1 ? 200u * 1024 : 220u * 1024 / per_sm - 6u * 1024;
+    pl.stages = std::max(2u, std::min(max_stages, budget / stage_bytes));
     const uint32_t target = (uint32_t)std::max(sms, 1) * per_sm;
     uint32_t ks = (target + pl.tiles / 2) / std::max(pl.tiles, 1u);
     // fp32 k-blocks carry three MMAs each: two of them per split still hide the fill
     ks = std::min(ks, std::max(1u, pl.kblocks / (f32 ? 2 : 4)));
     pl.ksplit = std::max(1u, ks);
+    // stagger of the tiles' first k-block (0 walks every tile from its first block; a
+    // tuning parameter: the fp32 sums keep their per-tile order, in a rotated sequence)
+    pl.krot = 7;
+    if (const char* e = std::getenv("AMMON_B200_GEMM_ROTATE")) pl.krot = (uint32_t)std::atol(e);
     pl.smem = (size_t)pl.stages * stage_bytes + 16 * 64 * 4 + 1024;
-    uint32_t cols = 32;
-    while (cols < pl.bn) cols <<= 1;
     pl.tmem_cols = cols;
     pl.ws_floats = pl.ksplit > 1 ? (uint64_t)pl.ksplit * pl.tiles * pl.bn * kTcBM : 0;
     return pl;
@@ -694,7 +723,7 @@ void gemm_tc_scratch(uint32_t max_tiles, uint32_t max_batch, int sms, uint64_t* 
                      uint32_t* tickets) {
     // ksplit <= round(target / tiles) keeps ksplit * tiles <= target + tiles
     const uint32_t bn = std::max(16u, (max_batch + 15) / 16 * 16);
-    const uint64_t target = (uint64_t)std::max(sms, 1) * 2;
+    const uint64_t target = (uint64_t)std::max(sms, 1) * 4;  // up to 4 resident CTAs per SM
     *ws_floats = (target + max_tiles) * (uint64_t)std::min(bn, 256u) * kTcBM;
     *tickets = max_tiles;
 }
@@ -791,6 +820,7 @@ void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, int32_t wdt
     p.ksplit = pl.ksplit;
     p.stages = pl.stages;
     p.tmem_cols = pl.tmem_cols;
+    p.krot = pl.krot;
     if (pl.ws_floats > p.ws_floats || (pl.ksplit > 1 && p.tickets_n < pl.tiles))
         fail(AB_ERR_ARGUMENT, std::string(label) + ": GEMM workspace too small");
     const int32_t dt = f32 ? AB_F32 : AB_BF16;

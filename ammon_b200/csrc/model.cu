@@ -174,6 +174,7 @@ struct ab_llama {
     ab_tensor pf_logits_all = {}, pf_pairs = {}, pf_pairs_all = {};
     std::vector<PrefillScheme> pf_schemes;
     uint64_t pf_clock = 0;
+    uint32_t pf_launches = 0;              // kernels and collectives of the last prefill
     ab_decode_step* h_pf_steps = nullptr;  // pinned [seq]
     float* h_pf_logits = nullptr;          // pinned [vocab]
 };
@@ -784,6 +785,26 @@ int ab_llama_decode_device(ab_llama* m, const ab_decode_step* start, uint32_t n,
     });
 }
 
+int ab_llama_prefill_scheme(ab_llama* m, uint32_t stream, uint32_t rows, int32_t head,
+                            ab_scheme** out) {
+    return guard([&] {
+        if (!m || !out) fail(AB_ERR_ARGUMENT, "null argument");
+        if (stream >= m->c.batch) fail(AB_ERR_ARGUMENT, "stream out of range");
+        m->rt->activate();
+        setup_prefill(m);
+        if (rows == 0 || rows > m->pf_rows)
+            fail(AB_ERR_ARGUMENT, "rows must be 1.." + std::to_string(m->pf_rows));
+        *out = prefill_scheme(m, stream, rows, head != 0);
+    });
+}
+
+int ab_llama_prefill_launches(const ab_llama* m, uint32_t* out) {
+    return guard([&] {
+        if (!m || !out) fail(AB_ERR_ARGUMENT, "null argument");
+        *out = m->pf_launches;
+    });
+}
+
 int ab_llama_prefill_rows(ab_llama* m, uint32_t rows) {
     return guard([&] {
         if (!m) fail(AB_ERR_ARGUMENT, "null model");
@@ -808,6 +829,7 @@ void run_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n
     // pinned steps for the whole prompt: each pass's copy reads its own slice
     cuda_check(cudaStreamSynchronize(rt->stream), "prefill synchronize");
     for (uint32_t i = 0; i < n; i++) m->h_pf_steps[i] = {(uint32_t)tokens[i], pos0 + i};
+    m->pf_launches = 0;
     for (uint32_t done = 0; done < n;) {
         const uint32_t rows = std::min(R, n - done);
         const bool last = done + rows == n;
@@ -817,6 +839,7 @@ void run_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n
                                    rt->stream),
                    "deposit prefill steps");
         check(ab_scheme_submit(s));
+        m->pf_launches += (uint32_t)s->nodes.size();
         done += rows;
     }
     (void)c;

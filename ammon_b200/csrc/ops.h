@@ -94,6 +94,7 @@ constexpr uint32_t kGemvMaxBatch = 4;
 // Parameters of one tensor-core GEMM launch (gemm_tc.cu).
 struct GemmTcParams {
     uint32_t K, nb, bn, tiles, kblocks, ksplit, stages, tmem_cols;
+    uint32_t krot;  // tile t starts at k-block (t * krot) mod its k-blocks
     uint32_t seg_tiles[3];
     int32_t interleave;  // tile t = rows [64t, 64t + 64) of segment 0, then of segment 1
     float* ws;
@@ -118,7 +119,7 @@ struct GemmTcParams {
 };
 
 struct GemmTcPlan {
-    uint32_t bn, tiles, kblocks, ksplit, stages, tmem_cols;
+    uint32_t bn, tiles, kblocks, ksplit, stages, tmem_cols, krot;
     size_t smem;
     uint64_t ws_floats;
 };

@@ -57,6 +57,8 @@ MICRO = {
     "ops": "Per-op microbench: RmsNorm rows {1,64,4096} x dim {4096,8192}, RoPE 32x128 at "
            "positions 0-8191 (theta 500000), SwiGLU rows {1,64} x 14336, embedding gather "
            "from 128256 x 4096; N(0,1) activations in f32 and bf16",
+    "prefill": "Batched prefill of one stream on the Llama-3-8B-shaped bf16 model: a uniform "
+               "prompt (seed 3) in passes of up to 256 rows, last token's logits read back",
     "attention": "Split attention decode: 32 query / 8 kv heads, head_dim 128, bf16 K/V, fp32 "
                  "accumulation; context {4096,32768,131072} x batch {1,8,64}; N(0,1) seed 2",
 }
@@ -459,6 +461,129 @@ def run_attention_micro(args):
     rt.close()
 
 
+def prefill_flops(w, P):
+    """Algorithmic FLOPs of prefilling P positions from 0: every projection once per
+    position (2 x weights), attention over positions 0..p for each p (QK and PV: 4 x heads x
+    head_dim per position attended), and the classifier for the last position only."""
+    d, F, V = w["dim"], w["hidden"], w["vocab"]
+    qd, kvd = w["heads"] * w["head_dim"], w["kv_heads"] * w["head_dim"]
+    per_layer = d * (qd + 2 * kvd) + qd * d + 3 * d * F
+    attn = 4 * qd * P * (P + 1) // 2
+    return w["layers"] * (2 * P * per_layer + attn) + 2 * V * d
+
+
+def run_prefill_micro(args):
+    import numpy as np
+    import torch
+
+    import ammon_b200 as ab
+
+    w = dict(WORKLOADS["llama3-8b-bf16"])
+    if args.layers:  # profiling aid, as for the decode workloads
+        w["layers"] = args.layers
+    if args.seq:
+        w["seq"] = args.seq
+    P = args.prompt_len
+    torch.cuda.set_device(0)
+    rt = ab.create_runtime(0)
+    cfg = ab.LlamaConfig(w["dim"], w["layers"], w["heads"], w["kv_heads"], w["head_dim"],
+                         w["hidden"], w["vocab"], w["seq"], batch=1, rope_theta=w["theta"],
+                         dtype=ab.BF16)
+    g = ab.LlamaModel(rt, cfg)
+    g.init_synthetic(w["seed"], 0.02)
+    prompt = prompt_tokens(w["seed"], 0, P, 0, w["vocab"])
+    ext = torch.cuda.ExternalStream(rt.stream)
+    for _ in range(args.warmup):
+        g.prefill(prompt)
+    dev_ms, e2e_s = [], []
+    with ClockSampler(0) as clocks:
+        for _ in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(ext)
+            t0 = time.perf_counter()
+            logits, am = g.prefill(prompt)
+            t1 = time.perf_counter()
+            e1.record(ext)
+            torch.cuda.synchronize()
+            dev_ms.append(e0.elapsed_time(e1))
+            e2e_s.append(t1 - t0)
+    ms = statistics.median(dev_ms)
+    launches = g.prefill_launches()
+    if args.no_parity:
+        print(json.dumps({"workload": "prefill", "tokens_per_s": P / ms * 1e3,
+                          "launches": launches}), flush=True)
+        g.close()
+        rt.close()
+        return
+    # the reference's way on the same kernels: one decode step per prompt token
+    loop_n = 32
+    rt.synchronize()
+    t0 = time.perf_counter()
+    for pos in range(loop_n):
+        g.step_batch([prompt[pos]], [pos], logits=False)
+    loop_tps = loop_n / (time.perf_counter() - t0)
+    # parity on a 256-token prompt: prefill against that token loop (bf16 rounding points
+    # differ between the GEMM and GEMV paths: the bf16 bar applies)
+    n_chk = 256
+    want = None
+    for pos in range(n_chk):
+        want, _ = g.step_batch([prompt[pos]], [pos], logits=True)
+    want = want[0].copy()
+    got, _ = g.prefill(prompt[:n_chk])
+    err = float(np.abs(got - want).max() / np.abs(want).max())
+    l2err = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    flops = prefill_flops(w, P)
+    peak = 1341.5
+    peak_kind = "fallback"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops_sustained"])
+            peak_kind = "measured (sustained)"
+    except Exception:
+        pass
+    achieved = flops / (ms / 1e3) / 1e12
+    passes = (P + 255) // 256
+    line = {
+        "metric": "prefill prompt tokens/s (one stream, batched passes)", "value": P / ms * 1e3,
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": MICRO["prefill"] + (f" ({w['layers']} layers: profiling case)"
+                                                   if args.layers else ""),
+                   "prompt": P, "rows_per_pass": 256,
+                   "passes": passes, "l2": "weights (15 GB) exceed L2 every pass"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "flops_per_prefill": flops, "traffic": None},
+        "e2e": {"value": P / statistics.median(e2e_s), "unit": "tokens/s",
+                "h2d_bytes_per_step": P * 8, "d2h_bytes_per_step": w["vocab"] * 4 + 4},
+        "token_loop": {"value": loop_tps, "unit": "tokens/s",
+                       "what": "the same model fed one DecodeStep per prompt token "
+                               "(src/generate.rs:60-66), logits not read back"},
+        "parity": {"max_rel_err_vs_token_loop": err, "rel_l2_err_vs_token_loop": l2err,
+                   "greedy_id_equal": bool(int(np.argmax(got)) == int(np.argmax(want))),
+                   "tolerance": 4e-2, "prompt": n_chk,
+                   "note": "two bf16 paths (GEMM passes vs GEMV steps), each held to 2e-2 "
+                           "against the oracle by the tests: their difference is bounded by "
+                           "twice that"},
+        "clocks": clocks.summary(),
+        "gpu_launches": launches * args.steps,
+    }
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        pos = [0, P // 4, P // 2, 3 * P // 4, P - 1]
+        per_token, _ = cpu_sample(w, 1, pos, threads)
+        line["cpu_baseline"] = {
+            "value": 1.0 / statistics.mean(per_token), "unit": "tokens/s", "cores": threads,
+            "kind": "port", "sample": "the reference feeds a prompt one decode step per token: "
+                                      "one decoder layer x layers + classifier slice at "
+                                      f"positions {pos}"}
+    print(json.dumps(line), flush=True)
+    g.close()
+    rt.close()
+
+
 def run_reference(args, w, rank, world):
     if rank != 0:
         return
@@ -495,6 +620,10 @@ def main():
                     sorted(MICRO))
     ap.add_argument("--contexts", default="4096,32768,131072", help="attention microbench")
     ap.add_argument("--batches", default="1,8,64", help="attention microbench")
+    ap.add_argument("--prompt-len", type=int, default=2048, help="prefill microbench")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="profiling aid: prefill microbench without the token-loop comparison "
+                         "(prints a short line, not a bench line)")
     ap.add_argument("--batch", type=int, default=0,
                     help="streams per rank (default: the workload's; the 110M workload's 256 "
                          "streams are split over the ranks)")
@@ -518,7 +647,8 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "kernel microbenchmarks "
                               "report the oracle's CPU rate as cpu_baseline in the main arm"}))
             return
-        (run_ops_micro if args.workload == "ops" else run_attention_micro)(args)
+        {"ops": run_ops_micro, "attention": run_attention_micro,
+         "prefill": run_prefill_micro}[args.workload](args)
         return
     w = dict(WORKLOADS[args.workload])
     if args.layers:

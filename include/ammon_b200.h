@@ -300,6 +300,13 @@ int ab_llama_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32
                      uint32_t pos0, float* logits_host, int32_t* argmax_host);
 /* Rows per prefill pass (1..256; 0 = the default); takes effect at the next prefill. */
 int ab_llama_prefill_rows(ab_llama* m, uint32_t rows);
+/* The recorded prefill pass of `rows` positions of `stream` (with the classifier when head
+ * is non-zero), for profiling: it reads the DecodeSteps the last prefill deposited. Owned by
+ * the model; a later prefill may drop it. */
+int ab_llama_prefill_scheme(ab_llama* m, uint32_t stream, uint32_t rows, int32_t head,
+                            ab_scheme** out);
+/* Graph nodes (kernels and collectives) the last prefill launched over all its passes. */
+int ab_llama_prefill_launches(const ab_llama* m, uint32_t* out);
 /* generate_tokens (src/generate.rs:43-91) on a batch-1 model, same arguments and results as
  * ab_generate_tokens, with the prompt run by ab_llama_prefill and each generated token by one
  * step with the device argmax (4 bytes read back). tokens_per_second counts the generated

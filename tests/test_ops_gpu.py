@@ -148,6 +148,44 @@ def test_fused_attention_entry_matches_float64(rt, orc, kv_bf16, hd, heads, kv_h
     s.close()
 
 
+@pytest.mark.parametrize("kv_bf16,hd,heads,kv_heads,rows,p0", [
+    (True, 128, 32, 8, 100, 317),   # the prompt kernel (64 queries per K/V tile), G = 4
+    (True, 64, 8, 8, 70, 0),        # G = 1, positions from 0
+    (True, 128, 16, 2, 16, 50),     # G = 8, the smallest batch the prompt kernel takes
+    (True, 64, 8, 4, 9, 200),       # fewer rows: the split decode kernel over one cache
+    (False, 64, 8, 2, 40, 90),      # f32 K/V: the warp kernel over one cache
+])
+def test_fused_attention_shared_cache_matches_float64(rt, orc, kv_bf16, hd, heads, kv_heads,
+                                                      rows, p0):
+    """Rows that are consecutive positions of one sequence, over one [seq, kv, head] cache:
+    row b attends over positions 0 .. p0 + b (causal), against float64."""
+    seq = p0 + rows + 37
+    q_host = orc.normal(rows * heads * hd, 8, 1, 0.0, 1.0).reshape(rows, heads, hd)
+    k_f = orc.normal(seq * kv_heads * hd, 8, 2, 0.0, 1.0).reshape(seq, kv_heads, hd)
+    v_f = orc.normal(seq * kv_heads * hd, 8, 3, 0.0, 1.0).reshape(seq, kv_heads, hd)
+    if kv_bf16:
+        k_f, v_f = orc.round_bf16(k_f), orc.round_bf16(v_f)
+        kc = ab.Tensor.from_array(rt, orc.to_bf16_bits(k_f).reshape(k_f.shape), ab.BF16)
+        vc = ab.Tensor.from_array(rt, orc.to_bf16_bits(v_f).reshape(v_f.shape), ab.BF16)
+    else:
+        kc, vc = ab.Tensor.from_array(rt, k_f), ab.Tensor.from_array(rt, v_f)
+    q = ab.Tensor.from_array(rt, q_host)
+    for out_dt in (ab.F32, ab.BF16):
+        out = ab.Tensor.zeros(rt, (rows, heads * hd), out_dt)
+        s = rt.scheme()
+        K.AttentionDecodeKernel.prepare(rt).record(s, "attn", q, kc, vc, out,
+                                                   steps(rt, [(0, p0 + b) for b in range(rows)]))
+        s.submit()
+        got = (out.read_f32() if out_dt == ab.BF16 else out.read()).reshape(rows, heads, hd)
+        worst = 0.0
+        for b in range(rows):
+            want = _attention_ref(q_host[b], k_f, v_f, p0 + b, kv_heads)
+            worst = max(worst, float(np.abs(got[b] - want).max() / np.abs(want).max()))
+        tol = 1e-2 if out_dt == ab.BF16 else (1e-4 if kv_bf16 else 1e-5)
+        assert worst < tol, (out_dt, worst)
+        s.close()
+
+
 def test_fused_attention_entry_validation(rt):
     q = ab.Tensor.zeros(rt, (2, 3, 64))
     kc = ab.Tensor.zeros(rt, (2, 16, 1, 64))
