@@ -24,7 +24,7 @@ from . import _abi
 from ._abi import AB_BF16, AB_F32, AB_U32
 from .generate import (AutoregressiveModel, GenerateOptions, GenerateOutput,
                        GenerateTokenOutput, generate, generate_tokens)
-from .tokenizer import BpeTokenizer, Tokenizer, sample_argmax
+from .tokenizer import BpeTokenizer, NativeBpeTokenizer, Tokenizer, sample_argmax
 
 DEFAULT_ROPE_THETA = 10000.0  # src/kernels.rs:8
 ATTENTION_SPLIT = 8           # src/kernels.rs:229
@@ -803,6 +803,7 @@ __all__ = [
     "CausalAttentionBlock", "CausalAttentionBlockWeights", "SwiGluBlock",
     "SwiGluBlockWeights", "LlamaConfig", "LlamaModel", "Comm", "AutoregressiveModel",
     "generate_tokens", "generate", "GenerateOptions", "GenerateOutput", "GenerateTokenOutput",
-    "sample_argmax", "BpeTokenizer", "Tokenizer", "kernels", "DEFAULT_ROPE_THETA",
+    "sample_argmax", "BpeTokenizer", "NativeBpeTokenizer", "Tokenizer", "kernels",
+    "DEFAULT_ROPE_THETA",
     "ATTENTION_SPLIT", "ATTENTION_MAX_HEAD", "F32", "BF16", "U32", "load",
 ]

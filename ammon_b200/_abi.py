@@ -118,6 +118,14 @@ SIGNATURES = {
     "ab_sample_argmax": (i32, [C.POINTER(f32), u32]),
     "ab_generate_tokens": (C.c_int, [C.POINTER(Model_t), C.POINTER(i32), u32, u32, i32, i32,
                                      C.POINTER(i32), u32, C.POINTER(u32), C.POINTER(C.c_double)]),
+    "ab_bpe_from_path": (C.c_int, [C.c_char_p, u32, PP]),
+    "ab_bpe_from_parts": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(u32), C.POINTER(f32), u32,
+                                    u32, PP]),
+    "ab_bpe_info": (C.c_int, [P, C.POINTER(u32), C.POINTER(u32)]),
+    "ab_bpe_encode": (C.c_int, [P, C.c_char_p, C.c_size_t, i32, i32, C.POINTER(i32), u32,
+                                C.POINTER(u32)]),
+    "ab_bpe_decode": (C.c_int, [P, i32, i32, C.c_char_p, u32, C.POINTER(u32)]),
+    "ab_bpe_destroy": (C.c_int, [P]),
     "ab_llama_create": (C.c_int, [P, C.POINTER(LlamaConfig_t), PP]),
     "ab_llama_init_synthetic": (C.c_int, [P, u64, f32]),
     "ab_llama_weight": (C.c_int, [P, i32, u32, C.POINTER(T)]),

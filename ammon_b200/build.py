@@ -1,4 +1,5 @@
-"""Builds libammon_b200.so (all CUDA sources, sm_100a) in-tree with nvcc.
+"""Builds libammon_b200.so (all CUDA sources for sm_100a with nvcc, host C++ with the host
+compiler) in-tree.
 
 Usage: python -m ammon_b200.build [--force] [-j N]
 """
@@ -32,8 +33,16 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+# host-only C++ (the tokenizer) is compiled by the host compiler
+CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-I", INCLUDE, "-I", CSRC]
+
+
+def cuda_include() -> str:
+    return os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+
+
 def sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
 
 def headers():
@@ -50,10 +59,14 @@ def _stale(target, deps):
 
 
 def _compile(src, obj, extra):
-    cmd = [nvcc()] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
+    if src.endswith(".cpp"):
+        cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+        cmd = [cxx] + CXX_FLAGS + ["-I", cuda_include(), "-c", src, "-o", obj]
+    else:
+        cmd = [nvcc()] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stderr}")
+        raise RuntimeError(f"compiler failed on {os.path.basename(src)}:\n{r.stderr}")
     return r.stderr
 
 
@@ -62,7 +75,7 @@ def build(force: bool = False, jobs: int = 0, verbose_ptxas: bool = False) -> st
     hdrs = headers()
     objs, todo = [], []
     for src in sources():
-        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(BUILD, os.path.splitext(os.path.basename(src))[0] + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + hdrs):
             todo.append((src, obj))

@@ -257,6 +257,28 @@ int ab_generate_tokens(const ab_autoregressive_model* m, const int32_t* prompt,
                        int32_t stop_on, int32_t* out_tokens, uint32_t cap, uint32_t* out_len,
                        double* tokens_per_second);
 
+/* ---- BPE tokenizer (src/tokenizer.rs:18-178) ---------------------------------------
+ * llama2.c tokenizer.bin pieces and scores; encode/decode as BpeTokenizer's Tokenizer impl.
+ * Host-only (no GPU needed). */
+typedef struct ab_bpe ab_bpe;
+/* BpeTokenizer::from_path (src/tokenizer.rs:28-60): u32 max_token_length, then per piece
+ * f32 score, i32 length, bytes; pieces are read as UTF-8 with ill-formed bytes replaced. */
+int ab_bpe_from_path(const char* path, uint32_t vocab_size, ab_bpe** out);
+/* BpeTokenizer::from_parts (src/tokenizer.rs:62-74): n pieces given as bytes + lengths. */
+int ab_bpe_from_parts(const char* const* pieces, const uint32_t* lengths, const float* scores,
+                      uint32_t n, uint32_t max_token_length, ab_bpe** out);
+/* vocab_size / max_token_length (either pointer may be NULL). */
+int ab_bpe_info(const ab_bpe* t, uint32_t* vocab_size, uint32_t* max_token_length);
+/* Tokenizer::encode (src/tokenizer.rs:101-160) of len UTF-8 bytes: writes the first
+ * min(n, cap) ids to out (may be NULL) and n to *n_out. */
+int ab_bpe_encode(const ab_bpe* t, const char* text, size_t len, int32_t bos, int32_t eos,
+                  int32_t* out, uint32_t cap, uint32_t* n_out);
+/* Tokenizer::decode (src/tokenizer.rs:162-172): the UTF-8 bytes of the piece (first
+ * min(n, cap) into out, not NUL-terminated) and n in *n_out. */
+int ab_bpe_decode(const ab_bpe* t, int32_t prev_token, int32_t token, char* out, uint32_t cap,
+                  uint32_t* n_out);
+int ab_bpe_destroy(ab_bpe* t);
+
 /* ---- Llama-shaped model assembly ----------------------------------------------
  * The reference leaves model assembly to architecture crates (README.md:5,21). This
  * is the llama2.c-layout composition the harness and benchmark use: Embedding,
