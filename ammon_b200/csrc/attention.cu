@@ -849,8 +849,13 @@ struct AttnPfLayout {
     static size_t smem() { return (size_t)kStages * kStage + 1024; }
 };
 
+// Two groups of four warps take alternate K/V tiles for the same 64 query rows (twice the
+// warps in flight over the same CTA count) and merge their (max, sum, O) at the end.
+constexpr uint32_t kPfGroups = 2;
+constexpr uint32_t kPfThreads = 128 * kPfGroups;
+
 template <typename OT, int G, int HD>
-__global__ void __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(kPfThreads)
     attn_prefill_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap) {
     using LY = AttnPfLayout<HD>;
@@ -868,15 +873,16 @@ __global__ void __launch_bounds__(kAttnThreads)
 
     const uint32_t kvh = blockIdx.y, b0 = blockIdx.x * QP;
     const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    const uint32_t grp = warp / 4, wq = warp % 4;  // tile parity group, query row block
     const uint32_t g = lane / 4, t = lane % 4;
 
     pdl_wait();
-    // this thread's query rows 16 * warp + g (+ 8): the last position each may see (-1: none)
+    // this thread's query rows 16 * wq + g (+ 8): the last position each may see (-1: none)
     int32_t lim[2];
     const float* qrow[2];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const uint32_t r = warp * 16 + g + 8 * h;
+        const uint32_t r = wq * 16 + g + 8 * h;
         const uint32_t b = b0 + r / G;
         lim[h] = -1;
         qrow[h] = nullptr;
@@ -914,7 +920,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         sm_end = e;
         for (uint32_t s = 0; s < S; s++) {
             mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), 4);
+            mbar_init(smem_u32(&empty_bar[s]), 4);  // the four warps of the consuming group
         }
         fence_barrier_init();
         sm_fail = 0;
@@ -954,11 +960,19 @@ __global__ void __launch_bounds__(kAttnThreads)
     for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
     const uint32_t mi = lane / 8, r8 = lane % 8;
-    for (uint32_t i = 0; i < ntiles; i++) {
-        if (tid == 0 && i >= 1 && issued < ntiles) {
-            const uint32_t r = i - 1;
-            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) issue(issued++);
-            else sm_fail = 1;
+    for (uint32_t i = grp; i < ntiles; i += kPfGroups) {
+        // thread 0 keeps the ring S tiles ahead of its own group: tile j reuses the stage of
+        // tile j - S, released by whichever group consumed it (earlier tiles only, so every
+        // wait ends)
+        if (tid == 0) {
+            while (issued < ntiles && issued < i + S) {
+                const uint32_t r = issued - S;
+                if (!mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) {
+                    sm_fail = 1;
+                    break;
+                }
+                issue(issued++);
+            }
         }
         __syncwarp();
         if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
@@ -1078,17 +1092,45 @@ __global__ void __launch_bounds__(kAttnThreads)
         lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 1);
         lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 2);
     }
+    // group 1 hands its (m, l, O) to group 0 through the (now idle) stage memory
+    float* xo = (float*)smem;                     // [4 warps][NT * 4][32 lanes]
+    float* xml = xo + 4 * NT * 4 * 32;            // [4 warps][4][32 lanes]: m0, m1, l0, l1
+    if (grp == 1) {
+#pragma unroll
+        for (int n = 0; n < NT; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) xo[((wq * NT + n) * 4 + e) * 32 + lane] = o[n][e];
+        xml[(wq * 4 + 0) * 32 + lane] = mrow[0];
+        xml[(wq * 4 + 1) * 32 + lane] = mrow[1];
+        xml[(wq * 4 + 2) * 32 + lane] = lrow[0];
+        xml[(wq * 4 + 3) * 32 + lane] = lrow[1];
+    }
+    __syncthreads();
+    if (grp != 0) return;
+    float w0[2], w1[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const float m1 = xml[(wq * 4 + h) * 32 + lane];
+        const float l1 = xml[(wq * 4 + 2 + h) * 32 + lane];
+        const float m = fmaxf(mrow[h], m1);
+        w0[h] = mrow[h] == -INFINITY ? 0.0f : expf(mrow[h] - m);
+        w1[h] = m1 == -INFINITY ? 0.0f : expf(m1 - m);
+        lrow[h] = lrow[h] * w0[h] + l1 * w1[h];
+    }
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         if (!qrow[h] || lrow[h] <= 0.0f) continue;
-        const uint32_t r = warp * 16 + g + 8 * h;
+        const uint32_t r = wq * 16 + g + 8 * h;
         const uint32_t b = b0 + r / G;
         const float inv = 1.0f / lrow[h];
         OT* dst = (OT*)p.out + ((uint64_t)b * p.heads + (uint64_t)kvh * G + r % G) * HD;
 #pragma unroll
         for (int n = 0; n < NT; n++) {
             const uint32_t d = n * 8 + 2 * t;
-            store_pair(dst + d, o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+            const float a0 = o[n][2 * h] * w0[h] + xo[((wq * NT + n) * 4 + 2 * h) * 32 + lane] * w1[h];
+            const float a1 =
+                o[n][2 * h + 1] * w0[h] + xo[((wq * NT + n) * 4 + 2 * h + 1) * 32 + lane] * w1[h];
+            store_pair(dst + d, a0 * inv, a1 * inv);
         }
     }
 }
@@ -1294,14 +1336,14 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
-                return launch(st, pgrid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+                return launch(st, pgrid, dim3(kPfThreads), smem, true, kern, p, kmap, vmap);
             });
         } else {
             auto kern = attn_prefill_mma_kernel<OT, G, 64>;
             s->add(label, [=](cudaStream_t st) {
                 cudaError_t e = set_smem((const void*)kern, smem);
                 if (e != cudaSuccess) return e;
-                return launch(st, pgrid, dim3(kAttnThreads), smem, true, kern, p, kmap, vmap);
+                return launch(st, pgrid, dim3(kPfThreads), smem, true, kern, p, kmap, vmap);
             });
         }
         return;
