@@ -258,7 +258,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
 
-    if (threadIdx.x == 0) {
+    // Roles: lane 0 of warp 0 issues the TMA loads, lane 0 of warp 1 the MMAs. The other lanes
+    // of those warps park at __syncwarp until their lane 0 is done: spinning on the done
+    // barrier in the same warp would take issue turns (and mbarrier suspends) from it.
+    if (warp == 0) {
+        if (lane == 0) {
         // TMA producer
         for (uint32_t i = 0; i < nk; i++) {
             const uint32_t s = i % p.stages;
@@ -284,7 +288,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             tma_load_2d(a + a_bytes, &tb, kx, 0, bar);
         }
-    } else if (threadIdx.x == 32) {
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
         // MMA issuer
         const uint32_t idesc = tc_idesc_bf16(kTcBM, p.bn);
         for (uint32_t i = 0; i < nk; i++) {
@@ -303,6 +310,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_commit(smem_u32(&empty_bar[s]));
         }
         tc_commit(smem_u32(&done_bar));
+        }
+        __syncwarp();
     }
     const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0);
     tc_fence_after();
@@ -395,7 +404,9 @@ __global__ void __launch_bounds__(kTfThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
 
-    if (threadIdx.x == 0) {
+    // roles as in gemm_tc_kernel: lanes 1-31 of the producer and MMA warps park at __syncwarp
+    if (warp == 0) {
+        if (lane == 0) {
         // TMA producer
         for (uint32_t i = 0; i < nk; i++) {
             const uint32_t s = i % p.stages;
@@ -423,7 +434,10 @@ __global__ void __launch_bounds__(kTfThreads, 1)
             tma_load_2d(b, &tb_hi, kx, 0, bar);
             tma_load_2d(b + b_bytes, &tb_lo, kx, 0, bar);
         }
-    } else if (threadIdx.x == 32) {
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
         // MMA issuer: small products first, then Whi.Xhi
         const uint32_t idesc = tc_idesc_tf32(kTcBM, p.bn);
         for (uint32_t i = 0; i < nk; i++) {
@@ -447,6 +461,8 @@ __global__ void __launch_bounds__(kTfThreads, 1)
             tc_commit(smem_u32(&empty_bar[s]));
         }
         tc_commit(smem_u32(&done_bar));
+        }
+        __syncwarp();
     } else if (warp >= 2) {
         // split the landed W tile: hi in place, lo beside it (same swizzled offsets)
         const uint32_t t = threadIdx.x - 64;
