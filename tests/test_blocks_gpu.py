@@ -193,10 +193,11 @@ def test_tiny_llama_greedy_tokens_bit_identical(rt, orc):
     assert out_py.tokens == want
 
 
-@pytest.mark.parametrize("batch", [5, 8, 20, 64])
+@pytest.mark.parametrize("batch", [5, 8, 20, 64, 128, 200])
 def test_batched_bf16_model_on_tensor_cores(rt, orc, batch):
     """Batches above 4 with bf16 weights run every projection on the tcgen05 GEMM (row tiles
-    of 128, split-K where K allows): each stream matches its own oracle decode."""
+    of 128, split-K where K allows; 128 and 200 columns run two CTAs per SM with two or
+    three stages): each stream matches its own oracle decode."""
     cfg = dict(dim=512, layers=2, heads=8, kv_heads=2, head_dim=64, hidden=1024, vocab=640,
                seq=24, theta=500000.0)
     o, g = make_pair(rt, orc, bf16=True, batch=batch, seed=13, **cfg)

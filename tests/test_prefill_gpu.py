@@ -77,27 +77,27 @@ def test_prefill_fp32_matches_the_token_loop(rt, orc, rows):
     g2.close()
 
 
-@pytest.mark.parametrize("head", [64, 128])
-def test_prefill_bf16_one_stream_of_a_batch(rt, orc, head):
+@pytest.mark.parametrize("head,n", [(64, 40), (128, 40), (128, 150)])
+def test_prefill_bf16_one_stream_of_a_batch(rt, orc, head, n):
     """bf16 weights and cache (tensor-core GEMM, tensor-core attention over the shared
-    cache): stream 1 of 3 prefilled with 40 tokens in one pass matches its oracle; the
-    other streams' caches stay untouched, and a batched step afterwards serves stream 1 at
-    position 40 next to fresh streams 0 and 2."""
+    cache): stream 1 of 3 prefilled with n tokens in one pass (150: a 160-column GEMM)
+    matches its oracle; the other streams' caches stay untouched, and a batched step
+    afterwards serves stream 1 at position n next to fresh streams 0 and 2."""
     cfg = dict(dim=8 * head, layers=2, heads=8, kv_heads=2, head_dim=head, hidden=1024,
-               vocab=640, seq=96, theta=500000.0)
+               vocab=640, seq=n + 56, theta=500000.0)
     o, g = model(rt, orc, cfg, bf16=True, batch=3, seed=13)
-    prompt = np.random.default_rng(head).integers(0, cfg["vocab"], 40).tolist()
+    prompt = np.random.default_rng(head).integers(0, cfg["vocab"], n).tolist()
     logits, am = g.prefill(prompt, stream=1)
     for pos, tok in enumerate(prompt):
         want = o.step(tok, pos)
     assert rel(logits, want) < BF16_TOL, rel(logits, want)
     assert am == int(np.argmax(logits))
     key = g.cache().layer(0).key.read()  # bf16 bits [3, seq, kv, head]
-    assert not key[0].any() and not key[2].any() and key[1, :40].any() and not key[1, 40:].any()
+    assert not key[0].any() and not key[2].any() and key[1, :n].any() and not key[1, n:].any()
     fresh = [orc.Model(**cfg, bf16=True, seed=13) for _ in range(2)]
     toks = [5, am, 77]
-    got, _ = g.step_batch(toks, [0, 40, 0])
-    assert rel(got[1], o.step(am, 40)) < BF16_TOL
+    got, _ = g.step_batch(toks, [0, n, 0])
+    assert rel(got[1], o.step(am, n)) < BF16_TOL
     assert rel(got[0], fresh[0].step(5, 0)) < BF16_TOL
     assert rel(got[2], fresh[1].step(77, 0)) < BF16_TOL
     g.close()
