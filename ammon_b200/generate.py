@@ -79,9 +79,15 @@ def generate_tokens(model: AutoregressiveModel, prompt_tokens: Sequence[int],
 
 def generate(model: AutoregressiveModel, tokenizer: Tokenizer, prompt: str,
              options: GenerateOptions = GenerateOptions()) -> GenerateOutput:
-    """src/generate.rs:93-118."""
+    """src/generate.rs:93-118. A model with a batched-prefill loop of its own (the library's
+    batch-1 Llama model: ``generate(prompt, max_new_tokens, stop_on)``) runs the prompt through
+    it; the ids are those of generate_tokens."""
     prompt_tokens = tokenizer.encode(prompt, options.bos, options.eos)
-    out = generate_tokens(model, prompt_tokens, options.max_new_tokens, options.stop_on)
+    own = getattr(model, "generate", None)
+    if callable(own) and getattr(getattr(model, "cfg", None), "batch", 0) == 1:
+        out = own(prompt_tokens, options.max_new_tokens, options.stop_on)
+    else:
+        out = generate_tokens(model, prompt_tokens, options.max_new_tokens, options.stop_on)
     text = []
     prev = prompt_tokens[0]
     for tok in out.tokens:

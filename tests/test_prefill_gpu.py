@@ -151,3 +151,29 @@ def test_prefill_argument_checks(rt, orc):
     with pytest.raises(ab.AmmonError, match="batch-1 model"):
         g.generate([1, 2], 5)
     g.close()
+
+
+def test_text_generate_uses_the_prefill_loop(rt, orc, known):
+    """generate() (src/generate.rs:93-118) with the C++ tokenizer: the library model runs its
+    prefill loop and returns the same ids and text as the reference loop over the oracle."""
+    from ammon_b200.tokenizer import NativeBpeTokenizer
+
+    k = known["tokenizer"]
+    tok = NativeBpeTokenizer.from_parts(k["toy_vocab"], k["toy_scores"], k["max_token_length"])
+    o, g = model(rt, orc, SMALL)
+
+    class Oracle:
+        def vocab_size(self):
+            return SMALL["vocab"]
+
+        def max_seq_len(self):
+            return SMALL["seq"]
+
+        def step(self, token, pos):
+            return o.step(token, pos)
+
+    opts = ab.GenerateOptions(max_new_tokens=20)
+    want = ab.generate(Oracle(), tok, "abab ba", opts)
+    got = ab.generate(g, tok, "abab ba", opts)
+    assert got.tokens == want.tokens and got.text == want.text
+    g.close()
