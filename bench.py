@@ -818,7 +818,9 @@ def main():
     t_launch = ms_dom / n_dom / 1e3
     peak, peak_kind = load_peaks()
     achieved = lb[dom] / t_launch / 1e9 if dom in lb else None
-    mean_pos = pos0 - args.steps - e2e_steps + args.steps / 2
+    # the timed loop decoded positions pos0 - steps .. pos0 - 1 (the e2e loop after it does not
+    # advance pos0)
+    mean_pos = pos0 - args.steps + (args.steps - 1) / 2
     sb = step_bytes(w, B, mean_pos, shards)
 
     line = {
@@ -828,8 +830,7 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
         "config": {"workload": w["title"], "batch": B, "seq_len": w["seq"],
-                   "positions": f"{pos0 - args.steps - e2e_steps}.."
-                                f"{pos0 - e2e_steps - 1}",
+                   "positions": f"{pos0 - args.steps}..{pos0 - 1}",
                    "parallelism": (f"tp{world}" if tp else f"dp{world}" if split_streams
                                    else f"replicas{world}") if world > 1 else "single",
                    "l2": "inputs larger than L2 (weights stream every step)"},
