@@ -821,7 +821,6 @@ namespace {
 // pass ends with the classifier and the greedy pick of its last row when `head`.
 void run_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n, uint32_t pos0,
                  bool head) {
-    const auto& c = m->c;
     Runtime* rt = m->rt;
     rt->activate();
     setup_prefill(m);
@@ -842,7 +841,6 @@ void run_prefill(ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n
         m->pf_launches += (uint32_t)s->nodes.size();
         done += rows;
     }
-    (void)c;
 }
 
 void check_prompt(const ab_llama* m, uint32_t stream, const int32_t* tokens, uint32_t n,
