@@ -136,23 +136,27 @@ __device__ __forceinline__ void tc_epilogue_chunk(const GemmTcParams& p, uint32_
                                                   float* xch) {
     const uint32_t live = p.nb > c0 ? min(16u, p.nb - c0) : 0u;
     if (EPI == kEpiSwiglu) {
-        // tile rows 0-63 are w1 rows tile*64 + row, rows 64-127 the matching w3 rows
-        if (row >= 64) {
+        // tile rows 0-63 are w1 rows tile*64 + row, rows 64-127 the matching w3 rows. Both
+        // halves go through shared memory so that all 128 threads share the SwiGLU math:
+        // thread `row` finishes unit row % 64 for 8 of the 16 columns.
+        float* x0 = xch;            // [16][64] w1 products
+        float* x1 = xch + 16 * 64;  // [16][64] w3 products
+        float* xs = row < 64 ? x0 + row : x1 + (row - 64);
 #pragma unroll
-            for (int j = 0; j < 16; j++) xch[j * 64 + (row - 64)] = v[j];
-        }
+        for (int j = 0; j < 16; j++) xs[j * 64] = v[j];
         epi_sync();
-        if (row < 64) {
-            const uint32_t u = tile * 64 + row;
+        const uint32_t uu = row % 64, jb = (row / 64) * 8;
+        const uint32_t u = tile * 64 + uu;
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                if ((uint32_t)j >= live) break;
-                const float y0 = v[j], y1 = xch[j * 64 + row];
-                const float s = y0 * (1.0f / (1.0f + expf(-y0)));
-                const uint64_t o = (uint64_t)(c0 + j) * p.out_stride + u;
-                if (p.out_dtype == AB_F32) ((float*)p.out)[o] = s * y1;
-                else ((bf16*)p.out)[o] = __float2bfloat16_rn(s * y1);
-            }
+        for (int jj = 0; jj < 8; jj++) {
+            const uint32_t j = jb + jj;
+            if (j >= live) break;
+            const float y0 = x0[j * 64 + uu], y1 = x1[j * 64 + uu];
+            // 1 / (1 + e^-y0) as a correctly rounded reciprocal (the same value as the division)
+            const float s = y0 * __frcp_rn(1.0f + expf(-y0));
+            const uint64_t o = (uint64_t)(c0 + j) * p.out_stride + u;
+            if (p.out_dtype == AB_F32) ((float*)p.out)[o] = s * y1;
+            else ((bf16*)p.out)[o] = __float2bfloat16_rn(s * y1);
         }
         epi_sync();
         return;
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t a_bytes = kTcBM * 128;
     const uint32_t stage_bytes = a_bytes + p.bn * 128;
-    float* xch = (float*)(smem + (size_t)p.stages * stage_bytes);  // [16][64]
+    float* xch = (float*)(smem + (size_t)p.stages * stage_bytes);  // [2][16][64]
     const uint32_t tile = blockIdx.x, split = blockIdx.y;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t kb0 = (uint32_t)((uint64_t)split * p.kblocks / p.ksplit);
@@ -377,7 +381,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
     const uint32_t a_bytes = kTcBM * 128;
     const uint32_t b_bytes = p.bn * 128;
     const uint32_t stage_bytes = 2 * a_bytes + 2 * b_bytes;
-    float* xch = (float*)(smem + (size_t)p.stages * stage_bytes);  // [16][64]
+    float* xch = (float*)(smem + (size_t)p.stages * stage_bytes);  // [2][16][64]
     const uint32_t tile = blockIdx.x, split = blockIdx.y;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t kb0 = (uint32_t)((uint64_t)split * p.kblocks / p.ksplit);
@@ -711,14 +715,14 @@ GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool
         const long v = std::atol(e);
         if (v >= 2 && v <= kTcMaxStages) max_stages = (uint32_t)v;
     }
-    // resident CTAs share 227 KB of shared memory (each also holds the 4 KB exchange buffer
+    // resident CTAs share 227 KB of shared memory (each also holds the 8 KB exchange buffer
     // and 1 KB of alignment slack) and the 512 TMEM columns
     uint32_t cols = 32;
     while (cols < pl.bn) cols <<= 1;
     while (per_sm > 1 && (per_sm * cols > 512 ||
-                          per_sm * (2 * stage_bytes + 6u * 1024) > 226u * 1024))
+                          per_sm * (2 * stage_bytes + 10u * 1024) > 226u * 1024))
         per_sm--;
-    const uint32_t budget = per_sm == 1 ? 200u * 1024 : 220u * 1024 / per_sm - 6u * 1024;
+    const uint32_t budget = per_sm == 1 ? 200u * 1024 : 220u * 1024 / per_sm - 10u * 1024;
     pl.stages = std::max(2u, std::min(max_stages, budget / stage_bytes));
     const uint32_t target = (uint32_t)std::max(sms, 1) * per_sm;
     uint32_t ks = (target + pl.tiles / 2) / std::max(pl.tiles, 1u);
@@ -733,7 +737,7 @@ GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool
     // tuning parameter: the fp32 sums keep their per-tile order, in a rotated sequence)
     pl.krot = f32 ? 0 : 7;  // measured: +1% on bf16 batch-64 decode, -2.5% on 3xTF32 batch 256
     if (const char* e = std::getenv("AMMON_B200_GEMM_ROTATE")) pl.krot = (uint32_t)std::atol(e);
-    pl.smem = (size_t)pl.stages * stage_bytes + 16 * 64 * 4 + 1024;
+    pl.smem = (size_t)pl.stages * stage_bytes + 2 * 16 * 64 * 4 + 1024;
     pl.tmem_cols = cols;
     pl.ws_floats = pl.ksplit > 1 ? (uint64_t)pl.ksplit * pl.tiles * pl.bn * kTcBM : 0;
     return pl;
