@@ -267,51 +267,64 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // barrier in the same warp would take issue turns (and mbarrier suspends) from it.
     if (warp == 0) {
         if (lane == 0) {
-        // TMA producer
+        // TMA producer: the W map and row of this tile are fixed; stage, phase and k-block
+        // advance as counters (no divisions in the loop)
+        const CUtensorMap* wmap = &ta0;
+        int32_t wy = (int32_t)(tile * kTcBM);
+        if (p.interleave) {
+            wy = (int32_t)(tile * 64);
+        } else if (tile >= p.seg_tiles[0] + p.seg_tiles[1]) {
+            wmap = &ta2;
+            wy = (int32_t)((tile - p.seg_tiles[0] - p.seg_tiles[1]) * kTcBM);
+        } else if (tile >= p.seg_tiles[0]) {
+            wmap = &ta1;
+            wy = (int32_t)((tile - p.seg_tiles[0]) * kTcBM);
+        }
+        const uint32_t smem0 = smem_u32(smem);
+        uint32_t s = 0, ph = 0, kb = kb0 + rot;
         for (uint32_t i = 0; i < nk; i++) {
-            const uint32_t s = i % p.stages;
-            if (i >= p.stages &&
-                !mbar_wait_bounded(smem_u32(&empty_bar[s]), ((i / p.stages) - 1) & 1)) {
+            if (i >= p.stages && !mbar_wait_bounded(smem_u32(&empty_bar[s]), ph ^ 1)) {
                 sm_ok = 0;
                 break;
             }
-            const int32_t kx = (int32_t)((kb0 + (i + rot) % nk) * kTcBK);
+            const int32_t kx = (int32_t)(kb * kTcBK);
             const uint32_t bar = smem_u32(&full_bar[s]);
-            const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
+            const uint32_t a = smem0 + s * stage_bytes;
             mbar_arrive_expect_tx(bar, stage_bytes);
-            if (p.interleave) {
-                tma_load_2d(a, &ta0, kx, (int32_t)(tile * 64), bar);
-                tma_load_2d(a + 64 * 128, &ta1, kx, (int32_t)(tile * 64), bar);
-            } else if (tile < p.seg_tiles[0]) {
-                tma_load_2d(a, &ta0, kx, (int32_t)(tile * kTcBM), bar);
-            } else if (tile < p.seg_tiles[0] + p.seg_tiles[1]) {
-                tma_load_2d(a, &ta1, kx, (int32_t)((tile - p.seg_tiles[0]) * kTcBM), bar);
-            } else {
-                tma_load_2d(a, &ta2, kx,
-                            (int32_t)((tile - p.seg_tiles[0] - p.seg_tiles[1]) * kTcBM), bar);
-            }
+            tma_load_2d(a, wmap, kx, wy, bar);
+            if (p.interleave) tma_load_2d(a + 64 * 128, &ta1, kx, wy, bar);
             tma_load_2d(a + a_bytes, &tb, kx, 0, bar);
+            if (++kb == kb1) kb = kb0;
+            if (++s == p.stages) {
+                s = 0;
+                ph ^= 1;
+            }
         }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-        // MMA issuer
+        // MMA issuer: descriptors of a stage's operands advance by 32 bytes (2 in the
+        // descriptor's address field) per 16-element k-step
         const uint32_t idesc = tc_idesc_bf16(kTcBM, p.bn);
+        const uint32_t smem0 = smem_u32(smem);
+        uint32_t s = 0, ph = 0;
         for (uint32_t i = 0; i < nk; i++) {
-            const uint32_t s = i % p.stages;
-            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), ph)) {
                 sm_ok = 0;
                 break;
             }
             tc_fence_after();
-            const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
-            const uint32_t b = a + a_bytes;
+            const uint32_t a = smem0 + s * stage_bytes;
+            const uint64_t da = sw128_desc(a), db = sw128_desc(a + a_bytes);
 #pragma unroll
             for (uint32_t k = 0; k < kTcBK / 16; k++)
-                tc_mma_bf16(tmem, sw128_desc(a + 32 * k), sw128_desc(b + 32 * k), idesc,
-                            (i | k) != 0);
+                tc_mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
             tc_commit(smem_u32(&empty_bar[s]));
+            if (++s == p.stages) {
+                s = 0;
+                ph ^= 1;
+            }
         }
         tc_commit(smem_u32(&done_bar));
         }
@@ -411,32 +424,39 @@ __global__ void __launch_bounds__(kTfThreads, 1)
     // roles as in gemm_tc_kernel: lanes 1-31 of the producer and MMA warps park at __syncwarp
     if (warp == 0) {
         if (lane == 0) {
-        // TMA producer
+        // TMA producer (counters as in gemm_tc_kernel)
+        const CUtensorMap* wmap = &ta0;
+        int32_t wy = (int32_t)(tile * kTcBM);
+        if (p.interleave) {
+            wy = (int32_t)(tile * 64);
+        } else if (tile >= p.seg_tiles[0] + p.seg_tiles[1]) {
+            wmap = &ta2;
+            wy = (int32_t)((tile - p.seg_tiles[0] - p.seg_tiles[1]) * kTcBM);
+        } else if (tile >= p.seg_tiles[0]) {
+            wmap = &ta1;
+            wy = (int32_t)((tile - p.seg_tiles[0]) * kTcBM);
+        }
+        const uint32_t smem0 = smem_u32(smem);
+        uint32_t s = 0, ph = 0, kb = kb0 + rot;
         for (uint32_t i = 0; i < nk; i++) {
-            const uint32_t s = i % p.stages;
-            if (i >= p.stages &&
-                !mbar_wait_bounded(smem_u32(&empty_bar[s]), ((i / p.stages) - 1) & 1)) {
+            if (i >= p.stages && !mbar_wait_bounded(smem_u32(&empty_bar[s]), ph ^ 1)) {
                 sm_ok = 0;
                 break;
             }
-            const int32_t kx = (int32_t)((kb0 + (i + rot) % nk) * kTfBK);
+            const int32_t kx = (int32_t)(kb * kTfBK);
             const uint32_t bar = smem_u32(&full_bar[s]);
-            const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
+            const uint32_t a = smem0 + s * stage_bytes;
             const uint32_t b = a + 2 * a_bytes;
             mbar_arrive_expect_tx(bar, a_bytes + 2 * b_bytes);
-            if (p.interleave) {
-                tma_load_2d(a, &ta0, kx, (int32_t)(tile * 64), bar);
-                tma_load_2d(a + 64 * 128, &ta1, kx, (int32_t)(tile * 64), bar);
-            } else if (tile < p.seg_tiles[0]) {
-                tma_load_2d(a, &ta0, kx, (int32_t)(tile * kTcBM), bar);
-            } else if (tile < p.seg_tiles[0] + p.seg_tiles[1]) {
-                tma_load_2d(a, &ta1, kx, (int32_t)((tile - p.seg_tiles[0]) * kTcBM), bar);
-            } else {
-                tma_load_2d(a, &ta2, kx,
-                            (int32_t)((tile - p.seg_tiles[0] - p.seg_tiles[1]) * kTcBM), bar);
-            }
+            tma_load_2d(a, wmap, kx, wy, bar);
+            if (p.interleave) tma_load_2d(a + 64 * 128, &ta1, kx, wy, bar);
             tma_load_2d(b, &tb_hi, kx, 0, bar);
             tma_load_2d(b + b_bytes, &tb_lo, kx, 0, bar);
+            if (++kb == kb1) kb = kb0;
+            if (++s == p.stages) {
+                s = 0;
+                ph ^= 1;
+            }
         }
         }
         __syncwarp();
@@ -444,25 +464,29 @@ __global__ void __launch_bounds__(kTfThreads, 1)
         if (lane == 0) {
         // MMA issuer: small products first, then Whi.Xhi
         const uint32_t idesc = tc_idesc_tf32(kTcBM, p.bn);
+        const uint32_t smem0 = smem_u32(smem);
+        uint32_t s = 0, ph = 0;
         for (uint32_t i = 0; i < nk; i++) {
-            const uint32_t s = i % p.stages;
-            if (!mbar_wait_bounded(smem_u32(&split_bar[s]), (i / p.stages) & 1)) {
+            if (!mbar_wait_bounded(smem_u32(&split_bar[s]), ph)) {
                 sm_ok = 0;
                 break;
             }
             tc_fence_after();
-            const uint32_t whi = smem_u32(smem + (size_t)s * stage_bytes);
-            const uint32_t wlo = whi + a_bytes;
-            const uint32_t xhi = whi + 2 * a_bytes;
-            const uint32_t xlo = xhi + b_bytes;
+            const uint32_t whi = smem0 + s * stage_bytes;
+            const uint64_t dwhi = sw128_desc(whi), dwlo = sw128_desc(whi + a_bytes);
+            const uint64_t dxhi = sw128_desc(whi + 2 * a_bytes);
+            const uint64_t dxlo = sw128_desc(whi + 2 * a_bytes + b_bytes);
 #pragma unroll
             for (uint32_t k = 0; k < kTfBK / 8; k++) {
-                tc_mma_tf32(tmem, sw128_desc(wlo + 32 * k), sw128_desc(xhi + 32 * k), idesc,
-                            (i | k) != 0);
-                tc_mma_tf32(tmem, sw128_desc(whi + 32 * k), sw128_desc(xlo + 32 * k), idesc, 1);
-                tc_mma_tf32(tmem, sw128_desc(whi + 32 * k), sw128_desc(xhi + 32 * k), idesc, 1);
+                tc_mma_tf32(tmem, dwlo + 2 * k, dxhi + 2 * k, idesc, (i | k) != 0);
+                tc_mma_tf32(tmem, dwhi + 2 * k, dxlo + 2 * k, idesc, 1);
+                tc_mma_tf32(tmem, dwhi + 2 * k, dxhi + 2 * k, idesc, 1);
             }
             tc_commit(smem_u32(&empty_bar[s]));
+            if (++s == p.stages) {
+                s = 0;
+                ph ^= 1;
+            }
         }
         tc_commit(smem_u32(&done_bar));
         }
