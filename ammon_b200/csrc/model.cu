@@ -78,12 +78,56 @@ __device__ __forceinline__ ArgPair row_argmax(const float* __restrict__ row, uin
     return r;
 }
 
-// Device argmax of each row of logits [batch, vocab].
-__global__ void __launch_bounds__(1024)
-    argmax_kernel(const float* __restrict__ logits, uint32_t vocab, int32_t* __restrict__ out) {
+// Device argmax with the row split over kArgmaxSplit CTAs: CTA (s, b) takes the first maximum
+// of its slice of row b, and the last CTA of the row to finish (atomic ticket, reset for the
+// next replay) keeps the first maximum of the slices' candidates (greater value, or the lower
+// id among equal values: the sample_argmax rule). One 1024-thread CTA per row read a 128k-entry
+// row at ~20 GB/s; the split takes the row in a few microseconds.
+constexpr uint32_t kArgmaxSplit = 64;
+
+__device__ __forceinline__ ArgPair first_max(ArgPair a, ArgPair b) {
+    if (b.i == 0xffffffffu) return a;
+    if (a.i == 0xffffffffu || b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+    return a;
+}
+
+__global__ void __launch_bounds__(256)
+    argmax_split_kernel(const float* __restrict__ logits, uint32_t vocab, ArgPair* part,
+                        uint32_t* tickets, int32_t* __restrict__ out) {
     pdl_wait();
-    const ArgPair r = row_argmax(logits + (uint64_t)blockIdx.x * vocab, vocab, 0);
-    if (threadIdx.x == 0) out[blockIdx.x] = r.i == 0xffffffffu ? 0 : (int32_t)r.i;
+    const uint32_t sl = blockIdx.x, b = blockIdx.y, ns = gridDim.x;
+    const uint32_t chunk = (vocab + ns - 1) / ns;
+    const uint32_t lo = min(vocab, sl * chunk), hi = min(vocab, lo + chunk);
+    const ArgPair r = row_argmax(logits + (uint64_t)b * vocab + lo, hi - lo, lo);
+    __shared__ int last;
+    if (threadIdx.x == 0) {
+        part[(uint64_t)b * ns + sl] = r;
+        __threadfence();
+        last = atomicAdd(&tickets[b], 1u) == ns - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x < 32) {
+        __threadfence();
+        ArgPair best = {-INFINITY, 0xffffffffu};
+        for (uint32_t k = threadIdx.x; k < ns; k += 32) {
+            const ArgPair* src = part + (uint64_t)b * ns + k;
+            ArgPair c;
+            c.v = __ldcg(&src->v);
+            c.i = __ldcg(&src->i);
+            best = first_max(best, c);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            ArgPair c;
+            c.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+            c.i = __shfl_xor_sync(0xffffffffu, best.i, o);
+            best = first_max(best, c);
+        }
+        if (threadIdx.x == 0) {
+            out[b] = best.i == 0xffffffffu ? 0 : (int32_t)best.i;
+            tickets[b] = 0;
+        }
+    }
     pdl_trigger();
 }
 
@@ -150,6 +194,7 @@ struct ab_llama {
     ab_swiglu_block* ffn = nullptr;
     ab_tensor x = {}, logits = {}, step = {}, argmax = {}, history = {};
     ab_tensor logits_all = {}, pairs = {}, pairs_all = {};  // tensor parallelism
+    ab_tensor amx_part = {}, amx_tickets = {};  // split argmax: [batch, split] pairs, [batch]
     ab_scheme* scheme = nullptr;       // one decode step (gathers the logits under TP)
     ab_scheme* loop_scheme = nullptr;  // one decode step + device sample feedback
     GemmScratch cls_tc;                // classifier's tensor-core GEMM scratch
@@ -233,7 +278,8 @@ void destroy_model(ab_llama* m) {
                     &m->w3})
         for (auto& t : *v) free_t(t);
     for (ab_tensor* t : {&m->embed, &m->wcls, &m->rms_final, &m->x, &m->logits, &m->step,
-                         &m->argmax, &m->history, &m->logits_all, &m->pairs, &m->pairs_all})
+                         &m->argmax, &m->history, &m->logits_all, &m->pairs, &m->pairs_all,
+                         &m->amx_part, &m->amx_tickets})
         free_t(*t);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_argmax) cudaFreeHost(m->h_argmax);
@@ -294,6 +340,8 @@ struct HeadOut {
     ArgPair* pairs_all;
     void* logits_all;
     const GemmScratch* tc;
+    ArgPair* split_part;      // [rows, kArgmaxSplit] slice candidates (one GPU)
+    uint32_t* split_tickets;  // [rows], zero between launches
 };
 
 // Final RmsNorm fused into the classifier's prologue (this rank's vocabulary rows), then the
@@ -322,8 +370,11 @@ void record_head(ab_llama* m, ab_scheme* s, const HeadOut& h, bool gather_logits
     const uint32_t batch = h.rows;
     if (m->world == 1) {
         const uint32_t vocab = c.vocab;
+        ArgPair* part = h.split_part;
+        uint32_t* tk = h.split_tickets;
         s->add("argmax", [=](cudaStream_t st) {
-            return launch(st, dim3(batch), dim3(1024), 0, true, argmax_kernel, lg, vocab, am);
+            return launch(st, dim3(kArgmaxSplit, batch), dim3(256), 0, true, argmax_split_kernel,
+                          lg, vocab, part, tk, am);
         });
     } else {
         ArgPair* pr = h.pairs;
@@ -361,7 +412,7 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
     record_head(m, s,
                 {(const float*)m->x.data, batch, (float*)m->logits.data, am,
                  (ArgPair*)m->pairs.data, (ArgPair*)m->pairs_all.data, m->logits_all.data,
-                 &m->cls_tc},
+                 &m->cls_tc, (ArgPair*)m->amx_part.data, (uint32_t*)m->amx_tickets.data},
                 gather_logits);
     if (feedback) {
         Step* stp = (Step*)m->step.data;
@@ -394,7 +445,8 @@ void record_prefill(ab_llama* m, ab_scheme* s, uint32_t stream, uint32_t rows, b
                     {(const float*)m->pf_x.data + (uint64_t)(rows - 1) * c.dim, 1,
                      (float*)m->pf_logits.data, (int32_t*)m->pf_argmax.data,
                      (ArgPair*)m->pf_pairs.data, (ArgPair*)m->pf_pairs_all.data,
-                     m->pf_logits_all.data, nullptr},
+                     m->pf_logits_all.data, nullptr, (ArgPair*)m->amx_part.data,
+                     (uint32_t*)m->amx_tickets.data},
                     true);
 }
 
@@ -535,6 +587,8 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
         m->x = alloc_t(rt, AB_F32, {c.batch, c.dim});
         m->logits = alloc_t(rt, AB_F32, {c.batch, m->vocab_l});
         m->argmax = alloc_t(rt, AB_U32, {c.batch});
+        m->amx_part = alloc_t(rt, AB_U32, {c.batch, kArgmaxSplit, 2});
+        m->amx_tickets = alloc_t(rt, AB_U32, {c.batch});
         m->history = alloc_t(rt, AB_U32, {c.seq, c.batch});
         if (world > 1) {
             m->logits_all = alloc_t(rt, AB_F32, {(uint32_t)world, c.batch, m->vocab_l});
