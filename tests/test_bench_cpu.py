@@ -1,0 +1,61 @@
+"""bench.py's bookkeeping on CPU: the algorithmic byte and FLOP counts its roofline figures
+divide by (restated here by hand on the 8B shapes), the prompt id generator, and the
+reference arm's JSON line on the tiny workload."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+W8B = bench.WORKLOADS["llama3-8b-bf16"]
+
+
+def test_step_bytes_8b_batch1():
+    # weights once: per layer (4096 x 6144 + 4096 x 4096 + 3 x 4096 x 14336) bf16, the
+    # classifier 128256 x 4096; plus K/V rows 0..pos for 32 layers of 8 x 128 bf16 each
+    d, F, V, L = 4096, 14336, 128256, 32
+    weights = L * (d * 6144 + d * d + 3 * d * F) * 2 + V * d * 2
+    sb = bench.step_bytes(W8B, 1, 199.0)
+    kv = L * 2 * 1024 * 2 * 200
+    assert abs(sb - weights - kv) / sb < 2e-3  # activations and gains are the remainder
+    assert 15.0e9 < weights < 15.1e9  # the 15.01 GB the metric is quoted with
+
+
+def test_step_bytes_grow_with_position_and_batch():
+    assert bench.step_bytes(W8B, 64, 300) > bench.step_bytes(W8B, 64, 100)
+    kv64 = bench.step_bytes(W8B, 64, 100) - bench.step_bytes(W8B, 64, 99)
+    assert kv64 == 64 * 32 * 2 * 1024 * 2
+    # tensor parallel over 8 ranks: one rank's share of the weights and K/V
+    assert bench.step_bytes(W8B, 1, 0, shards=8) < bench.step_bytes(W8B, 1, 0) / 7
+
+
+def test_prefill_flops_by_hand():
+    P = 2048
+    per_token = 2 * 32 * (4096 * (4096 + 2 * 1024) + 4096 * 4096 + 3 * 4096 * 14336)
+    attn = 32 * 4 * 4096 * P * (P + 1) // 2
+    assert bench.prefill_flops(W8B, P) == P * per_token + attn + 2 * 128256 * 4096
+
+
+def test_prompt_tokens_are_seeded_and_in_range():
+    a = bench.prompt_tokens(3, 1000, 128, 3, 128256)
+    assert a == bench.prompt_tokens(3, 1000, 128, 3, 128256)
+    assert a != bench.prompt_tokens(3, 1001, 128, 3, 128256)
+    assert all(3 <= t < 128256 for t in a)
+
+
+@pytest.mark.slow
+def test_reference_arm_prints_one_line():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload",
+                        "tiny-llama-f32", "--steps", "2", "--warmup", "1"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "tokens/s"
+    assert d["cpu_baseline"]["kind"] == "port" and d["e2e"]["value"] == d["value"]
