@@ -132,6 +132,6 @@ def test_long_text_encodes_fast():
     ids = nat.encode(text, True, True)
     assert time.perf_counter() - t0 < 5.0
     assert ids[0] == 1 and ids[-1] == 2
+    # the head of the same text against the reference loop (quadratic, so a short slice)
     py = BpeTokenizer.from_parts(vocab, scores, 8)
-    assert ids[:1] + nat.encode(text[:300], False, True)[1:] != [] and \
-        nat.encode(text[:300], True, True) == py.encode(text[:300], True, True)
+    assert nat.encode(text[:300], True, True) == py.encode(text[:300], True, True)
