@@ -70,6 +70,15 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// silu(g) * u in the order of the reference's swiglu kernel (src/kernels.rs:462-476):
+// g * (1 / (1 + e^-g)), then times u, with the accurate exponential and an IEEE division.
+// Every SwiGLU epilogue (GEMV, single-split GEMM, split-K fold, standalone kernel) calls
+// this one expression, so a layer's result does not depend on which of them ran it.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float s = g * (1.0f / (1.0f + expf(-g)));
+    return s * u;
+}
+
 // RoPE angle of pair i (even) of a head of size head at position pos
 // (src/kernels.rs:195-199): freq = 1 / theta^((i % head) / head).
 __device__ __forceinline__ void rope_cos_sin(uint32_t i, uint32_t head, uint32_t pos, float theta,

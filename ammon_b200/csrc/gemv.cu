@@ -254,8 +254,7 @@ __global__ void __launch_bounds__(kGemvThreads, 4) gemv_kernel(const GemvParams 
         }
         const uint32_t u = u0 + ul;
         if (EPI == kEpiSwiglu) {
-            const float v = y0 * (1.0f / (1.0f + expf(-y0)));
-            store_elem(p.out, p.out_dtype, (uint64_t)b * p.out_stride + u, v * y1);
+            store_elem(p.out, p.out_dtype, (uint64_t)b * p.out_stride + u, silu_mul(y0, y1));
         } else if (EPI == kEpiQkv) {
             const uint32_t r = 2 * u;
             const uint32_t pos = p.step[b].position;

@@ -457,9 +457,7 @@ __global__ void swiglu_kernel(T* hb, const T* __restrict__ hb2, uint64_t n) {
     pdl_wait();
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * blockDim.x) {
-        float v = to_f32(hb[i]);
-        v = v * (1.0f / (1.0f + expf(-v)));
-        hb[i] = from_f32<T>(v * to_f32(hb2[i]));
+        hb[i] = from_f32<T>(silu_mul(to_f32(hb[i]), to_f32(hb2[i])));
     }
     pdl_trigger();
 }

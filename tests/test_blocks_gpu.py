@@ -277,3 +277,60 @@ def test_position_beyond_seq_is_rejected(rt, orc):
         g.step(1, g.cfg.seq)
     with pytest.raises(ab.AmmonError, match="out of range"):
         g.step(g.cfg.vocab, 0)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_swiglu_result_independent_of_kernel_and_ksplit(rt, orc, dtype, monkeypatch):
+    """The gate/up SwiGLU runs in the GEMV epilogue (batch <= 4), the single-split GEMM
+    epilogue or, split over k, the fold kernel. All three use one expression
+    (src/kernels.rs:462-476 order), so with sums that are exact in fp32 whatever their order
+    (x = +-4096 normalises to exactly +-1, gate/up weights are small integers, w2 copies hb[r]
+    into row r) the block's result is bit-identical for every path and split count."""
+    dim, hidden = 512, 256
+    rng = np.random.default_rng(11)
+    x_host = np.where(rng.random((8, dim)) < 0.5, -4096.0, 4096.0).astype(np.float32)
+    w1 = (rng.integers(-1, 2, (hidden, dim)) * (rng.random((hidden, dim)) < 0.08)).astype(
+        np.float32)
+    w3 = (rng.integers(-2, 3, (hidden, dim)) * (rng.random((hidden, dim)) < 0.08)).astype(
+        np.float32)
+    w2 = np.zeros((dim, hidden), np.float32)
+    w2[np.arange(hidden), np.arange(hidden)] = 1.0
+    gain = np.ones(dim, np.float32)
+    dt = ab.BF16 if dtype == "bf16" else ab.F32
+
+    def dev(a):
+        return ab.Tensor.from_array(rt, orc.to_bf16_bits(a).reshape(a.shape) if dt == ab.BF16
+                                    else a, dt)
+
+    w = ab.SwiGluBlockWeights(dev(gain), dev(w1), dev(w3), dev(w2))
+
+    def run(batch, max_ksplit=None):
+        if max_ksplit:
+            monkeypatch.setenv("AMMON_B200_GEMM_MAX_KSPLIT", str(max_ksplit))
+        else:
+            monkeypatch.delenv("AMMON_B200_GEMM_MAX_KSPLIT", raising=False)
+        ffn = ab.SwiGluBlock(rt, dim, hidden, max_batch=batch)
+        x = ab.Tensor.from_array(rt, x_host[:batch])
+        s = rt.scheme()
+        ffn.record(s, x, w)
+        s.submit()
+        out = x.read()
+        monkeypatch.delenv("AMMON_B200_GEMM_MAX_KSPLIT", raising=False)
+        return out, s.node_labels()
+
+    split, labels_split = run(8)
+    single, labels_single = run(8, max_ksplit=1)
+    gemv, labels_gemv = run(4)
+    assert "ffn_gate_up_swiglu_splitk" in labels_split, labels_split
+    assert "ffn_gate_up_swiglu_splitk" not in labels_single, labels_single
+    assert np.array_equal(split, single)
+    assert np.array_equal(split[:4], gemv)
+    # and the value itself: silu(g) * u of the exact integer sums, against float64
+    g = x_host[:8] / 4096.0 @ w1.T.astype(np.float64)
+    u = x_host[:8] / 4096.0 @ w3.T.astype(np.float64)
+    h = g / (1.0 + np.exp(-g)) * u
+    if dt == ab.BF16:
+        h = orc.round_bf16(h.astype(np.float32)).reshape(h.shape)
+    want = x_host[:8].astype(np.float64)
+    want[:, :hidden] += h
+    assert rel(split, want) < 1e-6
