@@ -115,6 +115,7 @@ SIGNATURES = {
     "ab_swiglu_block_record": (C.c_int, [P, P, T, C.POINTER(SwigluWeights_t)]),
     "ab_swiglu_block_destroy": (C.c_int, [P]),
     "ab_attention_decode_noalloc": (C.c_int, [P, T, T, T, T, T]),
+    "ab_attention_decode_noalloc_status": (C.c_int, [P, C.POINTER(u32)]),
     "ab_sample_argmax": (i32, [C.POINTER(f32), u32]),
     "ab_generate_tokens": (C.c_int, [C.POINTER(Model_t), C.POINTER(i32), u32, u32, i32, i32,
                                      C.POINTER(i32), u32, C.POINTER(u32), C.POINTER(C.c_double)]),

@@ -1625,3 +1625,22 @@ extern "C" int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor 
         for (auto& n : tmp.nodes) cuda_check(n.launch(st), "attention launch");
     });
 }
+
+// The flag word the allocation-free attention raises (a position >= seq, a bounded wait that
+// ran out) is sticky across calls: this reads it after `stream` drains, clears it, and turns
+// a raised flag into AB_ERR_DEVICE. Copies through host stack memory; allocates nothing.
+extern "C" int ab_attention_decode_noalloc_status(void* stream, uint32_t* flags_out) {
+    return guard([&] {
+        if (flags_out) *flags_out = 0;
+        int device = 0;
+        unsigned char* base = noalloc_scratch(&device);
+        uint32_t* flags = (uint32_t*)(base + kNoAllocFloats * 4 + (uint64_t)kNoAllocTickets * 4);
+        cudaStream_t st = (cudaStream_t)stream;
+        uint32_t f = 0;
+        cuda_check(cudaMemcpyAsync(&f, flags, 4, cudaMemcpyDeviceToHost, st), "read flags");
+        cuda_check(cudaMemsetAsync(flags, 0, 4, st), "clear flags");
+        cuda_check(cudaStreamSynchronize(st), "synchronize");
+        if (flags_out) *flags_out = f;
+        if (f) fail(AB_ERR_DEVICE, "ab_attention_decode_noalloc: " + device_flag_message(f));
+    });
+}

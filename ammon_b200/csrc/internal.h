@@ -105,6 +105,9 @@ enum DeviceFlag : uint32_t {
     kFlagWaitTimeout = 4u,
 };
 
+// "device reported: ..." text for a non-zero flag word.
+std::string device_flag_message(uint32_t flags);
+
 // ---- schemes -------------------------------------------------------------------------
 using LaunchFn = std::function<cudaError_t(cudaStream_t)>;
 

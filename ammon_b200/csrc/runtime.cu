@@ -83,16 +83,20 @@ uint32_t expect_step(const ab_tensor& step, uint32_t need) {
 
 void Runtime::activate() const { cuda_check(cudaSetDevice(device), "cudaSetDevice"); }
 
+std::string device_flag_message(uint32_t f) {
+    std::string m = "device reported:";
+    if (f & kFlagTokenRange) m += " token id out of the embedding table's range;";
+    if (f & kFlagPositionRange) m += " decode position beyond the cache's seq_len;";
+    if (f & kFlagWaitTimeout) m += " a bounded wait timed out;";
+    return m;
+}
+
 void Runtime::check_flags() {
     uint32_t f = 0;
     cuda_check(cudaMemcpy(&f, flags, 4, cudaMemcpyDeviceToHost), "read device flags");
     if (f) {
         cuda_check(cudaMemset(flags, 0, 4), "clear device flags");
-        std::string m = "device reported:";
-        if (f & kFlagTokenRange) m += " token id out of the embedding table's range;";
-        if (f & kFlagPositionRange) m += " decode position beyond the cache's seq_len;";
-        if (f & kFlagWaitTimeout) m += " a bounded wait timed out;";
-        fail(AB_ERR_DEVICE, m);
+        fail(AB_ERR_DEVICE, device_flag_message(f));
     }
 }
 

@@ -233,9 +233,19 @@ int ab_swiglu_block_destroy(ab_swiglu_block* b);
  * tickets are cleared on the stream before each launch): calls that overlap on the GPU
  * race. The first call on each device looks up the array's address with
  * cudaGetSymbolAddress, with that device current; make that first call before any
- * stream capture begins. Positions >= seq produce zero rows. */
+ * stream capture begins. The looked-up address is kept for the life of the process: after
+ * cudaDeviceReset it is stale, so do not call this entry (or its status call) again in a
+ * process that reset the device. A row whose position is >= seq produces a zero row and
+ * raises a flag, as does a bounded wait inside the kernel that ran out (its row is then
+ * incomplete); read the flags with ab_attention_decode_noalloc_status. */
 int ab_attention_decode_noalloc(void* stream, ab_tensor q, ab_tensor key_cache,
                                 ab_tensor value_cache, ab_tensor out, ab_tensor step);
+/* Companion of ab_attention_decode_noalloc (no counterpart in the reference): waits for
+ * `stream`, reads and clears the device flag word the allocation-free calls on the current
+ * device raise, and returns AB_ERR_DEVICE (message via ab_last_error) if any call since the
+ * last status read flagged a position >= seq or a bounded wait that ran out. The raw bits go
+ * to *flags (may be NULL). Allocates nothing. */
+int ab_attention_decode_noalloc_status(void* stream, uint32_t* flags);
 
 /* ---- host decode loop (src/model.rs, src/generate.rs, src/tokenizer.rs) ------ */
 /* sample_argmax (src/tokenizer.rs:179-189): first index of the maximum. */
