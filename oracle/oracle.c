@@ -211,7 +211,7 @@ void or_gemv(const float* x, uint32_t n, const float* w, uint32_t d, float* xout
  * src/blocks.rs:220-225,254-255,268-274,305-315). The reference delegates to Goldy's
  * cuBLAS-backed matmul, whose summation order is unpinned; the oracle uses the serial
  * order of the reference's own gemv kernel (src/kernels.rs:67-70). Rows are
- * independent, so the OpenMP split over rows keeps each row's order. */
+ * independent, so the pthread split over rows keeps each row's order. */
 typedef struct {
     const void* w;
     uint32_t d_in;

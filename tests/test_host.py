@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 import ammon_b200 as ab
-from ammon_b200.tokenizer import BpeTokenizer
+from ammon_b200.tokenizer import BpeTokenizer  # the C++ tokenizer (ab_bpe_*)
 
 
 @pytest.fixture(scope="module")

