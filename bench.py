@@ -216,30 +216,48 @@ def step_bytes(w, batch, mean_pos, shards=1):
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_sample(w, batch, positions, threads):
-    """Times the oracle port of the reference's kernels on a bounded sample: one decoder
-    layer of the workload's shape at the given positions, and a 4096-row slice of the
-    classifier; scales to a full token (layers x layer time + classifier / slice)."""
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_port_model(w, seq):
+    """The oracle port of the reference's kernels (oracle/oracle.c, the serial per-row order
+    of src/kernels.rs) holding the workload's whole model: every layer and the full
+    classifier, its seeded weights drawn on the host by the generator the GPU uses. Returns
+    (model, threads)."""
     from oracle import oracle as orc
 
+    threads = host_threads()
     orc.set_threads(threads)
-    vslice = min(4096, w["vocab"])
-    m = orc.Model(w["dim"], 1, w["heads"], w["kv_heads"], w["head_dim"], w["hidden"], vslice,
-                  max(positions) + 2, theta=w["theta"], bf16=w["bf16"], seed=w["seed"])
-    x = orc.normal(w["dim"], 9, 9, 0.0, 1.0)
-    per_token = []
+    t0 = time.perf_counter()
+    m = orc.Model(w["dim"], w["layers"], w["heads"], w["kv_heads"], w["head_dim"], w["hidden"],
+                  w["vocab"], seq, theta=w["theta"], bf16=w["bf16"], seed=w["seed"])
+    print(f"cpu port: {w['title']} built in {time.perf_counter() - t0:.1f} s on {threads} "
+          "threads", file=sys.stderr, flush=True)
+    return m, threads
+
+
+def cpu_token_times(m, positions, token=7):
+    """Seconds of one full decode token (embedding, every layer, final norm, classifier) of
+    one stream at each position. The cache rows before a position are whatever the state
+    holds (zeros unless decoded): the work of a step depends on the position only."""
+    out = []
     for pos in positions:
-        m.set_x(x)
         t0 = time.perf_counter()
-        m.attention_block(0, pos)
-        m.ffn_block(0)
-        t1 = time.perf_counter()
-        m.classify()
-        t2 = time.perf_counter()
-        per_token.append(w["layers"] * (t1 - t0) + (t2 - t1) * w["vocab"] / vslice)
-    m.close()
-    # the port decodes streams one after another
-    return per_token, batch
+        m.step(token, pos)
+        out.append(time.perf_counter() - t0)
+    return out
+
+
+def cpu_streams_sampled(w, batch):
+    """Streams of a batch timed per step by the CPU arms: the port decodes streams one after
+    another at the same cost each, so a step of B streams is B x one stream's token. Large
+    models time one stream per step; small ones up to 8."""
+    big = w["layers"] * (4 * w["dim"] ** 2 + 3 * w["dim"] * w["hidden"]) > 10 ** 9
+    return 1 if big else min(batch, 8)
 
 
 # ----------------------------------------------------------------------------- microbenchmarks
@@ -593,151 +611,144 @@ def run_prefill_micro(args):
         "clocks": clocks.summary(),
         "gpu_launches": launches * args.steps,
     }
+    g.close()
+    rt.close()
     if not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
         pos = [0, P // 4, P // 2, 3 * P // 4, P - 1]
-        per_token, _ = cpu_sample(w, 1, pos, threads)
+        m, threads = cpu_port_model(w, P)
+        per_token = cpu_token_times(m, pos)
+        m.close()
         line["cpu_baseline"] = {
             "value": 1.0 / statistics.mean(per_token), "unit": "tokens/s", "cores": threads,
             "kind": "port", "sample": "the reference feeds a prompt one decode step per token: "
-                                      "one decoder layer x layers + classifier slice at "
-                                      f"positions {pos}"}
-    print(json.dumps(line), flush=True)
-    g.close()
-    rt.close()
-
-
-def run_reference(args, w, rank, world):
-    if rank != 0:
-        return
-    threads = os.cpu_count() or 1
-    nsteps = args.warmup + args.steps
-    positions = [w["prompt"] + i for i in range(nsteps)]
-    per_token, batch = cpu_sample(w, args.batch, positions, threads)
-    timed = per_token[args.warmup:]
-    step_s = statistics.mean(timed) * batch
-    value = batch / step_s
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
-        "config": {"workload": w["title"], "batch": args.batch, "parallelism": "cpu",
-                   "positions": f"{positions[args.warmup]}..{positions[-1]}"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": "one decoder layer x layers + 4096-row classifier slice "
-                                   "scaled to the vocab, per step; streams decoded in turn"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
+                                      "full tokens (every layer, the full classifier) of the "
+                                      f"oracle port at positions {pos}"}
     print(json.dumps(line), flush=True)
 
 
-# ----------------------------------------------------------------------------- GPU
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=256)
-    ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS) +
-                    sorted(MICRO))
-    ap.add_argument("--contexts", default="4096,32768,131072", help="attention microbench")
-    ap.add_argument("--batches", default="1,8,64", help="attention microbench")
-    ap.add_argument("--prompt-len", type=int, default=2048, help="prefill microbench")
-    ap.add_argument("--no-parity", action="store_true",
-                    help="profiling aid: prefill microbench without the token-loop comparison "
-                         "(prints a short line, not a bench line)")
-    ap.add_argument("--batch", type=int, default=0,
-                    help="streams per rank (default: the workload's; the 110M workload's 256 "
-                         "streams are split over the ranks)")
-    ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
-    ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
-                    help="N > 1: tensor parallel (8B default) or independent replicas")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=0, help="default: min(steps, 64)")
-    ap.add_argument("--layers", type=int, default=0,
-                    help="profiling aid: fewer layers of the same shapes (not a bench line)")
-    ap.add_argument("--prompt", type=int, default=0,
-                    help="profiling aid: shorter prompt (fewer launches before the timed loop)")
-    ap.add_argument("--seq", type=int, default=0,
-                    help="profiling aid: smaller KV cache (max context)")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-    if args.workload in MICRO:
-        if int(os.environ.get("RANK", "0")) != 0:
-            return  # single-GPU kernel microbenchmarks: other ranks have nothing to do
-        if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "kernel microbenchmarks "
-                              "report the oracle's CPU rate as cpu_baseline in the main arm"}))
-            return
-        {"ops": run_ops_micro, "attention": run_attention_micro,
-         "prefill": run_prefill_micro}[args.workload](args)
-        return
-    w = dict(WORKLOADS[args.workload])
-    if args.layers:
-        w["layers"] = args.layers
-        w["title"] += f" ({args.layers} layers: profiling case)"
-    if args.prompt:
-        w["prompt"] = args.prompt
-    if args.seq:
-        w["seq"] = args.seq
+def decode_config(w, B, first, last, world, mode):
+    """The `config` object of a decode line; the GPU arm and the reference arm build it with
+    this one function, so the two lines describe the same workload."""
+    return {"workload": w["title"], "batch": B, "seq_len": w["seq"],
+            "positions": f"{first}..{last}",
+            "parallelism": mode if world > 1 else "single",
+            "l2": "inputs larger than L2 (weights stream every step)"}
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    split_streams = False
-    if not args.batch:
-        args.batch = w["batch"]
-        if w.get("split_streams") and world > 1 and args.parallel != "tp":
-            if args.batch % world:
-                raise SystemExit(f"{args.batch} streams do not split over {world} ranks")
-            args.batch //= world
-            split_streams = True
-    if args.impl == "reference":
-        run_reference(args, w, rank, world)
-        return
 
-    import torch
+def timed_positions(w, args):
+    """Positions the timed steps decode: the prompt's forced ids fill positions
+    0 .. prompt - 2, the warm-up steps start at prompt - 1, the timed ones follow."""
+    first = w["prompt"] - 1 + args.warmup
+    return first, first + args.steps - 1
 
-    dist = None
-    if world > 1:
-        import datetime
 
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        with StdoutToStderr():
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
-
-    import ammon_b200 as ab
-
-    B = args.batch
-    rt = ab.create_runtime(local)
-    cfg = ab.LlamaConfig(w["dim"], w["layers"], w["heads"], w["kv_heads"], w["head_dim"],
-                         w["hidden"], w["vocab"], w["seq"], batch=B, rope_theta=w["theta"],
-                         dtype=ab.BF16 if w["bf16"] else ab.F32)
+def parallel_mode(w, args, world):
     mode = args.parallel
     if mode == "auto":
         mode = "tp" if w["bf16"] else "replicas"
+    if world == 1:
+        return "single"
+    if mode == "tp":
+        return f"tp{world}"
+    return f"dp{world}" if w.get("split_streams") else f"replicas{world}"
+
+
+def stream_assignment(w, batch, parallel, world, rank):
+    """(streams this rank decodes, global id of its first stream, whether the workload's
+    streams are split over the ranks). The 110M workload's 256 independent streams split
+    data-parallel into contiguous blocks of 256 / world per rank with no collective; tensor
+    parallel ranks all decode the same streams (0 ..); replicas each decode their own batch
+    (rank * batch ..). An explicit batch is per rank and never split."""
+    mode = parallel
+    if mode == "auto":
+        mode = "tp" if w["bf16"] else "replicas"
     tp = world > 1 and mode == "tp"
-    comm = None
-    if tp:
-        # rank 0 makes the NCCL id of the model's communicator; torch.distributed carries it
-        with StdoutToStderr():
-            uid = torch.zeros(ab._abi.COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
-            if rank == 0:
-                uid.copy_(torch.frombuffer(bytearray(ab.Comm.unique_id()), dtype=torch.uint8))
-            dist.broadcast(uid, 0)
-            comm = ab.Comm(rt, bytes(uid.cpu().numpy().tobytes()), rank, world)
+    if batch:
+        return batch, 0 if tp else rank * batch, False
+    batch = w["batch"]
+    if w.get("split_streams") and world > 1 and not tp:
+        if batch % world:
+            raise SystemExit(f"{batch} streams do not split over {world} ranks")
+        per = batch // world
+        return per, rank * per, True
+    return batch, 0 if tp else rank * batch, False
+
+
+def batch64_wanted(args, w):
+    """The default 8B line carries batch 64 as a sub-record (BASELINE metric: batch 1 and
+    64); other workloads and explicit --batch runs report one batch."""
+    return (args.workload == "llama3-8b-bf16" and not args.batch_given and not args.layers
+            and not args.no_batch64)
+
+
+def run_reference(args, w, rank, world):
+    """The reference arm: the oracle port of the reference's per-token kernels on the host
+    cores, full tokens (every layer and the full classifier) at the positions the GPU arm
+    times, streams decoded one after another."""
+    if rank != 0:
+        return
+    first, last = timed_positions(w, args)
+    positions = list(range(first - args.warmup, last + 1))
+    m, threads = cpu_port_model(w, last + 1)
+    mode = parallel_mode(w, args, world)
+
+    def arm(B):
+        S = cpu_streams_sampled(w, B)
+        steps = []
+        for pos in positions:
+            steps.append(sum(cpu_token_times(m, [pos] * S)) * B / S)
+        timed = steps[args.warmup:]
+        step_s = statistics.mean(timed)
+        value = B / step_s
+        sample = (f"full tokens of the oracle port at positions {first}..{last}, "
+                  + ("one stream per step" if S == 1 else f"{S} streams per step")
+                  + (f", scaled to the batch's {B} streams (decoded one after another)"
+                     if S < B else ""))
+        return {"value": value, "ms_per_step": step_s * 1e3,
+                "config": decode_config(w, B, first, last, world, mode),
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                                 "kind": "port", "sample": sample},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+
+    top = arm(args.batch)
+    line = {"impl": "reference", "metric": METRIC, "value": top["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": top["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
+            "config": top["config"], "cpu_baseline": top["cpu_baseline"], "e2e": top["e2e"]}
+    if batch64_wanted(args, w):
+        sub = arm(64)
+        line["batch64"] = {"value": sub["value"], "unit": "tokens/s",
+                           "ms_per_step": sub["ms_per_step"], "config": sub["config"],
+                           "cpu_baseline": sub["cpu_baseline"], "e2e": sub["e2e"]}
+    m.close()
+    print(json.dumps(line), flush=True)
+
+
+def run_decode(args, w, B, env):
+    """One decode line of the GPU arm at batch B (per rank): the device greedy loop timed
+    between CUDA events (max over ranks), e2e through step(), per-kernel times and the
+    roofline of the dominant kernel."""
+    import numpy as np
+    import torch
+
+    import ammon_b200 as ab
+
+    rank, world, local, dist = env["rank"], env["world"], env["local"], env["dist"]
+    tp, split_streams = env["tp"], env["split_streams"]
+    rt = env["rt"]
+    cfg = ab.LlamaConfig(w["dim"], w["layers"], w["heads"], w["kv_heads"], w["head_dim"],
+                         w["hidden"], w["vocab"], w["seq"], batch=B, rope_theta=w["theta"],
+                         dtype=ab.BF16 if w["bf16"] else ab.F32)
     with StdoutToStderr():
-        model = ab.LlamaModel(rt, cfg, comm)
+        model = ab.LlamaModel(rt, cfg, env["comm"])
         model.init_synthetic(w["seed"], 0.02)
     P = w["prompt"]
-    # tensor parallel ranks decode the same streams; replicas each decode their own
-    sbase = 0 if tp else rank * B
+    # tensor parallel ranks decode the same streams; replicas and data-parallel ranks each
+    # decode their own (batch 64 of the default line: streams 0..63 on every arm)
+    sbase = env["sbase"] if B == env["batch"] else (0 if tp else rank * B)
     prompts = [prompt_tokens(w["seed"], 1000 + sbase + b, P, 3, w["vocab"]) for b in range(B)]
     # prompt: forced tokens at positions 0..P-2
     for pos in range(P - 1):
@@ -775,6 +786,7 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t = float(tt.item())
     start_tok = toks[-1].tolist()
+    first, last = pos0, pos0 + args.steps - 1
     pos0 += args.steps
     streams = B if tp else world * B
     value = streams * args.steps / t
@@ -784,8 +796,6 @@ def main():
                       if "allreduce" not in l and "allgather" not in l]) + (2 if tp else 1)
 
     # e2e through the reference-facing step(): DecodeSteps up, [B, vocab] logits down
-    import numpy as np
-
     tok = start_tok
     if dist:
         dist.barrier()
@@ -818,29 +828,23 @@ def main():
     t_launch = ms_dom / n_dom / 1e3
     peak, peak_kind = load_peaks()
     achieved = lb[dom] / t_launch / 1e9 if dom in lb else None
-    # the timed loop decoded positions pos0 - steps .. pos0 - 1 (the e2e loop after it does not
-    # advance pos0)
-    mean_pos = pos0 - args.steps + (args.steps - 1) / 2
+    mean_pos = (first + last) / 2
     sb = step_bytes(w, B, mean_pos, shards)
-
+    suffix = "" if B == 1 else f"_b{B}"
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong" if tp or split_streams else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if w["bf16"] else "f32", "data": "synthetic",
-        "config": {"workload": w["title"], "batch": B, "seq_len": w["seq"],
-                   "positions": f"{pos0 - args.steps}..{pos0 - 1}",
-                   "parallelism": (f"tp{world}" if tp else f"dp{world}" if split_streams
-                                   else f"replicas{world}") if world > 1 else "single",
-                   "l2": "inputs larger than L2 (weights stream every step)"},
+        "config": decode_config(w, B, first, last, world, parallel_mode(w, args, world)),
         "step_bytes": sb, "step_gbs": sb / (t / args.steps) / 1e9,
         "step_frac": sb / (t / args.steps) / 1e9 / peak,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,
                      "bytes_per_launch": lb.get(dom), "launch_ms": t_launch * 1e3,
-                     "traffic": profile_traffic(dom, args.workload, lb.get(dom))},
+                     "traffic": profile_traffic(dom, args.workload + suffix, lb.get(dom))},
         "kernels": {l: {"launches": c[0], "ms": round(c[1], 4),
                         "share": round(c[1] / total_ms, 4),
                         "gbs": round(lb[l] * c[0] / (c[1] / 1e3) / 1e9, 1) if l in lb else None}
@@ -850,18 +854,127 @@ def main():
         "gpu_launches": nodes_loop * args.steps,
         "clocks": clocks.summary(),
     }
+    model.close()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--workload", default="llama3-8b-bf16", choices=sorted(WORKLOADS) +
+                    sorted(MICRO))
+    ap.add_argument("--contexts", default="4096,32768,131072", help="attention microbench")
+    ap.add_argument("--batches", default="1,8,64", help="attention microbench")
+    ap.add_argument("--prompt-len", type=int, default=2048, help="prefill microbench")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="profiling aid: prefill microbench without the token-loop comparison "
+                         "(prints a short line, not a bench line)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="streams per rank (default: the workload's; the 110M workload's 256 "
+                         "streams are split over the ranks)")
+    ap.add_argument("--no-batch64", action="store_true",
+                    help="the default 8B line without its batch-64 sub-record")
+    ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
+    ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
+                    help="N > 1: tensor parallel (8B default) or independent replicas")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="default: min(steps, 64)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling aid: fewer layers of the same shapes (not a bench line)")
+    ap.add_argument("--prompt", type=int, default=0,
+                    help="profiling aid: shorter prompt (fewer launches before the timed loop)")
+    ap.add_argument("--seq", type=int, default=0,
+                    help="profiling aid: smaller KV cache (max context)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    args.batch_given = args.batch > 0
+    if args.workload in MICRO:
+        if int(os.environ.get("RANK", "0")) != 0:
+            return  # single-GPU kernel microbenchmarks: other ranks have nothing to do
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "kernel microbenchmarks "
+                              "report the oracle's CPU rate as cpu_baseline in the main arm"}))
+            return
+        {"ops": run_ops_micro, "attention": run_attention_micro,
+         "prefill": run_prefill_micro}[args.workload](args)
+        return
+    w = dict(WORKLOADS[args.workload])
+    if args.layers:
+        w["layers"] = args.layers
+        w["title"] += f" ({args.layers} layers: profiling case)"
+    if args.prompt:
+        w["prompt"] = args.prompt
+    if args.seq:
+        w["seq"] = args.seq
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    args.batch, sbase, split_streams = stream_assignment(w, args.batch, args.parallel, world,
+                                                         rank)
+    if args.impl == "reference":
+        run_reference(args, w, rank, world)
+        return
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        with StdoutToStderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+
+    import ammon_b200 as ab
+
+    rt = ab.create_runtime(local)
+    mode = args.parallel
+    if mode == "auto":
+        mode = "tp" if w["bf16"] else "replicas"
+    tp = world > 1 and mode == "tp"
+    comm = None
+    if tp:
+        # rank 0 makes the NCCL id of the model's communicator; torch.distributed carries it
+        with StdoutToStderr():
+            uid = torch.zeros(ab._abi.COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(ab.Comm.unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            comm = ab.Comm(rt, bytes(uid.cpu().numpy().tobytes()), rank, world)
+    env = dict(rank=rank, world=world, local=local, dist=dist, tp=tp, sbase=sbase,
+               batch=args.batch,
+               split_streams=split_streams, rt=rt, comm=comm)
+    line = run_decode(args, w, args.batch, env)
+    if batch64_wanted(args, w):
+        sub = run_decode(args, w, 64, env)
+        line["batch64"] = {k: sub[k] for k in (
+            "value", "unit", "ms_per_step", "config", "step_bytes", "step_gbs", "step_frac",
+            "roofline", "kernels", "e2e", "gpu_launches", "clocks")}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        cpos = [w["prompt"] + i for i in range(3)]
-        per_token, batch = cpu_sample(w, B, cpos, threads)
+        first, last = timed_positions(w, args)
+        cpos = [first, (first + last) // 2, last]
+        m, threads = cpu_port_model(w, last + 1)
+        per_token = cpu_token_times(m, cpos)
+        m.close()
         v = 1.0 / statistics.mean(per_token)
-        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": "oracle: one decoder layer x layers + 4096-row "
-                                          "classifier slice scaled to the vocab, positions "
-                                          f"{cpos[0]}..{cpos[-1]}, one stream"}
+        base = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": "full tokens (every layer, the full classifier) of the oracle port "
+                          f"at positions {cpos}, one stream"}
+        line["cpu_baseline"] = base
+        if "batch64" in line:
+            line["batch64"]["cpu_baseline"] = dict(
+                base, sample=base["sample"] + "; the port decodes the 64 streams one after "
+                                              "another, 64 such tokens per step")
     if rank == 0:
         print(json.dumps(line), flush=True)
-    model.close()
     if comm is not None:
         comm.close()
     rt.close()

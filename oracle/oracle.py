@@ -294,12 +294,38 @@ class Model:
         self._s = lib().or_state_create(self._m)
 
     def close(self):
-        if self._s:
-            lib().or_state_destroy(self._s)
-            self._s = None
+        states = getattr(self, "_states", {0: self._s})
+        states[None] = self._s
+        for h in {v for v in states.values() if v}:
+            lib().or_state_destroy(h)
+        self._states = {}
+        self._s = None
         if self._m:
             lib().or_model_destroy(self._m)
             self._m = None
+
+    def select_stream(self, k):
+        """Make decode state k current (one KV cache per stream, sharing the weights); state
+        0 is the one the model starts with, others are created zeroed on first use."""
+        if not hasattr(self, "_states"):
+            self._states = {0: self._s}
+        if k not in self._states:
+            self._states[k] = lib().or_state_create(self._m)
+        self._s = self._states[k]
+
+    def set_cache(self, layer, key, value):
+        """Overwrite layer `layer` of the current state's K/V cache ([seq, kv_heads, head]:
+        float32 values, or uint16 bf16 bits for a bf16 model)."""
+        c = self.cfg
+        per = c.seq * c.kv_heads * c.head_dim
+        dt, ct = (np.uint16, C.c_uint16) if self.bf16 else (np.float32, C.c_float)
+        for which, src in ((0, key), (1, value)):
+            src = np.ascontiguousarray(src, dt).ravel()
+            if src.size != per:
+                raise ValueError(f"cache layer needs {per} elements, got {src.size}")
+            ptr = lib().or_state_cache(self._s, which)
+            dst = np.frombuffer((ct * (c.layers * per)).from_address(ptr), dt)
+            dst[layer * per:(layer + 1) * per] = src
 
     def __del__(self):
         try:
@@ -308,8 +334,15 @@ class Model:
             pass
 
     def reset(self):
+        """Zero the current decode state (a new sequence)."""
+        fresh = lib().or_state_create(self._m)
+        states = getattr(self, "_states", None)
+        if states is not None:
+            for k, v in states.items():
+                if v == self._s:
+                    states[k] = fresh
         lib().or_state_destroy(self._s)
-        self._s = lib().or_state_create(self._m)
+        self._s = fresh
 
     def weight(self, name, layer=0) -> np.ndarray:
         """Copy of one weight tensor: float32 for gains and fp32 models, uint16 bf16
