@@ -324,7 +324,13 @@ def test_swiglu_result_independent_of_kernel_and_ksplit(rt, orc, dtype, monkeypa
     assert "ffn_gate_up_swiglu_splitk" in labels_split, labels_split
     assert "ffn_gate_up_swiglu_splitk" not in labels_single, labels_single
     assert np.array_equal(split, single)
-    assert np.array_equal(split[:4], gemv)
+    if dt == ab.BF16:
+        assert np.array_equal(split[:4], gemv)
+    else:
+        # 3xTF32 carries the f32 w2 operand as tf32 hi + lo halves, and lo keeps 11 of its up
+        # to 13 significant bits: the identity projection of hb is exact to ~2^-22 relative,
+        # far below one ulp of the +-4096 residual it lands on
+        assert np.abs(split[:4] - gemv).max() <= 2.0 ** -10
     # and the value itself: silu(g) * u of the exact integer sums, against float64
     g = x_host[:8] / 4096.0 @ w1.T.astype(np.float64)
     u = x_host[:8] / 4096.0 @ w3.T.astype(np.float64)

@@ -59,11 +59,20 @@ def oracle_8b(orc):
     m.close()
 
 
-def _model_8b(rt, batch):
+def _model_8b(rt, batch, fused=True):
     c = L8B
-    g = ab.LlamaModel(rt, ab.LlamaConfig(c["dim"], c["layers"], c["heads"], c["kv_heads"],
-                                         c["head_dim"], c["hidden"], c["vocab"], c["seq"],
-                                         batch=batch, rope_theta=c["theta"], dtype=ab.BF16))
+    old = os.environ.get("AMMON_B200_FUSED_STEP")
+    os.environ["AMMON_B200_FUSED_STEP"] = "1" if fused else "0"
+    try:
+        g = ab.LlamaModel(rt, ab.LlamaConfig(c["dim"], c["layers"], c["heads"], c["kv_heads"],
+                                             c["head_dim"], c["hidden"], c["vocab"], c["seq"],
+                                             batch=batch, rope_theta=c["theta"],
+                                             dtype=ab.BF16))
+    finally:
+        if old is None:
+            os.environ.pop("AMMON_B200_FUSED_STEP")
+        else:
+            os.environ["AMMON_B200_FUSED_STEP"] = old
     g.init_synthetic(3, 0.02)
     return g
 
@@ -101,14 +110,22 @@ def _check_step(g, o, batch, streams, tokens, positions, tag):
     return logits, am
 
 
-def test_llama3_8b_shape_batch1_gemv(rt, orc, oracle_8b):
-    """Batch 1: every projection on the GEMV (K = 4096 and 14336), the 128256-row classifier,
-    attention over 129 and 601 positions (the second step reads the first step's row)."""
-    g = _model_8b(rt, 1)
+@pytest.mark.parametrize("path", ["fused", "graph"])
+def test_llama3_8b_shape_batch1(rt, orc, oracle_8b, path):
+    """Batch 1, both ways the library runs it: the persistent single-launch step (the default)
+    and the per-kernel step graph (GEMV projections at K = 4096 and 14336, the 128256-row
+    classifier); attention over 129 and 601 positions (the second step reads the first
+    step's row)."""
+    g = _model_8b(rt, 1, fused=path == "fused")
     o = oracle_8b
+    o.select_stream(0)
     _seed_caches(g, o, 1, [0], seed=31)
     labels = g.scheme().node_labels()
-    assert "final_norm_classifier" in labels and not any(l.endswith("_splitk") for l in labels)
+    if path == "fused":
+        assert labels == ["decode_step"]
+    else:
+        assert "final_norm_classifier" in labels
+        assert not any(l.endswith("_splitk") for l in labels)
     for pos, tok in ((128, 91234), (600, 17)):
         logits, am = _check_step(g, o, 1, [0], [tok], [pos], f"b1 pos {pos}")
         want = o.tensor("logits")
@@ -239,8 +256,9 @@ def test_split_attention_long_context_matches_float64(rt, ctx, batch):
     vc = ab.Tensor.zeros(rt, (batch, ctx, KV, hd), ab.BF16).fill_normal(2, 3)
     q = ab.Tensor.zeros(rt, (batch, H, hd)).fill_normal(2, 1)
     out = ab.Tensor.zeros(rt, (batch, H * hd))
-    positions = [ctx - 1 - 977 * b for b in range(batch)]
+    positions = [ctx - 1 - (ctx // (batch + 1)) * b - 37 * (b % 2) for b in range(batch)]
     positions[-1] = ctx - 1
+    assert all(0 <= p < ctx for p in positions)
     st = ab.DecodeStep.parcel(rt, batch)
     rt.deposit(st, [ab.DecodeStep(0, p) for p in positions])
     s = rt.scheme()
