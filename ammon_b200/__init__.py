@@ -725,6 +725,19 @@ class LlamaModel:
         s.close = lambda: None  # owned by the model
         return s
 
+    def step_trace(self):
+        """[barriers, grid] %globaltimer ns of each CTA's arrival at each grid barrier of the
+        last persistent decode step (AMMON_B200_STEP_TRACE set at creation), or None."""
+        nb, ng = C.c_uint32(), C.c_uint32()
+        _check(_abi.lib().ab_llama_step_trace(self._h, None, 0, C.byref(nb), C.byref(ng)))
+        if nb.value == 0:
+            return None
+        out = np.zeros((nb.value, ng.value), np.uint64)
+        _check(_abi.lib().ab_llama_step_trace(
+            self._h, out.ctypes.data_as(C.POINTER(C.c_uint64)), out.size, C.byref(nb),
+            C.byref(ng)))
+        return out
+
     def logits_tensor(self) -> Tensor:
         t = _abi.Tensor_t()
         _check(_abi.lib().ab_llama_logits(self._h, C.byref(t)))

@@ -144,6 +144,8 @@ SIGNATURES = {
                                            C.POINTER(i32), u32, C.POINTER(u32),
                                            C.POINTER(C.c_double)]),
     "ab_llama_scheme": (C.c_int, [P, PP]),
+    "ab_llama_step_trace": (C.c_int, [P, C.POINTER(C.c_uint64), u32, C.POINTER(u32),
+                                      C.POINTER(u32)]),
     "ab_llama_logits": (C.c_int, [P, C.POINTER(T)]),
     "ab_llama_reset": (C.c_int, [P]),
     "ab_llama_as_model": (C.c_int, [P, C.POINTER(Model_t)]),

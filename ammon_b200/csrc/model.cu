@@ -198,6 +198,7 @@ struct ab_llama {
     ab_scheme* scheme = nullptr;       // one decode step (gathers the logits under TP)
     ab_scheme* loop_scheme = nullptr;  // one decode step + device sample feedback
     GemmScratch cls_tc;                // classifier's tensor-core GEMM scratch
+    FusedStep* fused = nullptr;        // persistent single-launch step (batch 1, bf16)
     float* h_logits = nullptr;         // pinned [batch, vocab]
     int32_t* h_argmax = nullptr;
     ab_decode_step* h_steps = nullptr;
@@ -270,6 +271,7 @@ void destroy_model(ab_llama* m) {
     free_prefill(m);
     if (m->scheme) ab_scheme_destroy(m->scheme);
     if (m->loop_scheme) ab_scheme_destroy(m->loop_scheme);
+    fused_step_destroy(m->fused);
     free_tc_scratch(&m->cls_tc);
     if (m->attn) ab_attention_block_destroy(m->attn);
     if (m->ffn) ab_swiglu_block_destroy(m->ffn);
@@ -400,6 +402,10 @@ void record_head(ab_llama* m, ab_scheme* s, const HeadOut& h, bool gather_logits
 void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
     s->nodes.clear();
     s->dirty = true;
+    if (m->fused) {
+        record_fused_step(s, m->fused, feedback);
+        return;
+    }
     const auto& c = m->c;
     ab_tensor x = m->x;
     if (c.batch == 1) {
@@ -602,6 +608,47 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
                    "pinned steps");
         check(ab_scheme_create(rt, &m->scheme));
         check(ab_scheme_create(rt, &m->loop_scheme));
+        if (world == 1 && fused_step_enabled()) {
+            FusedStepModel fm;
+            fm.batch = c.batch;
+            fm.layers = c.layers;
+            fm.dim = c.dim;
+            fm.heads = c.heads;
+            fm.kv_heads = c.kv_heads;
+            fm.head_dim = c.head_dim;
+            fm.hidden = c.hidden;
+            fm.vocab = c.vocab;
+            fm.seq = c.seq;
+            fm.dtype = c.dtype;
+            fm.rope_theta = c.rope_theta;
+            fm.norm_eps = c.norm_eps;
+            if (fused_step_unsupported(fm, rt->sm_count).empty()) {
+                fm.embed = m->embed.data;
+                fm.wcls = m->wcls.data;
+                fm.rms_final = m->rms_final.data;
+                for (uint32_t l = 0; l < c.layers; l++) {
+                    fm.rms_att.push_back(m->rms_att[l].data);
+                    fm.wq.push_back(m->wq[l].data);
+                    fm.wk.push_back(m->wk[l].data);
+                    fm.wv.push_back(m->wv[l].data);
+                    fm.wo.push_back(m->wo[l].data);
+                    fm.rms_ffn.push_back(m->rms_ffn[l].data);
+                    fm.w1.push_back(m->w1[l].data);
+                    fm.w2.push_back(m->w2[l].data);
+                    fm.w3.push_back(m->w3[l].data);
+                    ab_tensor key, value;
+                    check(ab_kvcache_layer(m->cache, l, &key, &value));
+                    fm.kcache.push_back(key.data);
+                    fm.vcache.push_back(value.data);
+                }
+                fm.x = (float*)m->x.data;
+                fm.logits = (float*)m->logits.data;
+                fm.argmax = (int32_t*)m->argmax.data;
+                fm.step = m->step.data;
+                fm.history = (int32_t*)m->history.data;
+                m->fused = fused_step_create(rt, fm);
+            }
+        }
     } catch (...) {
         destroy_model(m);
         throw;
@@ -1004,6 +1051,22 @@ int ab_llama_generate_tokens(ab_llama* m, const int32_t* prompt, uint32_t prompt
         }
         if (out_len) *out_len = n;
         if (tokens_per_second) *tokens_per_second = elapsed > 0.0 ? decoded / elapsed : 0.0;
+    });
+}
+
+int ab_llama_step_trace(ab_llama* m, uint64_t* out, uint32_t cap, uint32_t* barriers,
+                        uint32_t* grid) {
+    return guard([&] {
+        if (!m || !barriers || !grid) fail(AB_ERR_ARGUMENT, "null argument");
+        std::vector<uint64_t> t;
+        m->rt->activate();
+        cuda_check(cudaStreamSynchronize(m->rt->stream), "trace synchronize");
+        if (!fused_step_trace(m->fused, &t, barriers, grid)) {
+            *barriers = 0;
+            *grid = 0;
+            return;
+        }
+        if (out) std::memcpy(out, t.data(), std::min<size_t>(cap, t.size()) * 8);
     });
 }
 

@@ -233,6 +233,37 @@ uint32_t attention_max_splits(uint32_t max_groups, uint32_t seq, int sm_count,
 bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t kv_dtype);
 void record_attention(ab_scheme* s, const char* label, AttnParams p);
 
+// ---- persistent decode step (step_fused.cu) ----------------------------------------------
+// What the single-launch batch-1 decode step reads and writes (device pointers; per-layer
+// K/V caches are [seq, kv_heads, head] views).
+struct FusedStepModel {
+    uint32_t batch, layers, dim, heads, kv_heads, head_dim, hidden, vocab, seq;
+    int32_t dtype;
+    float rope_theta, norm_eps;
+    const void* embed;
+    const void* wcls;
+    const void* rms_final;
+    std::vector<const void*> rms_att, wq, wk, wv, wo, rms_ffn, w1, w2, w3;
+    std::vector<void*> kcache, vcache;
+    float* x;
+    float* logits;
+    int32_t* argmax;
+    void* step;
+    int32_t* history;
+};
+struct FusedStep;
+// AMMON_B200_FUSED_STEP=0 turns the persistent step off (the per-kernel step graph runs).
+bool fused_step_enabled();
+// "" when the persistent step can run the model, else the reason it cannot.
+std::string fused_step_unsupported(const FusedStepModel& m, int sms);
+FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m);
+void fused_step_destroy(FusedStep* f);
+// One node "decode_step" (a cooperative launch); with feedback the argmax becomes the next
+// DecodeStep and the token history entry, as feedback_kernel does for the step graph.
+void record_fused_step(ab_scheme* s, FusedStep* f, bool feedback);
+bool fused_step_trace(FusedStep* f, std::vector<uint64_t>* out, uint32_t* barriers,
+                      uint32_t* grid);
+
 // Rejects batched shapes the single-row reference kernels cannot take.
 void record_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x);
 void record_rmsnorm_ref(ab_scheme* s, ab_tensor x, ab_tensor weight, ab_tensor o, float eps);

@@ -792,8 +792,12 @@ def run_decode(args, w, B, env):
     value = streams * args.steps / t
     # our kernels per device-loop step: the step graph's kernel nodes (not the NCCL
     # collectives, not the logits gather of step()) plus the sample feedback
-    nodes_loop = len([l for l in model.scheme().node_labels()
-                      if "allreduce" not in l and "allgather" not in l]) + (2 if tp else 1)
+    step_labels = model.scheme().node_labels()
+    if step_labels == ["decode_step"]:
+        nodes_loop = 1  # the persistent step: its last CTA also writes the next DecodeStep
+    else:
+        nodes_loop = len([l for l in step_labels
+                          if "allreduce" not in l and "allgather" not in l]) + (2 if tp else 1)
 
     # e2e through the reference-facing step(): DecodeSteps up, [B, vocab] logits down
     tok = start_tok
@@ -823,6 +827,8 @@ def run_decode(args, w, B, env):
     shards = world if tp else 1
     # the timed nodes replay the last deposited steps: the e2e loop's final position
     lb = layer_bytes(w, B, shards, attn_pos=pos0 + e2e_steps - 1)
+    # the persistent single-launch step moves one whole step's algorithmic bytes
+    lb["decode_step"] = step_bytes(w, B, pos0 + e2e_steps - 1, shards)
     dom = max(per_label, key=lambda l: per_label[l][1])
     n_dom, ms_dom = per_label[dom]
     t_launch = ms_dom / n_dom / 1e3

@@ -347,6 +347,13 @@ int ab_llama_generate_tokens(ab_llama* m, const int32_t* prompt, uint32_t prompt
                              uint32_t max_new_tokens, int32_t has_stop, int32_t stop_on,
                              int32_t* out_tokens, uint32_t cap, uint32_t* out_len,
                              double* tokens_per_second);
+/* Profiling aid with no reference counterpart: when the model runs its decode step as the
+ * persistent single launch (batch 1, bf16, one GPU; AMMON_B200_STEP_TRACE set at model
+ * creation), the %globaltimer nanoseconds at which each CTA arrived at each grid barrier of
+ * the last step, [barriers][grid] (the first min(cap, barriers * grid) values); *barriers and
+ * *grid are 0 when no trace is kept. */
+int ab_llama_step_trace(ab_llama* m, uint64_t* out, uint32_t cap, uint32_t* barriers,
+                        uint32_t* grid);
 /* The model's step scheme (recorded on first use), for profiling. */
 int ab_llama_scheme(ab_llama* m, ab_scheme** out);
 /* Device logits [batch, vocab] of the last step. */
