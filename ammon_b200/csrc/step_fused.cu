@@ -59,17 +59,18 @@ constexpr uint32_t kPsGainOff = 24 * 1024;
 
 enum : uint32_t { kPhQkv = 0, kPhWo = 1, kPhGateUp = 2, kPhDown = 3, kPhCls = 4 };
 
-// dot of eight bf16 weights with eight bf16 activations (one 16-byte vector each)
-__device__ __forceinline__ float dot_bf16x8(const uint4& w, const uint4& x, float acc) {
-    acc = fmaf(bf16lo(w.x), bf16lo(x.x), acc);
-    acc = fmaf(bf16hi(w.x), bf16hi(x.x), acc);
-    acc = fmaf(bf16lo(w.y), bf16lo(x.y), acc);
-    acc = fmaf(bf16hi(w.y), bf16hi(x.y), acc);
-    acc = fmaf(bf16lo(w.z), bf16lo(x.z), acc);
-    acc = fmaf(bf16hi(w.z), bf16hi(x.z), acc);
-    acc = fmaf(bf16lo(w.w), bf16lo(x.w), acc);
-    acc = fmaf(bf16hi(w.w), bf16hi(x.w), acc);
-    return acc;
+// dot of eight bf16 weights with eight bf16 activations (one 16-byte vector each) over two
+// accumulators: even elements into a0, odd into a1
+__device__ __forceinline__ void dot_bf16x8_2(const uint4& w, const uint4& x, float& a0,
+                                             float& a1) {
+    a0 = fmaf(bf16lo(w.x), bf16lo(x.x), a0);
+    a1 = fmaf(bf16hi(w.x), bf16hi(x.x), a1);
+    a0 = fmaf(bf16lo(w.y), bf16lo(x.y), a0);
+    a1 = fmaf(bf16hi(w.y), bf16hi(x.y), a1);
+    a0 = fmaf(bf16lo(w.z), bf16lo(x.z), a0);
+    a1 = fmaf(bf16hi(w.z), bf16hi(x.z), a1);
+    a0 = fmaf(bf16lo(w.w), bf16lo(x.w), a0);
+    a1 = fmaf(bf16hi(w.w), bf16hi(x.w), a1);
 }
 
 struct PsLayer {
@@ -94,7 +95,8 @@ struct PsParams {
     bf16* h;          // [F] SwiGLU output (feeds w2)
     float* logits;    // [V]
     float* part;      // attention block partials O [KV][grid][G][hd]
-    float* part_ml;   // and their (max, sum) [KV][grid][G][2]
+    float* part_ml;   // and their (max, sum) [KV][ml_stride] ([grid][G][2] used)
+    uint32_t ml_stride;  // floats per kv head in part_ml (a multiple of 4)
     uint32_t* tickets;  // [KV + 1]: attention folds, then the argmax merge
     float* cand_v;    // [grid] best logit of each CTA
     uint32_t* cand_i;
@@ -167,6 +169,12 @@ __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
     return v;
 }
 
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ bool aborted(const PsParams& p) { return ld_relaxed(p.bar + 2) != 0; }
 
 __device__ __forceinline__ void raise_abort(const PsParams& p) {
@@ -228,7 +236,9 @@ __device__ __forceinline__ void cta_range(uint32_t units, uint32_t* u0, uint32_t
 }
 
 // ---- producer ------------------------------------------------------------------------------
-// Streams the CTA's rows of one phase into the ring; g counts chunks over the whole step.
+// Streams the CTA's rows of one phase into the ring; g counts chunks over the whole step. One
+// thread: its reaction time (slot freed -> copies issued) is part of every ring round trip,
+// so it keeps the layer's pointers in registers and does nothing else.
 __device__ bool produce_phase(const PsParams& p, const PsSmem& s, uint32_t kind, uint32_t l,
                               uint32_t& g) {
     const PsGeom gm = ps_geom(p, kind);
@@ -293,24 +303,45 @@ __device__ __forceinline__ void chunk_dots(const unsigned char* slot, const unsi
     const uint32_t lane = threadIdx.x % 32, nv = K / 8;
     const uint4* w = reinterpret_cast<const uint4*>(slot);
     const uint4* xv = reinterpret_cast<const uint4*>(act);
+    // two accumulator chains per row (even and odd elements): twice the independent FMAs
+    float a0[kPsMaxRows], a1[kPsMaxRows];
 #pragma unroll
-    for (uint32_t r = 0; r < kPsMaxRows; r++) acc[r] = 0.0f;
+    for (uint32_t r = 0; r < kPsMaxRows; r++) a0[r] = a1[r] = 0.0f;
     if (rows == kPsMaxRows) {
         for (uint32_t j = lane; j < nv; j += 32) {
             const uint4 x = xv[j];
 #pragma unroll
-            for (uint32_t r = 0; r < kPsMaxRows; r++) acc[r] = dot_bf16x8(w[r * nv + j], x, acc[r]);
+            for (uint32_t r = 0; r < kPsMaxRows; r++) dot_bf16x8_2(w[r * nv + j], x, a0[r], a1[r]);
         }
+    } else if (rows == 1) {
+        // one long row (a w2 row): four vectors in flight per lane, four accumulator chains
+        uint32_t j = lane;
+        for (; j + 96 < nv; j += 128) {
+            uint4 xa[4], wa[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                xa[k] = xv[j + 32 * k];
+                wa[k] = w[j + 32 * k];
+            }
+            dot_bf16x8_2(wa[0], xa[0], a0[0], a1[0]);
+            dot_bf16x8_2(wa[1], xa[1], a0[1], a1[1]);
+            dot_bf16x8_2(wa[2], xa[2], a0[2], a1[2]);
+            dot_bf16x8_2(wa[3], xa[3], a0[3], a1[3]);
+        }
+        for (; j < nv; j += 32) dot_bf16x8_2(w[j], xv[j], a0[0], a1[0]);
+        a0[0] += a0[1] + a0[2] + a0[3];
+        a1[0] += a1[1] + a1[2] + a1[3];
+        a0[1] = a0[2] = a0[3] = a1[1] = a1[2] = a1[3] = 0.0f;
     } else {
         for (uint32_t j = lane; j < nv; j += 32) {
             const uint4 x = xv[j];
 #pragma unroll
             for (uint32_t r = 0; r < kPsMaxRows; r++)
-                if (r < rows) acc[r] = dot_bf16x8(w[r * nv + j], x, acc[r]);
+                if (r < rows) dot_bf16x8_2(w[r * nv + j], x, a0[r], a1[r]);
         }
     }
 #pragma unroll
-    for (uint32_t r = 0; r < kPsMaxRows; r++) acc[r] = warp_sum(acc[r]);
+    for (uint32_t r = 0; r < kPsMaxRows; r++) acc[r] = warp_sum(a0[r] + a1[r]);
 }
 
 struct PsBest {
@@ -417,16 +448,13 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
         uint32_t ok = s.misc[2] == 0;
         if (p.stall_barrier == epoch && blockIdx.x == 0) ok = 0;  // test hook: never arrives
         if (ok && p.trace)
-            p.trace[(uint64_t)(epoch - 1) * gridDim.x + blockIdx.x] = global_timer_ns();
-        if (ok) {
-            __threadfence();
-            atomicAdd(p.bar, 1u);
-        }
+            p.trace[((uint64_t)(epoch - 1) * 3 + 0) * gridDim.x + blockIdx.x] = global_timer_ns();
+        if (ok) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const uint32_t target = epoch * gridDim.x;
-        if (ok && ld_relaxed(p.bar) < target) {
+        if (ok && ld_acquire(p.bar) < target) {
             const uint64_t t0 = global_timer_ns();
             uint32_t n = 0;
-            while (ld_relaxed(p.bar) < target) {
+            while (ld_acquire(p.bar) < target) {
                 if ((++n & 15) == 0) {
                     if (aborted(p)) {
                         ok = 0;
@@ -440,11 +468,18 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
                 }
             }
         }
-        __threadfence();
         s.misc[0] = ok;
+        if (ok && p.trace)
+            p.trace[((uint64_t)(epoch - 1) * 3 + 1) * gridDim.x + blockIdx.x] = global_timer_ns();
     }
     consumers_sync();
     return s.misc[0] != 0;
+}
+
+// Trace point: the CTA has staged the operand of the phase that ends at barrier epoch + 1.
+__device__ __forceinline__ void trace_staged(const PsParams& p, uint32_t epoch) {
+    if (p.trace && threadIdx.x == 0)
+        p.trace[((uint64_t)epoch * 3 + 2) * gridDim.x + blockIdx.x] = global_timer_ns();
 }
 
 // ---- attention -----------------------------------------------------------------------------
@@ -456,26 +491,79 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
 // group end to end (lanes own positions for q.K, head dimensions for P.V). With one item per
 // kv head the warp writes the output; otherwise it leaves (O, m, l) and the last CTA of the kv
 // head (atomic ticket) folds the blocks in block order.
+constexpr uint32_t kPsTile = 32;  // attention positions per tile
+// The K/V tiles live behind the staged projection operand (at most 8 KB while QKV runs).
+constexpr uint32_t kPsTileOff = 8 * 1024;
+
+// This CTA's attention item: kv head, block and its positions [t0, t1); false when it has none.
+struct PsItem {
+    uint32_t kvh, blk, Se, t0, t1;
+};
+__device__ __forceinline__ bool attn_item(const PsParams& p, uint32_t npos, PsItem* it) {
+    uint32_t S = min(gridDim.x / p.KV, (npos + kPsTile - 1) / kPsTile);
+    S = max(S, 1u);
+    const uint32_t bl = ((npos + S - 1) / S + kPsTile - 1) / kPsTile * kPsTile;
+    it->Se = npos ? (npos + bl - 1) / bl : 1;
+    if (blockIdx.x >= p.KV * it->Se) return false;
+    it->kvh = blockIdx.x / it->Se;
+    it->blk = blockIdx.x % it->Se;
+    it->t0 = min(npos, it->blk * bl);
+    it->t1 = min(npos, it->t0 + bl);
+    return true;
+}
+
+// Copies rows [tile, tile + n) of the item's K (16-byte chunks XOR-swizzled by row) and V into
+// the tile stage, skipping row `skip` (written later in this launch).
 template <int HD>
-__device__ void ps_attention(const PsParams& p, const PsSmem& s, uint32_t l, uint32_t npos) {
+__device__ __forceinline__ void attn_load_tile(const PsParams& p, const PsSmem& s,
+                                               const PsLayer& ly, uint32_t kvh, uint32_t tile,
+                                               uint32_t n, uint32_t skip) {
+    constexpr uint32_t NCH = HD * 2 / 16, ROWB = HD * 2;
+    unsigned char* ks = s.act + kPsTileOff;
+    unsigned char* vs = ks + kPsTile * ROWB;
+    const bf16* kbase = ly.kcache + (uint64_t)kvh * HD;
+    const bf16* vbase = ly.vcache + (uint64_t)kvh * HD;
+    for (uint32_t c = threadIdx.x; c < n * NCH; c += kPsConsumers * 32) {
+        const uint32_t row = c / NCH, ch = c % NCH;
+        if (tile + row == skip) continue;
+        const uint64_t off = (uint64_t)(tile + row) * p.kvd + ch * 8;
+        cp_async16(ks + row * ROWB + ((ch ^ (row % NCH)) * 16), kbase + off);
+        cp_async16(vs + row * ROWB + ch * 16, vbase + off);
+    }
+}
+
+// Issued right after the QKV operand is staged: the item's first tile without the row at pos
+// (that one is this step's, written by the QKV phase). Returns whether it issued.
+template <int HD>
+__device__ bool attn_prestage(const PsParams& p, const PsSmem& s, uint32_t l, uint32_t npos) {
+    PsItem it;
+    if (npos == 0 || !attn_item(p, npos, &it) || it.t0 >= it.t1) return false;
+    attn_load_tile<HD>(p, s, p.layers[l], it.kvh, it.t0, min(kPsTile, it.t1 - it.t0), npos - 1);
+    return true;
+}
+
+__device__ bool attn_prestage_any(const PsParams& p, const PsSmem& s, uint32_t l, uint32_t npos) {
+    if (p.hd == 128) return attn_prestage<128>(p, s, l, npos);
+    if (p.hd == 64) return attn_prestage<64>(p, s, l, npos);
+    return attn_prestage<32>(p, s, l, npos);
+}
+
+template <int HD>
+__device__ void ps_attention(const PsParams& p, const PsSmem& s, uint32_t l, uint32_t npos,
+                             bool staged) {
     constexpr uint32_t DPL = HD / 32;      // head dims per lane
     constexpr uint32_t NCH = HD * 2 / 16;  // 16-byte chunks per row
-    constexpr uint32_t TP = 32;            // positions per tile
+    constexpr uint32_t TP = kPsTile;
     constexpr uint32_t ROWB = HD * 2;
     const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const uint32_t KV = p.KV, G = p.H / p.KV;
-    uint32_t S = min(gridDim.x / KV, (npos + TP - 1) / TP);
-    S = max(S, 1u);
-    const uint32_t bl = ((npos + S - 1) / S + TP - 1) / TP * TP;
-    const uint32_t Se = npos ? (npos + bl - 1) / bl : 1;
-    const uint32_t item = blockIdx.x;
-    if (item >= KV * Se) return;  // CTA-uniform
-    const uint32_t kvh = item / Se, blk = item % Se;
-    const uint32_t t0 = min(npos, blk * bl), t1 = min(npos, t0 + bl);
+    const uint32_t G = p.H / p.KV;
+    PsItem it;
+    if (!attn_item(p, npos, &it)) return;  // CTA-uniform
+    const uint32_t kvh = it.kvh, blk = it.blk, Se = it.Se, t0 = it.t0, t1 = it.t1;
     const PsLayer& ly = p.layers[l];
-    unsigned char* ks = s.act;                                    // [TP][ROWB], swizzled
-    unsigned char* vs = s.act + TP * ROWB;                        // [TP][ROWB]
-    float* qs = reinterpret_cast<float*>(s.act + 2 * TP * ROWB);  // [G][HD]
+    unsigned char* ks = s.act + kPsTileOff;                       // [TP][ROWB], swizzled
+    unsigned char* vs = ks + TP * ROWB;                           // [TP][ROWB]
+    float* qs = reinterpret_cast<float*>(s.act);                  // [G][HD]
     stage_async(qs, p.q + (uint64_t)kvh * G * HD, G * HD / 4);
     const float scale = 1.0f / sqrtf((float)HD);
     const uint32_t h0 = warp, h1 = warp + kPsConsumers;  // this warp's heads (if < G)
@@ -484,16 +572,20 @@ __device__ void ps_attention(const PsParams& p, const PsSmem& s, uint32_t l, uin
     for (int hs = 0; hs < 2; hs++)
 #pragma unroll
         for (uint32_t d = 0; d < DPL; d++) acc[hs][d] = 0.0f;
-    const uint64_t kvd = p.kvd;
-    const bf16* kbase = ly.kcache + (uint64_t)kvh * HD;
-    const bf16* vbase = ly.vcache + (uint64_t)kvh * HD;
     for (uint32_t tile = t0; tile < t1; tile += TP) {
         const uint32_t n = min(TP, t1 - tile);
-        for (uint32_t c = tid; c < n * NCH; c += kPsConsumers * 32) {
-            const uint32_t row = c / NCH, ch = c % NCH;
-            const uint64_t off = (uint64_t)(tile + row) * kvd + ch * 8;
-            cp_async16(ks + row * ROWB + ((ch ^ (row % NCH)) * 16), kbase + off);
-            cp_async16(vs + row * ROWB + ch * 16, vbase + off);
+        if (tile == t0 && staged) {
+            // the rest of the first tile arrived during the QKV phase; add the row at pos
+            if (npos - 1 >= tile && npos - 1 < tile + n) {
+                const uint32_t row = npos - 1 - tile;
+                for (uint32_t ch = tid; ch < NCH; ch += kPsConsumers * 32) {
+                    const uint64_t off = (uint64_t)(npos - 1) * p.kvd + (uint64_t)kvh * HD + ch * 8;
+                    cp_async16(ks + row * ROWB + ((ch ^ (row % NCH)) * 16), ly.kcache + off);
+                    cp_async16(vs + row * ROWB + ch * 16, ly.vcache + off);
+                }
+            }
+        } else {
+            attn_load_tile<HD>(p, s, ly, kvh, tile, n, 0xffffffffu);
         }
         cp_async_wait_all();
         consumers_sync();
@@ -571,8 +663,9 @@ __device__ void ps_attention(const PsParams& p, const PsSmem& s, uint32_t l, uin
 #pragma unroll
             for (uint32_t d = 0; d < DPL; d++) p.part[slot * HD + lane * DPL + d] = acc[hs][d];
             if (lane == 0) {
-                p.part_ml[slot * 2] = m[hs];
-                p.part_ml[slot * 2 + 1] = lsum[hs];
+                float* ml = p.part_ml + (uint64_t)kvh * p.ml_stride + ((uint64_t)blk * G + h) * 2;
+                ml[0] = m[hs];
+                ml[1] = lsum[hs];
             }
         }
     }
@@ -588,19 +681,23 @@ __device__ void ps_attention(const PsParams& p, const PsSmem& s, uint32_t l, uin
     // fold: per head the blocks' weights exp(m_b - M) (shared), then O over the blocks in
     // block order with eight loads in flight per thread
     const uint64_t base = (uint64_t)kvh * gridDim.x * G;
+    // every block's (m, l) in one round trip: [Se][G][2] floats, 16-byte pieces
+    float* ml = reinterpret_cast<float*>(s.act + 16 * 1024);
+    stage_async(ml, p.part_ml + (uint64_t)kvh * p.ml_stride, (Se * G * 2 + 3) / 4);
+    cp_async_wait_all();
+    consumers_sync();
     float* wts = reinterpret_cast<float*>(s.act);  // [G][Se] weights, then [G] 1 / L
     float* inv = wts + G * Se;
     if (tid < G) {
         const uint32_t h = tid;
         float M = -INFINITY;
-        for (uint32_t b = 0; b < Se; b++)
-            M = fmaxf(M, __ldcg(p.part_ml + (base + (uint64_t)b * G + h) * 2));
+        for (uint32_t b = 0; b < Se; b++) M = fmaxf(M, ml[(b * G + h) * 2]);
         float Lt = 0.0f;
         for (uint32_t b = 0; b < Se; b++) {
-            const float mb = __ldcg(p.part_ml + (base + (uint64_t)b * G + h) * 2);
+            const float mb = ml[(b * G + h) * 2];
             const float w = (M == -INFINITY || mb == -INFINITY) ? 0.0f : expf(mb - M);
             wts[h * Se + b] = w;
-            Lt += __ldcg(p.part_ml + (base + (uint64_t)b * G + h) * 2 + 1) * w;
+            Lt += ml[(b * G + h) * 2 + 1] * w;
         }
         inv[h] = Lt > 0.0f ? 1.0f / Lt : 0.0f;
     }
@@ -636,10 +733,11 @@ __device__ void ps_attention(const PsParams& p, const PsSmem& s, uint32_t l, uin
     if (tid == 0) p.tickets[kvh] = 0;
 }
 
-__device__ void ps_attention_any(const PsParams& p, const PsSmem& s, uint32_t l, uint32_t npos) {
-    if (p.hd == 128) ps_attention<128>(p, s, l, npos);
-    else if (p.hd == 64) ps_attention<64>(p, s, l, npos);
-    else ps_attention<32>(p, s, l, npos);
+__device__ void ps_attention_any(const PsParams& p, const PsSmem& s, uint32_t l, uint32_t npos,
+                                 bool staged) {
+    if (p.hd == 128) ps_attention<128>(p, s, l, npos, staged);
+    else if (p.hd == 64) ps_attention<64>(p, s, l, npos, staged);
+    else ps_attention<32>(p, s, l, npos, staged);
 }
 
 // ---- the kernel ----------------------------------------------------------------------------
@@ -701,21 +799,29 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
     for (uint32_t l = 0; l < p.L && ok; l++) {
         const PsLayer& ly = p.layers[l];
         stage_norm(p, s, ly.rms_att);
+        trace_staged(p, epoch);
+        // this CTA's attention item's first tile (rows before pos) lands during the QKV phase
+        const bool staged = attn_prestage_any(p, s, l, npos);
         ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhQkv, l, g, pos, pos_ok, &best));
         if (!ok) break;
-        ps_attention_any(p, s, l, npos);
+        trace_staged(p, epoch);
+        ps_attention_any(p, s, l, npos, staged);
         ok = grid_barrier(p, s, epoch);
         if (!ok) break;
         stage_copy(s, p.o, p.qd);
+        trace_staged(p, epoch);
         ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best));
         if (!ok) break;
         stage_norm(p, s, ly.rms_ffn);
+        trace_staged(p, epoch);
         ok = grid_barrier(p, s, epoch,
                           consume_phase(p, s, kPhGateUp, l, g, pos, pos_ok, &best));
         if (!ok) break;
         stage_copy(s, p.h, p.F);
+        trace_staged(p, epoch);
         ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best));
     }
+    cp_async_wait_all();  // an aborted layer may leave a prestaged tile in flight
     if (ok) {
         stage_norm(p, s, p.rms_final);
         if (!consume_phase(p, s, kPhCls, 0, g, pos, pos_ok, &best)) s.misc[2] = 1;
@@ -869,11 +975,12 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     const size_t b_layers = al(sizeof(PsLayer) * m.layers);
     const size_t b_q = al(4ull * p.qd), b_o = al(2ull * p.qd), b_h = al(2ull * p.F);
     const size_t b_part = al(4ull * p.KV * f->grid * G * p.hd);
-    const size_t b_ml = al(4ull * p.KV * f->grid * G * 2);
+    p.ml_stride = (f->grid * G * 2 + 3) / 4 * 4;
+    const size_t b_ml = al(4ull * p.KV * p.ml_stride);
     const size_t b_tk = al(4ull * (p.KV + 1));
     const size_t b_cand = al(8ull * f->grid);
     const size_t b_bar = 256;
-    const size_t b_trace = trace ? al(8ull * f->barriers * f->grid) : 0;
+    const size_t b_trace = trace ? al(8ull * 3 * f->barriers * f->grid) : 0;
     const size_t total =
         b_layers + b_q + b_o + b_h + b_part + b_ml + b_tk + b_cand + b_bar + b_trace;
     try {
@@ -962,12 +1069,13 @@ void record_fused_step(ab_scheme* s, FusedStep* f, bool feedback) {
     });
 }
 
-// Per-barrier arrival times of the last launch (AMMON_B200_STEP_TRACE set): [barriers][grid]
-// nanoseconds of %globaltimer; false when tracing is off.
+// Per-barrier times of the last launch (AMMON_B200_STEP_TRACE set): [barriers][3][grid]
+// nanoseconds of %globaltimer -- arrival, release, and when the CTA had staged the operand of
+// the phase that ends at that barrier; false when tracing is off.
 bool fused_step_trace(FusedStep* f, std::vector<uint64_t>* out, uint32_t* barriers,
                       uint32_t* grid) {
     if (!f || !f->p.trace) return false;
-    out->resize((size_t)f->barriers * f->grid);
+    out->resize((size_t)3 * f->barriers * f->grid);
     cuda_check(cudaMemcpy(out->data(), f->p.trace, out->size() * 8, cudaMemcpyDeviceToHost),
                "fused step trace");
     *barriers = f->barriers;
