@@ -80,6 +80,11 @@ struct ab_comm {
     unsigned char* peer_base[ab::kTpMaxWorld] = {};
     uint64_t* epoch = nullptr;   // device: bumped once per recorded step
     uint32_t next_site = 0;      // all-reduce sites numbered in recording order
+    // the persistent decode step's exchange block (comm_fused_block), one per rank, opened
+    // by every peer through CUDA IPC; released with the communicator
+    size_t fused_bytes = 0;
+    unsigned char* fused_local = nullptr;
+    unsigned char* fused_peer[ab::kTpMaxWorld] = {};
 };
 
 namespace ab {
@@ -175,6 +180,61 @@ void comm_peers_release(ab_comm* c) {
 }
 
 bool comm_has_peers(const ab_comm* c) { return c && c->peers; }
+
+static void fused_block_release(ab_comm* c) {
+    for (int r = 0; r < (int)kTpMaxWorld; r++) {
+        if (c->fused_peer[r] && r != c->rank) cudaIpcCloseMemHandle(c->fused_peer[r]);
+        c->fused_peer[r] = nullptr;
+    }
+    if (c->fused_local) cudaFree(c->fused_local);
+    c->fused_local = nullptr;
+    c->fused_bytes = 0;
+}
+
+bool comm_fused_block(ab_comm* c, size_t bytes, unsigned char** local,
+                      unsigned char* peers[kTpMaxWorld]) {
+    if (c->fused_local) {
+        if (bytes > c->fused_bytes) fail(AB_ERR_ARGUMENT, "fused exchange block set up smaller");
+    } else {
+        if (c->world < 2 || c->world > (int)kTpMaxWorld) return false;
+        c->rt->activate();
+        cudaIpcMemHandle_t mine;
+        std::memset(&mine, 0, sizeof(mine));
+        int ok = 0;
+        if (cudaMalloc(&c->fused_local, bytes) == cudaSuccess &&
+            cudaMemset(c->fused_local, 0, bytes) == cudaSuccess &&
+            cudaIpcGetMemHandle(&mine, c->fused_local) == cudaSuccess)
+            ok = 1;
+        cudaGetLastError();
+        std::vector<cudaIpcMemHandle_t> all(c->world);
+        allgather_host(c, &mine, all.data(), sizeof(mine));
+        for (int r = 0; r < c->world && ok; r++) {
+            if (r == c->rank) {
+                c->fused_peer[r] = c->fused_local;
+                continue;
+            }
+            void* ptr = nullptr;
+            if (cudaIpcOpenMemHandle(&ptr, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+            } else {
+                c->fused_peer[r] = (unsigned char*)ptr;
+            }
+        }
+        std::vector<int> oks(c->world);
+        allgather_host(c, &ok, oks.data(), sizeof(int));
+        bool every = true;
+        for (int v : oks) every = every && v == 1;
+        if (!every) {
+            fused_block_release(c);
+            return false;
+        }
+        c->fused_bytes = bytes;
+    }
+    *local = c->fused_local;
+    for (int r = 0; r < (int)kTpMaxWorld; r++) peers[r] = c->fused_peer[r];
+    return true;
+}
 void comm_begin_recording(ab_comm* c) {
     if (c) c->next_site = 0;
 }
@@ -383,6 +443,7 @@ int ab_comm_destroy(ab_comm* c) {
             }
         }
         comm_peers_release(c);
+        fused_block_release(c);
         if (c->comm) nccl().comm_destroy(c->comm);
         delete c;
     });

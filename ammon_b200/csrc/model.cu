@@ -404,6 +404,9 @@ void record_step(ab_llama* m, ab_scheme* s, bool feedback, bool gather_logits) {
     s->dirty = true;
     if (m->fused) {
         record_fused_step(s, m->fused, feedback);
+        if (m->world > 1 && gather_logits)
+            record_allgather_bytes(s, "logits_allgather", m->comm, m->logits.data,
+                                   m->logits_all.data, (size_t)m->c.batch * m->vocab_l * 4);
         return;
     }
     const auto& c = m->c;
@@ -608,21 +611,31 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
                    "pinned steps");
         check(ab_scheme_create(rt, &m->scheme));
         check(ab_scheme_create(rt, &m->loop_scheme));
-        if (world == 1 && fused_step_enabled()) {
+        if (fused_step_enabled()) {
+            // this rank's shard; every rank reaches the same decision (same config and
+            // environment), so the collective exchange-block set-up is entered by all or none
             FusedStepModel fm;
+            fm.world = (uint32_t)world;
+            fm.rank = (uint32_t)rank;
             fm.batch = c.batch;
             fm.layers = c.layers;
             fm.dim = c.dim;
-            fm.heads = c.heads;
-            fm.kv_heads = c.kv_heads;
+            fm.heads = m->heads_l;
+            fm.kv_heads = m->kv_l;
             fm.head_dim = c.head_dim;
-            fm.hidden = c.hidden;
-            fm.vocab = c.vocab;
+            fm.hidden = m->hidden_l;
+            fm.vocab = m->vocab_l;
             fm.seq = c.seq;
             fm.dtype = c.dtype;
             fm.rope_theta = c.rope_theta;
             fm.norm_eps = c.norm_eps;
-            if (fused_step_unsupported(fm, rt->sm_count).empty()) {
+            bool go = fused_step_unsupported(fm, rt->sm_count).empty();
+            if (go && world > 1) {
+                unsigned char* local = nullptr;
+                go = comm_fused_block(comm, fused_step_xblock_bytes(world, c.dim), &local,
+                                      fm.xblock);
+            }
+            if (go) {
                 fm.embed = m->embed.data;
                 fm.wcls = m->wcls.data;
                 fm.rms_final = m->rms_final.data;

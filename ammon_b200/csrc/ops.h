@@ -180,6 +180,12 @@ int comm_world(const ab_comm* c);
 bool comm_peers_setup(ab_comm* c, size_t max_elems);
 void comm_peers_release(ab_comm* c);
 bool comm_has_peers(const ab_comm* c);
+// The persistent decode step's exchange block of `bytes` on every rank (collective): this
+// rank's (zeroed) and every rank's as this rank addresses it through CUDA IPC. Kept until
+// the communicator is destroyed (after a barrier of all ranks). False on every rank when a
+// peer cannot be opened.
+bool comm_fused_block(ab_comm* c, size_t bytes, unsigned char** local,
+                      unsigned char* peers[kTpMaxWorld]);
 void comm_begin_recording(ab_comm* c);
 void record_tp_epoch(ab_scheme* s, ab_comm* c);
 TpPush comm_push_target(ab_comm* c);
@@ -237,6 +243,10 @@ void record_attention(ab_scheme* s, const char* label, AttnParams p);
 // What the single-launch batch-1 decode step reads and writes (device pointers; per-layer
 // K/V caches are [seq, kv_heads, head] views).
 struct FusedStepModel {
+    // tensor parallelism: this rank's shard sizes below (heads, kv_heads, hidden, vocab),
+    // and every rank's exchange block (comm_fused_block); world 1 without
+    uint32_t world = 1, rank = 0;
+    unsigned char* xblock[kTpMaxWorld] = {};
     uint32_t batch, layers, dim, heads, kv_heads, head_dim, hidden, vocab, seq;
     int32_t dtype;
     float rope_theta, norm_eps;
@@ -263,6 +273,8 @@ void fused_step_destroy(FusedStep* f);
 void record_fused_step(ab_scheme* s, FusedStep* f, bool feedback);
 bool fused_step_trace(FusedStep* f, std::vector<uint64_t>* out, uint32_t* barriers,
                       uint32_t* grid);
+// Bytes of the exchange block a tensor-parallel persistent step over `world` ranks needs.
+size_t fused_step_xblock_bytes(uint32_t world, uint32_t dim);
 
 // Rejects batched shapes the single-row reference kernels cannot take.
 void record_embed(ab_scheme* s, ab_tensor table, ab_tensor step, ab_tensor x);

@@ -108,7 +108,29 @@ struct PsParams {
     uint64_t wait_ns;
     uint32_t stall_barrier;  // test hook: CTA 0 never arrives at this barrier (0 = none)
     uint64_t* trace;         // optional [barriers][grid] %globaltimer at each arrival
+    // tensor parallelism (world > 1): every rank's exchange block as this rank addresses it
+    // (layout kXb*), the second residual buffer (all-reduce sites alternate x and x2), this
+    // rank's launch count and the first vocabulary id of its classifier rows
+    uint32_t world, rank, vocab_off;
+    unsigned char* xb[kTpMaxWorld];
+    float* x2;
+    unsigned long long* launch;
 };
+
+// Exchange block of one rank: [0] all-reduce arrivals (u64), [8] argmax arrivals (u64),
+// [16] this rank's launch count (u64), [64] argmax candidates [world] x (f32 value, u32 id),
+// [256] partial projections [2 parities][world][d] f32. Counters only grow, kept with the
+// block for the communicator's life: a site's target is the launch count times the sites per
+// launch, plus the site, times the arrivals per site.
+constexpr uint32_t kXbAr = 0, kXbAm = 8, kXbLaunch = 16, kXbCand = 64, kXbPart = 256;
+
+__device__ __forceinline__ unsigned long long* xb_ctr(const PsParams& p, uint32_t r,
+                                                      uint32_t off) {
+    return reinterpret_cast<unsigned long long*>(p.xb[r] + off);
+}
+__device__ __forceinline__ float* xb_part(const PsParams& p, uint32_t r, uint32_t par) {
+    return reinterpret_cast<float*>(p.xb[r] + kXbPart) + (size_t)par * p.world * p.d;
+}
 
 // ---- shared-memory layout ------------------------------------------------------------------
 struct PsSmem {
@@ -265,11 +287,11 @@ __device__ bool produce_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
 // ---- consumers: staging --------------------------------------------------------------------
 // xs = bf16(gain * (ss * x)), ss = 1 / sqrt(mean(x^2) + eps): the RMSNorm of
 // src/kernels.rs:75-101 (o = w * (ss * x)) with bf16 rounding of the operand of the next Linear.
-__device__ void stage_norm(const PsParams& p, const PsSmem& s, const bf16* gain) {
+// The norm of the x already staged (f32) in the activation region.
+__device__ void norm_from_xf(const PsParams& p, const PsSmem& s, const bf16* gain) {
     const uint32_t tid = threadIdx.x, n = kPsConsumers * 32;
     float* xf = reinterpret_cast<float*>(s.act + kPsXOff);
     bf16* gs = reinterpret_cast<bf16*>(s.act + kPsGainOff);
-    stage_async(xf, p.x, p.d / 4);
     stage_async(gs, gain, p.d / 8);
     cp_async_wait_all();
     consumers_sync();
@@ -285,6 +307,45 @@ __device__ void stage_norm(const PsParams& p, const PsSmem& s, const bf16* gain)
     bf16* xs = reinterpret_cast<bf16*>(s.act);
     for (uint32_t i = tid; i < p.d; i += n)
         xs[i] = __float2bfloat16_rn(__bfloat162float(gs[i]) * (scale * xf[i]));
+    consumers_sync();
+}
+
+__device__ void stage_norm(const PsParams& p, const PsSmem& s, const float* x, const bf16* gain) {
+    stage_async(s.act + kPsXOff, x, p.d / 4);
+    norm_from_xf(p, s, gain);
+}
+
+// Tensor parallelism: x_new = x_old + the ranks' partial projections of site parity `par`,
+// summed in rank order (every CTA of every rank adds the same values in the same order, so the
+// replicated residual stays bit-identical); the whole x_new is left staged (f32) for the next
+// norm, and this CTA writes its slice of it to x_new for the site after.
+__device__ void tp_reduce_stage(const PsParams& p, const PsSmem& s, uint32_t par,
+                                const float* x_old, float* x_new) {
+    float4* xf = reinterpret_cast<float4*>(s.act + kPsXOff);
+    const float* part = xb_part(p, p.rank, par);
+    const uint32_t nv = p.d / 4;
+    const uint32_t i0 = (uint32_t)((uint64_t)p.d * blockIdx.x / gridDim.x);
+    const uint32_t i1 = (uint32_t)((uint64_t)p.d * (blockIdx.x + 1) / gridDim.x);
+    for (uint32_t v = threadIdx.x; v < nv; v += kPsConsumers * 32) {
+        float4 a = __ldcg(reinterpret_cast<const float4*>(x_old) + v);
+        float4 pr[kTpMaxWorld];
+#pragma unroll
+        for (uint32_t r = 0; r < kTpMaxWorld; r++)
+            if (r < p.world) pr[r] = __ldcg(reinterpret_cast<const float4*>(part + (size_t)r * p.d) + v);
+#pragma unroll
+        for (uint32_t r = 0; r < kTpMaxWorld; r++) {
+            if (r >= p.world) break;
+            a.x += pr[r].x;
+            a.y += pr[r].y;
+            a.z += pr[r].z;
+            a.w += pr[r].w;
+        }
+        xf[v] = a;
+        const float c[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (uint32_t e = 0; e < 4; e++)
+            if (4 * v + e >= i0 && 4 * v + e < i1) x_new[4 * v + e] = c[e];
+    }
     consumers_sync();
 }
 
@@ -358,6 +419,8 @@ __device__ __forceinline__ PsBest first_max2(PsBest a, PsBest b) {
 // Consumes this warp's chunks of one phase (chunk g goes to warp g % kPsSlots).
 __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind, uint32_t l,
                               uint32_t& g, uint32_t pos, bool pos_ok, PsBest* best) {
+    const bool tp = p.world > 1;
+    const uint32_t par = kind == kPhDown ? 1u : 0u;  // all-reduce site parity
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const PsGeom gm = ps_geom(p, kind);
     const PsLayer* ly = kind == kPhCls ? nullptr : p.layers + l;
@@ -370,8 +433,9 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
         const uint32_t rows = n * gm.rpu;
         // the residual rows this chunk adds to, loaded before the wait hide their latency
         float2 xr = make_float2(0.0f, 0.0f);
-        if (kind == kPhWo && lane < n) xr = __ldcg(reinterpret_cast<const float2*>(p.x) + u + lane);
-        if (kind == kPhDown && lane == 0) xr.x = __ldcg(p.x + u);
+        if (!tp && kind == kPhWo && lane < n)
+            xr = __ldcg(reinterpret_cast<const float2*>(p.x) + u + lane);
+        if (!tp && kind == kPhDown && lane == 0) xr.x = __ldcg(p.x + u);
         // every lane waits; the warp agrees on one outcome before the full-mask shuffles below
         const bool landed = ps_wait(p, smem_u32(&s.full[slot]), (g / kPsSlots) & 1);
         if (!__all_sync(0xffffffffu, landed)) return false;
@@ -389,13 +453,20 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
                 if (lane == r) p.logits[row] = acc[r];
                 if (acc[r] > best->v || (best->i == 0xffffffffu && acc[r] == best->v)) {
                     best->v = acc[r];
-                    best->i = row;
+                    best->i = row + p.vocab_off;
                 }
             }
             continue;
         }
         if (kind == kPhDown) {
-            if (lane == 0) p.x[u] = xr.x + acc[0];
+            if (lane == 0) {
+                if (tp) {  // this rank's partial row, into every rank's exchange block
+                    for (uint32_t r = 0; r < p.world; r++)
+                        xb_part(p, r, par)[(size_t)p.rank * p.d + u] = acc[0];
+                } else {
+                    p.x[u] = xr.x + acc[0];
+                }
+            }
             continue;
         }
         if (lane >= n) continue;
@@ -410,7 +481,13 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
         if (kind == kPhGateUp) {
             p.h[unit] = __float2bfloat16_rn(silu_mul(y0, y1));
         } else if (kind == kPhWo) {
-            reinterpret_cast<float2*>(p.x)[unit] = make_float2(xr.x + y0, xr.y + y1);
+            if (tp) {
+                for (uint32_t r = 0; r < p.world; r++)
+                    reinterpret_cast<float2*>(xb_part(p, r, par) + (size_t)p.rank * p.d)[unit] =
+                        make_float2(y0, y1);
+            } else {
+                reinterpret_cast<float2*>(p.x)[unit] = make_float2(xr.x + y0, xr.y + y1);
+            }
         } else {  // kPhQkv: RoPE (src/kernels.rs:174-210) and the K/V append (:212-226)
             const uint32_t r = 2 * unit;
             if (r < p.qd) {
@@ -455,6 +532,59 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
             const uint64_t t0 = global_timer_ns();
             uint32_t n = 0;
             while (ld_acquire(p.bar) < target) {
+                if ((++n & 15) == 0) {
+                    if (aborted(p)) {
+                        ok = 0;
+                        break;
+                    }
+                    if (global_timer_ns() - t0 > p.wait_ns) {
+                        raise_abort(p);
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+        }
+        s.misc[0] = ok;
+        if (ok && p.trace)
+            p.trace[((uint64_t)(epoch - 1) * 3 + 1) * gridDim.x + blockIdx.x] = global_timer_ns();
+    }
+    consumers_sync();
+    return s.misc[0] != 0;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Tensor parallelism: the barrier of an all-reduce site over every CTA of every rank. Each
+// CTA, once its partial rows are in every rank's exchange block, adds one arrival to every
+// rank's counter (release, system scope); thread 0 then waits until this rank's counter
+// reaches `target` (acquire). Bounded like grid_barrier; a rank that gives up leaves the
+// others to run out of their own waits.
+__device__ bool tp_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch, bool ok_in,
+                           unsigned long long target) {
+    if (!ok_in) s.misc[2] = 1;
+    consumers_sync();
+    epoch++;
+    if (threadIdx.x == 0) {
+        uint32_t ok = s.misc[2] == 0;
+        if (p.stall_barrier == epoch && blockIdx.x == 0) ok = 0;  // test hook
+        if (ok && p.trace)
+            p.trace[((uint64_t)(epoch - 1) * 3 + 0) * gridDim.x + blockIdx.x] = global_timer_ns();
+        if (ok) {
+            __threadfence_system();
+            for (uint32_t r = 0; r < p.world; r++)
+                asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(xb_ctr(p, r, kXbAr))
+                             : "memory");
+        }
+        const unsigned long long* mine = xb_ctr(p, p.rank, kXbAr);
+        if (ok && ld_acquire_sys64(mine) < target) {
+            const uint64_t t0 = global_timer_ns();
+            uint32_t n = 0;
+            while (ld_acquire_sys64(mine) < target) {
                 if ((++n & 15) == 0) {
                     if (aborted(p)) {
                         ok = 0;
@@ -796,9 +926,16 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
     }
     // ok stays uniform over the CTA's consumer warps: every phase ends in a grid barrier
     ok = grid_barrier(p, s, epoch);
+    const bool tp = p.world > 1;
+    // tensor parallelism: all-reduce site k of this launch (wo of layer l is 2l, w2 is 2l + 1)
+    const unsigned long long launch = tp ? *p.launch : 0ull;
+    auto ar_target = [&](uint32_t k) {
+        return (launch * 2ull * p.L + k + 1) * (unsigned long long)p.world * gridDim.x;
+    };
     for (uint32_t l = 0; l < p.L && ok; l++) {
         const PsLayer& ly = p.layers[l];
-        stage_norm(p, s, ly.rms_att);
+        if (tp && l > 0) norm_from_xf(p, s, ly.rms_att);  // x staged by the last w2 site
+        else stage_norm(p, s, p.x, ly.rms_att);
         trace_staged(p, epoch);
         // this CTA's attention item's first tile (rows before pos) lands during the QKV phase
         const bool staged = attn_prestage_any(p, s, l, npos);
@@ -810,20 +947,36 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
         if (!ok) break;
         stage_copy(s, p.o, p.qd);
         trace_staged(p, epoch);
-        ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best));
-        if (!ok) break;
-        stage_norm(p, s, ly.rms_ffn);
+        if (tp) {
+            ok = tp_barrier(p, s, epoch, consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best),
+                            ar_target(2 * l));
+            if (!ok) break;
+            tp_reduce_stage(p, s, 0, p.x, p.x2);
+            norm_from_xf(p, s, ly.rms_ffn);
+        } else {
+            ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best));
+            if (!ok) break;
+            stage_norm(p, s, p.x, ly.rms_ffn);
+        }
         trace_staged(p, epoch);
         ok = grid_barrier(p, s, epoch,
                           consume_phase(p, s, kPhGateUp, l, g, pos, pos_ok, &best));
         if (!ok) break;
         stage_copy(s, p.h, p.F);
         trace_staged(p, epoch);
-        ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best));
+        if (tp) {
+            ok = tp_barrier(p, s, epoch, consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best),
+                            ar_target(2 * l + 1));
+            if (ok) tp_reduce_stage(p, s, 1, p.x2, p.x);
+        } else {
+            ok = grid_barrier(p, s, epoch,
+                              consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best));
+        }
     }
     cp_async_wait_all();  // an aborted layer may leave a prestaged tile in flight
     if (ok) {
-        stage_norm(p, s, p.rms_final);
+        if (tp && p.L > 0) norm_from_xf(p, s, p.rms_final);
+        else stage_norm(p, s, p.x, p.rms_final);
         if (!consume_phase(p, s, kPhCls, 0, g, pos, pos_ok, &best)) s.misc[2] = 1;
     }
     // the CTA's first maximum, then the last CTA keeps the first maximum of all CTAs
@@ -843,6 +996,37 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
             PsBest a = {-INFINITY, 0xffffffffu};
             for (uint32_t c = 0; c < gridDim.x; c++)
                 a = first_max2(a, PsBest{__ldcg(p.cand_v + c), __ldcg(p.cand_i + c)});
+            bool merged = true;
+            if (tp) {
+                // every rank's best (value, id) into every rank's block, then the first maximum
+                // over the ranks in rank order: all ranks pick the same id
+                for (uint32_t r = 0; r < p.world; r++) {
+                    float* c = reinterpret_cast<float*>(p.xb[r] + kXbCand) + 2 * p.rank;
+                    c[0] = a.v;
+                    reinterpret_cast<uint32_t*>(c)[1] = a.i;
+                }
+                __threadfence_system();
+                for (uint32_t r = 0; r < p.world; r++)
+                    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(
+                                     xb_ctr(p, r, kXbAm))
+                                 : "memory");
+                const unsigned long long want = (launch + 1) * p.world;
+                const unsigned long long* mine = xb_ctr(p, p.rank, kXbAm);
+                const uint64_t t0 = global_timer_ns();
+                while (ld_acquire_sys64(mine) < want) {
+                    if (global_timer_ns() - t0 > p.wait_ns) {
+                        raise_abort(p);
+                        merged = false;
+                        break;
+                    }
+                }
+                a = PsBest{-INFINITY, 0xffffffffu};
+                const float* cand = reinterpret_cast<const float*>(p.xb[p.rank] + kXbCand);
+                for (uint32_t r = 0; merged && r < p.world; r++)
+                    a = first_max2(a, PsBest{__ldcv(cand + 2 * r),
+                                             __ldcv(reinterpret_cast<const unsigned int*>(cand) +
+                                                    2 * r + 1)});
+            }
             const int32_t id = a.i == 0xffffffffu ? 0 : (int32_t)a.i;
             p.argmax[0] = id;
             p.tickets[p.KV] = 0;
@@ -865,6 +1049,7 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
         if (atomicAdd(p.bar + 1, 1u) == gridDim.x - 1) {
             if (ld_relaxed(p.bar + 2))
                 for (uint32_t k = 0; k <= p.KV; k++) p.tickets[k] = 0;
+            if (tp) *p.launch += 1;
             p.bar[0] = 0;
             p.bar[1] = 0;
             p.bar[2] = 0;
@@ -912,8 +1097,13 @@ static uint32_t env_stall_barrier() {
     return 0;
 }
 
+size_t fused_step_xblock_bytes(uint32_t world, uint32_t dim) {
+    return kXbPart + 2ull * world * dim * sizeof(float);
+}
+
 // Why the fused step cannot run this model ("" when it can).
 std::string fused_step_unsupported(const FusedStepModel& m, int sms) {
+    if (m.world > kTpMaxWorld) return "more than 8 ranks";
     if (m.batch != 1) return "batch is not 1";
     if (m.dtype != AB_BF16) return "weights are not bf16";
     const uint32_t qd = m.heads * m.head_dim, kvd = m.kv_heads * m.head_dim;
@@ -924,6 +1114,7 @@ std::string fused_step_unsupported(const FusedStepModel& m, int sms) {
     if (m.dim % 8 || qd % 8 || kvd % 8 || m.hidden % 8) return "dims not multiples of 8";
     if (m.dim % 2 || m.vocab % 2) return "odd dim or vocab";
     if (m.dim > 4096) return "dim above 4096 (the norm stages x and its gain in 24 KB)";
+    if (m.world > 1 && m.dim % 4) return "dim not a multiple of 4";
     const uint64_t pair = 2ull * 2 * std::max(m.dim, qd);
     if (pair > kPsSlotBytes) return "a row pair exceeds the 32 KB ring slot";
     if ((uint64_t)m.hidden * 2 > kPsSlotBytes) return "a w2 row exceeds the 32 KB ring slot";
@@ -965,6 +1156,11 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     p.argmax = m.argmax;
     p.history = m.history;
     p.flags = rt->flags;
+    p.world = m.world;
+    p.rank = m.rank;
+    p.vocab_off = m.rank * m.vocab;
+    for (uint32_t r = 0; r < kTpMaxWorld; r++) p.xb[r] = r < m.world ? m.xblock[r] : nullptr;
+    p.launch = m.world > 1 ? (unsigned long long*)(m.xblock[m.rank] + kXbLaunch) : nullptr;
     p.wait_ns = env_wait_ns();
     p.stall_barrier = env_stall_barrier();
     // one scratch allocation: layer table, q, o, h, attention partials, tickets, candidates,
@@ -974,6 +1170,7 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     auto al = [](size_t n) { return (n + 255) / 256 * 256; };
     const size_t b_layers = al(sizeof(PsLayer) * m.layers);
     const size_t b_q = al(4ull * p.qd), b_o = al(2ull * p.qd), b_h = al(2ull * p.F);
+    const size_t b_x2 = m.world > 1 ? al(4ull * p.d) : 0;
     const size_t b_part = al(4ull * p.KV * f->grid * G * p.hd);
     p.ml_stride = (f->grid * G * 2 + 3) / 4 * 4;
     const size_t b_ml = al(4ull * p.KV * p.ml_stride);
@@ -982,7 +1179,7 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     const size_t b_bar = 256;
     const size_t b_trace = trace ? al(8ull * 3 * f->barriers * f->grid) : 0;
     const size_t total =
-        b_layers + b_q + b_o + b_h + b_part + b_ml + b_tk + b_cand + b_bar + b_trace;
+        b_layers + b_q + b_o + b_h + b_x2 + b_part + b_ml + b_tk + b_cand + b_bar + b_trace;
     try {
         cuda_check(cudaMalloc(&f->scratch, total), "fused step scratch");
         cuda_check(cudaMemset(f->scratch, 0, total), "fused step scratch");
@@ -996,6 +1193,8 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
         c += b_o;
         p.h = (bf16*)c;
         c += b_h;
+        p.x2 = b_x2 ? (float*)c : nullptr;
+        c += b_x2;
         p.part = (float*)c;
         c += b_part;
         p.part_ml = (float*)c;
@@ -1049,6 +1248,7 @@ void fused_step_destroy(FusedStep* f) {
 }
 
 void record_fused_step(ab_scheme* s, FusedStep* f, bool feedback) {
+    // (the tensor-parallel step() scheme adds the logits all-gather after this node)
     PsParams p = f->p;
     p.feedback = feedback ? 1u : 0u;
     const uint32_t grid = f->grid;

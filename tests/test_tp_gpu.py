@@ -21,7 +21,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=False):
+def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=False,
+            fused=None):
     import datetime
 
     import torch
@@ -32,6 +33,8 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
 
     cfg_d = cfg or CFG
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    if fused is not None:
+        os.environ["AMMON_B200_FUSED_STEP"] = "1" if fused else "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120),
@@ -53,6 +56,8 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
             model.init_synthetic(17, 0.02)
         ref = orc.Model(**cfg_d, theta=500000.0, bf16=bf16, seed=17)
         worst, same = 0.0, True
+        if fused is not None:
+            same &= ("decode_step" in model.scheme().node_labels()) == fused
         if prefill:
             # the prompt in one pass of 6 rows (NCCL all-reduce), then in passes of 2 (peer
             # all-reduce) over the same positions; then decode continues from the cache
@@ -92,7 +97,7 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
         dist.destroy_process_group()
 
 
-def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False):
+def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False, fused=None):
     import torch
     import torch.multiprocessing as mp
 
@@ -102,7 +107,7 @@ def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg, ckpt,
-                                                    prefill))
+                                                    prefill, fused))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -159,3 +164,25 @@ def test_tensor_parallel_prefill_matches_oracle():
     for rank, worst, same, _ in _run(False, 1, prefill=True):
         assert worst < 1e-5, (rank, worst)
         assert same
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_persistent_step_matches_oracle(world):
+    """bf16 at batch 1 runs the persistent single-launch step on every rank: partial wo / w2
+    rows go straight into every rank's exchange block over NVLink, a system-scope arrival
+    counter per rank closes each all-reduce site, the ranks' argmax candidates merge inside
+    the kernel. Logits match the single-device oracle at the bf16 bar, every rank picks the
+    same ids, and the per-kernel TP step graph (AMMON_B200_FUSED_STEP=0) agrees."""
+    import torch
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    cfg = CFG if world == 2 else CFG8
+    fused = _run(True, 1, world, cfg, fused=True)
+    for rank, worst, same, agree in fused:
+        assert worst < 2e-2, (world, rank, worst)
+        assert same and agree
+    graph = _run(True, 1, world, cfg, fused=False)
+    for rank, worst, same, agree in graph:
+        assert worst < 2e-2, (world, rank, worst)
+        assert same and agree
