@@ -579,6 +579,8 @@ __device__ bool tp_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch, 
             for (uint32_t r = 0; r < p.world; r++)
                 asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(xb_ctr(p, r, kXbAr))
                              : "memory");
+            // the local grid-barrier counter counts this barrier too (its targets follow epoch)
+            asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         }
         const unsigned long long* mine = xb_ctr(p, p.rank, kXbAr);
         if (ok && ld_acquire_sys64(mine) < target) {
