@@ -112,6 +112,7 @@ struct PsParams {
     // (layout kXb*), the second residual buffer (all-reduce sites alternate x and x2), this
     // rank's launch count and the first vocabulary id of its classifier rows
     uint32_t world, rank, vocab_off;
+    uint32_t vocab_all;  // rows of the (replicated) embedding table: V times the ranks
     unsigned char* xb[kTpMaxWorld];
     float* x2;
     unsigned long long* launch;
@@ -909,7 +910,7 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
     const uint32_t pos = st.position;
     const bool pos_ok = pos < p.seq;
     uint32_t tok = st.token;
-    if (tok >= p.V) {
+    if (tok >= p.vocab_all) {
         if (tid == 0 && blockIdx.x == 0) atomicOr(p.flags, kFlagTokenRange);
         tok = 0;
     }
@@ -1161,6 +1162,7 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     p.world = m.world;
     p.rank = m.rank;
     p.vocab_off = m.rank * m.vocab;
+    p.vocab_all = m.vocab * m.world;
     for (uint32_t r = 0; r < kTpMaxWorld; r++) p.xb[r] = r < m.world ? m.xblock[r] : nullptr;
     p.launch = m.world > 1 ? (unsigned long long*)(m.xblock[m.rank] + kXbLaunch) : nullptr;
     p.wait_ns = env_wait_ns();
