@@ -87,6 +87,17 @@ class Runtime:
         _check(_abi.lib().ab_runtime_sm_count(self._h, C.byref(n)))
         return n.value
 
+    @property
+    def wait_limit_ms(self) -> int:
+        """Limit of every bounded wait in this runtime's kernels (milliseconds)."""
+        n = C.c_uint32()
+        _check(_abi.lib().ab_runtime_wait_limit(self._h, C.byref(n)))
+        return n.value
+
+    @wait_limit_ms.setter
+    def wait_limit_ms(self, ms: int):
+        _check(_abi.lib().ab_runtime_set_wait_limit(self._h, int(ms)))
+
     def scheme(self) -> "Scheme":
         return Scheme(self)
 
@@ -518,12 +529,17 @@ class Comm:
     with ``Comm.unique_id()`` and shares it with the other ranks (e.g. a torch.distributed
     broadcast); every rank then builds its Comm with the same id."""
 
-    def __init__(self, rt: Runtime, uid: bytes, rank: int, world: int):
+    def __init__(self, rt: Runtime, uid: bytes, rank: int, world: int,
+                 timeout_ms: Optional[int] = None):
         if len(uid) != _abi.COMM_ID_BYTES:
             raise ValueError("communicator id must be 128 bytes")
         buf = (C.c_uint8 * _abi.COMM_ID_BYTES).from_buffer_copy(uid)
         h = C.c_void_p()
-        _check(_abi.lib().ab_comm_create(rt.handle, buf, rank, world, C.byref(h)))
+        if timeout_ms is None:
+            _check(_abi.lib().ab_comm_create(rt.handle, buf, rank, world, C.byref(h)))
+        else:
+            _check(_abi.lib().ab_comm_create_timeout(rt.handle, buf, rank, world,
+                                                     int(timeout_ms), C.byref(h)))
         self._h = h
         self.rt = rt
         self.rank, self.world = rank, world
@@ -533,6 +549,15 @@ class Comm:
         buf = (C.c_uint8 * _abi.COMM_ID_BYTES)()
         _check(_abi.lib().ab_comm_unique_id(buf))
         return bytes(buf)
+
+    @staticmethod
+    def loopback_reduce(rt: Runtime, world: int, ready: int, n: int) -> np.ndarray:
+        """ab_comm_loopback_reduce: the all-reduce kernel over `world` ranks held in this
+        GPU's memory, ranks outside the `ready` mask never arriving."""
+        out = np.zeros(n, np.float32)
+        _check(_abi.lib().ab_comm_loopback_reduce(
+            rt.handle, world, ready, n, out.ctypes.data_as(C.POINTER(C.c_float))))
+        return out
 
     @property
     def handle(self):

@@ -69,6 +69,8 @@ SIGNATURES = {
     "ab_runtime_synchronize": (C.c_int, [P]),
     "ab_runtime_stream": (P, [P]),
     "ab_runtime_sm_count": (C.c_int, [P, C.POINTER(i32)]),
+    "ab_runtime_set_wait_limit": (C.c_int, [P, u32]),
+    "ab_runtime_wait_limit": (C.c_int, [P, C.POINTER(u32)]),
     "ab_tensor_zeros": (C.c_int, [P, i32, i32, C.POINTER(u32), C.POINTER(T)]),
     "ab_tensor_free": (C.c_int, [P, C.POINTER(T)]),
     "ab_tensor_write": (C.c_int, [P, T, P, u64]),
@@ -152,6 +154,8 @@ SIGNATURES = {
     "ab_llama_destroy": (C.c_int, [P]),
     "ab_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "ab_comm_create": (C.c_int, [P, C.POINTER(C.c_uint8), i32, i32, PP]),
+    "ab_comm_create_timeout": (C.c_int, [P, C.POINTER(C.c_uint8), i32, i32, u32, PP]),
+    "ab_comm_loopback_reduce": (C.c_int, [P, u32, u32, u32, C.POINTER(C.c_float)]),
     "ab_comm_rank": (C.c_int, [P, C.POINTER(i32), C.POINTER(i32)]),
     "ab_comm_abort": (C.c_int, [P]),
     "ab_comm_destroy": (C.c_int, [P]),

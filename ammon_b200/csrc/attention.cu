@@ -431,13 +431,13 @@ __global__ void __launch_bounds__(kAttnThreads)
     for (uint32_t i = 0; i < ntiles; i++) {
         if (tid == 0 && i >= 1 && issued < ntiles) {
             const uint32_t r = i - 1;
-            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) issue(issued++);
+            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1, p.flags)) issue(issued++);
             else sm_fail = 1;
         }
         __syncwarp();
         if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
         const uint32_t s = i % S;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1))) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1, p.flags))) {
             sm_fail = 1;
             break;
         }
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         if (tid == 0) {
             atomicOr(p.flags, kFlagWaitTimeout);
             for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
-                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1);
+                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1, p.flags);
         }
         __syncthreads();
         pdl_trigger();
@@ -700,13 +700,13 @@ __global__ void __launch_bounds__(kAttnThreads)
         // thread 0 refills the stage of tile i - 1 once all four warps released it
         if (tid == 0 && i >= 1 && issued < ntiles) {
             const uint32_t r = i - 1;
-            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) issue(issued++);
+            if (mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1, p.flags)) issue(issued++);
             else sm_fail = 1;
         }
         __syncwarp();
         if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
         const uint32_t s = i % S;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1))) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1, p.flags))) {
             sm_fail = 1;
             break;
         }
@@ -786,7 +786,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         if (tid == 0) {
             atomicOr(p.flags, kFlagWaitTimeout);
             for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
-                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1);
+                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1, p.flags);
         }
         __syncthreads();
         pdl_trigger();
@@ -967,7 +967,7 @@ __global__ void __launch_bounds__(kPfThreads)
         if (tid == 0) {
             while (issued < ntiles && issued < i + S) {
                 const uint32_t r = issued - S;
-                if (!mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1)) {
+                if (!mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1, p.flags)) {
                     sm_fail = 1;
                     break;
                 }
@@ -977,7 +977,7 @@ __global__ void __launch_bounds__(kPfThreads)
         __syncwarp();
         if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
         const uint32_t s = i % S;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1))) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1, p.flags))) {
             sm_fail = 1;
             break;
         }
@@ -1080,7 +1080,7 @@ __global__ void __launch_bounds__(kPfThreads)
         if (tid == 0) {
             atomicOr(p.flags, kFlagWaitTimeout);
             for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
-                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1);
+                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1, p.flags);
         }
         __syncthreads();
         pdl_trigger();

@@ -7,8 +7,11 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -28,6 +31,12 @@ struct NcclApi {
                                cudaStream_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+    ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int,
+                                          ncclConfig_t*) = nullptr;
+    ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*comm_finalize)(ncclComm_t) = nullptr;
     const char* (*error_string)(ncclResult_t) = nullptr;
     bool ok = false;
 };
@@ -49,9 +58,15 @@ static NcclApi& nccl() {
         api.all_gather = (decltype(api.all_gather))sym("ncclAllGather");
         api.comm_destroy = (decltype(api.comm_destroy))sym("ncclCommDestroy");
         api.comm_abort = (decltype(api.comm_abort))sym("ncclCommAbort");
+        api.comm_init_rank_config =
+            (decltype(api.comm_init_rank_config))sym("ncclCommInitRankConfig");
+        api.get_async_error = (decltype(api.get_async_error))sym("ncclCommGetAsyncError");
+        api.broadcast = (decltype(api.broadcast))sym("ncclBroadcast");
+        api.comm_finalize = (decltype(api.comm_finalize))sym("ncclCommFinalize");
         api.error_string = (decltype(api.error_string))sym("ncclGetErrorString");
         api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather &&
-                 api.comm_destroy && api.comm_abort && api.error_string;
+                 api.comm_destroy && api.comm_abort && api.comm_init_rank_config &&
+                 api.get_async_error && api.broadcast && api.comm_finalize && api.error_string;
     });
     if (!api.ok) fail(AB_ERR_NCCL, "libnccl.so.2 could not be loaded (set AMMON_B200_NCCL)");
     return api;
@@ -292,11 +307,11 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpSources srcs,
         uint64_t v;
         asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
         if (v < want) {
-            const uint64_t t0 = global_timer_ns();
+            WaitClock clock;
             while (true) {
                 asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
                 if (v >= want) break;
-                if (global_timer_ns() - t0 > 1000000000ull) {
+                if (clock.expired(err)) {
                     ok = 0;
                     break;
                 }
@@ -394,6 +409,103 @@ void record_allgather_bytes(ab_scheme* s, const char* label, ab_comm* c, const v
 
 }  // namespace ab
 
+namespace ab {
+
+// Polls a nonblocking communicator until its pending operation ends; false when `deadline`
+// (steady clock) passes first. Throws on an NCCL error.
+static bool nccl_settle(ncclComm_t comm, std::chrono::steady_clock::time_point deadline,
+                        const char* what) {
+    while (true) {
+        ncclResult_t st = ncclInProgress;
+        nccl_check(nccl().get_async_error(comm, &st), what);
+        if (st == ncclSuccess) return true;
+        if (st != ncclInProgress) nccl_check(st, what);
+        if (std::chrono::steady_clock::now() > deadline) return false;
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+}
+
+// Creates the rank's communicator in two stages so that a rank that never joins ends the
+// call instead of blocking it forever. Stage 1, the rendezvous: a nonblocking communicator on
+// the caller's id, polled until every rank joined or `timeout_ms` passed; on timeout it is
+// aborted (ncclCommAbort) and the call fails. Over it rank 0 broadcasts a fresh id, and the
+// rendezvous communicator is finalised and destroyed. Stage 2: the blocking communicator on
+// the fresh id that the step's collectives use (captured into CUDA graphs, which a nonblocking
+// communicator's deferred launches would not allow); every rank is known alive by then.
+static ncclComm_t comm_init_bounded(Runtime* rt, const ncclUniqueId& id, int world, int rank,
+                                    uint32_t timeout_ms) {
+    NcclApi& api = nccl();
+    const auto deadline =
+        std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t probe = nullptr;
+    ncclResult_t r = api.comm_init_rank_config(&probe, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) nccl_check(r, "ncclCommInitRankConfig");
+    auto give_up = [&](const std::string& why) {
+        api.comm_abort(probe);
+        fail(AB_ERR_NCCL, why + " (rendezvous communicator aborted)");
+    };
+    bool ok = false;
+    try {
+        ok = nccl_settle(probe, deadline, "communicator rendezvous");
+    } catch (...) {
+        api.comm_abort(probe);
+        throw;
+    }
+    if (!ok)
+        give_up("not every one of the " + std::to_string(world) + " ranks joined the "
+                "communicator within " + std::to_string(timeout_ms) + " ms");
+    ncclUniqueId fresh = {};
+    if (rank == 0) {
+        r = api.get_unique_id(&fresh);
+        if (r != ncclSuccess) give_up(std::string("ncclGetUniqueId: ") + api.error_string(r));
+    }
+    unsigned char* d = nullptr;
+    if (cudaMalloc(&d, sizeof(fresh)) != cudaSuccess) give_up("cudaMalloc of the id buffer");
+    cudaError_t e = cudaMemcpy(d, &fresh, sizeof(fresh), cudaMemcpyHostToDevice);
+    r = e == cudaSuccess ? api.broadcast(d, d, sizeof(fresh), ncclUint8, 0, probe, rt->stream)
+                         : ncclSuccess;
+    bool done = e == cudaSuccess && (r == ncclSuccess || r == ncclInProgress) &&
+                nccl_settle(probe, deadline, "id broadcast");
+    // the broadcast's kernel ends once every rank took part; wait for it, bounded
+    while (done) {
+        e = cudaStreamQuery(rt->stream);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady || std::chrono::steady_clock::now() > deadline) {
+            done = false;
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (done) done = cudaMemcpy(&fresh, d, sizeof(fresh), cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (!done) {
+        api.comm_abort(probe);
+        cudaStreamSynchronize(rt->stream);
+        cudaFree(d);
+        fail(AB_ERR_NCCL, "id broadcast over the rendezvous communicator did not complete "
+                          "within " + std::to_string(timeout_ms) + " ms (aborted)");
+    }
+    cudaFree(d);
+    r = api.comm_finalize(probe);
+    if ((r != ncclSuccess && r != ncclInProgress) || !nccl_settle(probe, deadline, "finalize"))
+        give_up("rendezvous communicator did not finalise");
+    api.comm_destroy(probe);
+    ncclComm_t comm = nullptr;
+    nccl_check(api.comm_init_rank(&comm, world, fresh, rank), "ncclCommInitRank");
+    return comm;
+}
+
+static uint32_t env_comm_timeout_ms() {
+    if (const char* e = std::getenv("AMMON_B200_COMM_TIMEOUT_MS")) {
+        const long v = std::atol(e);
+        if (v > 0) return (uint32_t)v;
+    }
+    return 300000;
+}
+
+}  // namespace ab
+
 using namespace ab;
 
 extern "C" {
@@ -407,24 +519,77 @@ int ab_comm_unique_id(uint8_t* id) {
     });
 }
 
-int ab_comm_create(ab_runtime* rt, const uint8_t* id, int32_t rank, int32_t world,
-                   ab_comm** out) {
+int ab_comm_create_timeout(ab_runtime* rt, const uint8_t* id, int32_t rank, int32_t world,
+                           uint32_t timeout_ms, ab_comm** out) {
     return guard([&] {
         if (!rt || !id || !out) fail(AB_ERR_ARGUMENT, "null argument");
         if (world < 1 || rank < 0 || rank >= world) fail(AB_ERR_ARGUMENT, "bad rank / world");
+        if (timeout_ms == 0) fail(AB_ERR_ARGUMENT, "timeout must be at least 1 ms");
         ncclUniqueId u;
         std::memcpy(u.internal, id, NCCL_UNIQUE_ID_BYTES);
         rt->activate();
+        ncclComm_t comm = comm_init_bounded(rt, u, world, rank, timeout_ms);
         auto* c = new ab_comm();
         c->rt = rt;
         c->rank = rank;
         c->world = world;
-        ncclResult_t r = nccl().comm_init_rank(&c->comm, world, u, rank);
-        if (r != ncclSuccess) {
-            delete c;
-            nccl_check(r, "ncclCommInitRank");
-        }
+        c->comm = comm;
         *out = c;
+    });
+}
+
+int ab_comm_create(ab_runtime* rt, const uint8_t* id, int32_t rank, int32_t world,
+                   ab_comm** out) {
+    return ab_comm_create_timeout(rt, id, rank, world, env_comm_timeout_ms(), out);
+}
+
+// A one-rank run of the all-reduce kernel over `world` slots in this GPU's memory; the
+// arrivals of the ranks not in `ready` are never written.
+int ab_comm_loopback_reduce(ab_runtime* rt, uint32_t world, uint32_t ready, uint32_t n,
+                            float* out) {
+    return guard([&] {
+        if (!rt || !out) fail(AB_ERR_ARGUMENT, "null argument");
+        if (world < 1 || world > kTpMaxWorld) fail(AB_ERR_ARGUMENT, "world must be 1..8");
+        if (n == 0 || n > (1u << 24)) fail(AB_ERR_ARGUMENT, "n must be 1..2^24");
+        rt->activate();
+        // [arrivals: kTpMaxWorld u64][sinks for the peers' copies: kTpMaxWorld u64][epoch u64]
+        // [pad to 256][world slots of n floats][n floats of result]
+        const size_t bytes = 256 + ((size_t)world + 1) * n * 4;
+        unsigned char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes), "cudaMalloc");
+        uint64_t* arrivals = reinterpret_cast<uint64_t*>(d);
+        uint64_t* sinks = arrivals + kTpMaxWorld;
+        uint64_t* epoch = sinks + kTpMaxWorld;
+        float* slots = reinterpret_cast<float*>(d + 256);
+        float* x = slots + (size_t)world * n;
+        std::vector<uint64_t> head(32, 0);
+        const uint64_t ep = 1;
+        const uint32_t site = 0;
+        for (uint32_t r = 1; r < world; r++)
+            if (ready & (1u << r)) head[r] = tp_signal_value(ep, site);
+        head[2 * kTpMaxWorld] = ep;
+        std::vector<float> h((size_t)world * n);
+        for (uint32_t r = 0; r < world; r++)
+            for (uint32_t i = 0; i < n; i++) h[(size_t)r * n + i] = (float)(r + 1) + 0.25f * (i % 7);
+        TpSources srcs = {};
+        for (uint32_t r = 0; r < world; r++) {
+            srcs.src[r] = slots + (size_t)r * n;
+            srcs.flag[r] = r == 0 ? arrivals : sinks + r;
+        }
+        const unsigned grid = std::max(1u, std::min(32u, (n + 1023) / 1024));
+        cudaError_t e = cudaMemset(d, 0, bytes);
+        if (e == cudaSuccess) e = cudaMemcpy(d, head.data(), head.size() * 8, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(slots, h.data(), h.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = launch(rt->stream, dim3(grid), dim3(256), 0, false, tp_reduce_kernel, srcs,
+                       (const uint64_t*)arrivals, (const uint64_t*)epoch, site, world, x, n,
+                       rt->flags);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+        if (e == cudaSuccess) e = cudaMemcpy(out, x, (size_t)n * 4, cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        cuda_check(e, "loopback all-reduce");
+        rt->check_flags();
     });
 }
 

@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t smem0 = smem_u32(smem);
         uint32_t s = 0, ph = 0, kb = kb0 + rot;
         for (uint32_t i = 0; i < nk; i++) {
-            if (i >= p.stages && !mbar_wait_bounded(smem_u32(&empty_bar[s]), ph ^ 1)) {
+            if (i >= p.stages && !mbar_wait_bounded(smem_u32(&empty_bar[s]), ph ^ 1, p.flags)) {
                 sm_ok = 0;
                 break;
             }
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t smem0 = smem_u32(smem);
         uint32_t s = 0, ph = 0;
         for (uint32_t i = 0; i < nk; i++) {
-            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), ph)) {
+            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), ph, p.flags)) {
                 sm_ok = 0;
                 break;
             }
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
     }
-    const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0);
+    const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0, p.flags);
     tc_fence_after();
     __syncthreads();
     const bool ok = __syncthreads_and(got && sm_ok != 0);
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (threadIdx.x == 0) {
             atomicOr(p.flags, kFlagWaitTimeout);
             // let the committed MMAs drain before TMEM is released
-            mbar_wait_bounded(smem_u32(&done_bar), 0);
+            mbar_wait_bounded(smem_u32(&done_bar), 0, p.flags);
         }
     }
     tc_fence_before();
@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
         const uint32_t smem0 = smem_u32(smem);
         uint32_t s = 0, ph = 0, kb = kb0 + rot;
         for (uint32_t i = 0; i < nk; i++) {
-            if (i >= p.stages && !mbar_wait_bounded(smem_u32(&empty_bar[s]), ph ^ 1)) {
+            if (i >= p.stages && !mbar_wait_bounded(smem_u32(&empty_bar[s]), ph ^ 1, p.flags)) {
                 sm_ok = 0;
                 break;
             }
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
         const uint32_t smem0 = smem_u32(smem);
         uint32_t s = 0, ph = 0;
         for (uint32_t i = 0; i < nk; i++) {
-            if (!mbar_wait_bounded(smem_u32(&split_bar[s]), ph)) {
+            if (!mbar_wait_bounded(smem_u32(&split_bar[s]), ph, p.flags)) {
                 sm_ok = 0;
                 break;
             }
@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
         const uint32_t t = threadIdx.x - 64;
         for (uint32_t i = 0; i < nk; i++) {
             const uint32_t s = i % p.stages;
-            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+            if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (i / p.stages) & 1, p.flags)) {
                 sm_ok = 0;
                 break;
             }
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
             mbar_arrive(smem_u32(&split_bar[s]));
         }
     }
-    const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0);
+    const bool got = mbar_wait_bounded(smem_u32(&done_bar), 0, p.flags);
     tc_fence_after();
     const bool ok = __syncthreads_and(got && sm_ok != 0);
     pdl_trigger();
@@ -541,7 +541,7 @@ __global__ void __launch_bounds__(kTfThreads, 1)
         }
     } else if (threadIdx.x == 0) {
         atomicOr(p.flags, kFlagWaitTimeout);
-        mbar_wait_bounded(smem_u32(&done_bar), 0);
+        mbar_wait_bounded(smem_u32(&done_bar), 0, p.flags);
     }
     tc_fence_before();
     __syncthreads();

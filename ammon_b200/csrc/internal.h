@@ -94,9 +94,13 @@ struct Runtime {
     int device = 0;
     int sm_count = 0;
     cudaStream_t stream = nullptr;
-    uint32_t* flags = nullptr;  // device word: bit flags raised by kernels
+    // device flag block (256 bytes): [0] u32 bit flags raised by kernels, [8] u64 limit of
+    // every bounded wait in nanoseconds (read by the kernels once a wait has lasted 1 ms)
+    uint32_t* flags = nullptr;
+    uint64_t wait_limit_ms = 2000;
     void activate() const;      // cudaSetDevice(device)
     void check_flags();         // reads + clears the flag word, throws AB_ERR_DEVICE
+    void set_wait_limit_ms(uint64_t ms);  // writes the limit into the flag block
 };
 
 enum DeviceFlag : uint32_t {

@@ -6,6 +6,7 @@
 // scheme is a list of validated launch closures; the first submit captures them into a
 // CUDA graph on the runtime stream and later submits relaunch the instantiated graph.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <sstream>
 
@@ -89,6 +90,14 @@ std::string device_flag_message(uint32_t f) {
     if (f & kFlagPositionRange) m += " decode position beyond the cache's seq_len;";
     if (f & kFlagWaitTimeout) m += " a bounded wait timed out;";
     return m;
+}
+
+void Runtime::set_wait_limit_ms(uint64_t ms) {
+    const uint64_t ns = ms * 1000000ull;
+    cuda_check(cudaMemcpy(reinterpret_cast<unsigned char*>(flags) + 8, &ns, 8,
+                          cudaMemcpyHostToDevice),
+               "write wait limit");
+    wait_limit_ms = ms;
 }
 
 void Runtime::check_flags() {
@@ -234,6 +243,12 @@ int ab_runtime_create(int32_t device, ab_runtime** out) {
                        "create stream");
             cuda_check(cudaMalloc(&rt->flags, 256), "allocate flag word");
             cuda_check(cudaMemset(rt->flags, 0, 256), "clear flag word");
+            uint64_t limit_ms = 2000;
+            if (const char* e = std::getenv("AMMON_B200_WAIT_MS")) {
+                const long v = std::atol(e);
+                if (v > 0) limit_ms = (uint64_t)v;
+            }
+            rt->set_wait_limit_ms(limit_ms);
         } catch (...) {
             if (rt->stream) cudaStreamDestroy(rt->stream);
             if (rt->flags) cudaFree(rt->flags);
@@ -265,6 +280,23 @@ int ab_runtime_synchronize(ab_runtime* rt) {
 }
 
 void* ab_runtime_stream(ab_runtime* rt) { return rt ? (void*)rt->stream : nullptr; }
+
+int ab_runtime_set_wait_limit(ab_runtime* rt, uint32_t ms) {
+    return guard([&] {
+        if (!rt) fail(AB_ERR_ARGUMENT, "null runtime");
+        if (ms == 0) fail(AB_ERR_ARGUMENT, "wait limit must be at least 1 ms");
+        rt->activate();
+        cuda_check(cudaStreamSynchronize(rt->stream), "stream synchronize");
+        rt->set_wait_limit_ms(ms);
+    });
+}
+
+int ab_runtime_wait_limit(ab_runtime* rt, uint32_t* ms) {
+    return guard([&] {
+        if (!rt || !ms) fail(AB_ERR_ARGUMENT, "null argument");
+        *ms = (uint32_t)rt->wait_limit_ms;
+    });
+}
 
 int ab_runtime_sm_count(ab_runtime* rt, int32_t* out) {
     return guard([&] {

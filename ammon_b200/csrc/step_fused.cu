@@ -105,7 +105,6 @@ struct PsParams {
     uint32_t feedback;
     uint32_t* bar;     // [0] grid barrier counter, [1] exit counter, [2] abort word
     uint32_t* flags;
-    uint64_t wait_ns;
     uint32_t stall_barrier;  // test hook: CTA 0 never arrives at this barrier (0 = none)
     uint64_t* trace;         // optional [barriers][grid] %globaltimer at each arrival
     // tensor parallelism (world > 1): every rank's exchange block as this rank addresses it
@@ -208,12 +207,12 @@ __device__ __forceinline__ void raise_abort(const PsParams& p) {
 // Bounded wait on an mbarrier phase that also gives up when another CTA aborted.
 __device__ __forceinline__ bool ps_wait(const PsParams& p, uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
+    WaitClock clock;
     uint32_t n = 0;
     while (!mbar_try_wait(bar, parity)) {
         if ((++n & 63) == 0) {
             if (aborted(p)) return false;
-            if (global_timer_ns() - t0 > p.wait_ns) {
+            if (clock.expired(p.flags)) {
                 raise_abort(p);
                 return false;
             }
@@ -530,7 +529,7 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
         if (ok) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const uint32_t target = epoch * gridDim.x;
         if (ok && ld_acquire(p.bar) < target) {
-            const uint64_t t0 = global_timer_ns();
+            WaitClock clock;
             uint32_t n = 0;
             while (ld_acquire(p.bar) < target) {
                 if ((++n & 15) == 0) {
@@ -538,7 +537,7 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
                         ok = 0;
                         break;
                     }
-                    if (global_timer_ns() - t0 > p.wait_ns) {
+                    if (clock.expired(p.flags)) {
                         raise_abort(p);
                         ok = 0;
                         break;
@@ -585,7 +584,7 @@ __device__ bool tp_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch, 
         }
         const unsigned long long* mine = xb_ctr(p, p.rank, kXbAr);
         if (ok && ld_acquire_sys64(mine) < target) {
-            const uint64_t t0 = global_timer_ns();
+            WaitClock clock;
             uint32_t n = 0;
             while (ld_acquire_sys64(mine) < target) {
                 if ((++n & 15) == 0) {
@@ -593,7 +592,7 @@ __device__ bool tp_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch, 
                         ok = 0;
                         break;
                     }
-                    if (global_timer_ns() - t0 > p.wait_ns) {
+                    if (clock.expired(p.flags)) {
                         raise_abort(p);
                         ok = 0;
                         break;
@@ -900,8 +899,7 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
         if (!ok) {
             // aborting: wait (bounded) for the copies still in flight into the ring
             for (uint32_t k = g > kPsSlots ? g - kPsSlots : 0; k < g; k++)
-                mbar_wait_bounded(smem_u32(&s.full[k % kPsSlots]), (k / kPsSlots) & 1,
-                                  p.wait_ns);
+                mbar_wait_bounded(smem_u32(&s.full[k % kPsSlots]), (k / kPsSlots) & 1, p.flags);
         }
         return;
     }
@@ -1015,9 +1013,9 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
                                  : "memory");
                 const unsigned long long want = (launch + 1) * p.world;
                 const unsigned long long* mine = xb_ctr(p, p.rank, kXbAm);
-                const uint64_t t0 = global_timer_ns();
+                WaitClock clock;
                 while (ld_acquire_sys64(mine) < want) {
-                    if (global_timer_ns() - t0 > p.wait_ns) {
+                    if (clock.expired(p.flags)) {
                         raise_abort(p);
                         merged = false;
                         break;
@@ -1076,17 +1074,6 @@ struct FusedStep {
 bool fused_step_enabled() {
     const char* e = std::getenv("AMMON_B200_FUSED_STEP");
     return !(e && e[0] == '0');
-}
-
-// Limit of every bounded wait of the launch (AMMON_B200_WAIT_MS, default 2 s; read at model
-// creation). A phase takes at most a few hundred microseconds, so the limit only ends waits
-// that would otherwise never end.
-static uint64_t env_wait_ns() {
-    if (const char* e = std::getenv("AMMON_B200_WAIT_MS")) {
-        const long v = std::atol(e);
-        if (v > 0) return (uint64_t)v * 1000000ull;
-    }
-    return 2000000000ull;
 }
 
 // Test hook for the error path (AMMON_B200_TEST_STALL_BARRIER=n, read at model creation): CTA 0
@@ -1165,7 +1152,6 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     p.vocab_all = m.vocab * m.world;
     for (uint32_t r = 0; r < kTpMaxWorld; r++) p.xb[r] = r < m.world ? m.xblock[r] : nullptr;
     p.launch = m.world > 1 ? (unsigned long long*)(m.xblock[m.rank] + kXbLaunch) : nullptr;
-    p.wait_ns = env_wait_ns();
     p.stall_barrier = env_stall_barrier();
     // one scratch allocation: layer table, q, o, h, attention partials, tickets, candidates,
     // barrier words, trace

@@ -54,13 +54,41 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
-// Waits for phase `phase` of the barrier, giving up after `limit_ns` (returns false).
+// Limit of every bounded wait. The runtime's flag block holds it as a u64 (nanoseconds) at
+// byte 8, behind the flag word (ab_runtime_set_wait_limit; 0 = the default of 2 s). A wait
+// reads it only once it has lasted kWaitFloorNs, so waits that end sooner cost no load.
+constexpr uint64_t kWaitDefaultNs = 2000000000ull;
+constexpr uint64_t kWaitFloorNs = 1000000ull;
+__device__ __forceinline__ uint64_t wait_limit_ns(const uint32_t* flags) {
+    const uint64_t v = flags ? *reinterpret_cast<const volatile uint64_t*>(flags + 2) : 0;
+    return v ? v : kWaitDefaultNs;
+}
+
+// Tracks one bounded wait: expired() is true once the wait has lasted the flag block's limit
+// (and at least kWaitFloorNs).
+struct WaitClock {
+    uint64_t t0;
+    uint64_t limit = kWaitFloorNs;
+    bool read = false;
+    __device__ __forceinline__ WaitClock() : t0(global_timer_ns()) {}
+    __device__ __forceinline__ bool expired(const uint32_t* flags) {
+        const uint64_t dt = global_timer_ns() - t0;
+        if (dt <= limit) return false;
+        if (read) return true;
+        read = true;
+        limit = wait_limit_ns(flags);
+        return dt > limit;
+    }
+};
+
+// Waits for phase `phase` of the barrier, giving up after the flag block's limit (returns
+// false).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t phase,
-                                                  uint64_t limit_ns = 2000000000ull) {
+                                                  const uint32_t* flags) {
     if (mbar_try_wait(bar, phase)) return true;
-    const uint64_t t0 = global_timer_ns();
+    WaitClock clock;
     while (!mbar_try_wait(bar, phase))
-        if (global_timer_ns() - t0 > limit_ns) return false;
+        if (clock.expired(flags)) return false;
     return true;
 }
 

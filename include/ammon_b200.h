@@ -78,6 +78,14 @@ int ab_runtime_synchronize(ab_runtime* rt);
 void* ab_runtime_stream(ab_runtime* rt);
 /* Number of SMs of the runtime's device. */
 int ab_runtime_sm_count(ab_runtime* rt, int32_t* out);
+/* Limit of every bounded wait inside the runtime's kernels (mbarrier rings, grid barriers of
+ * the persistent step, peer flags of the all-reduce), in milliseconds; at least 1 ms takes
+ * effect. Default 2000, or AMMON_B200_WAIT_MS when the runtime is created. A wait that runs out
+ * ends its kernel early and the next synchronising call reports AB_ERR_DEVICE ("bounded wait
+ * timed out"); the device stays usable. Synchronises the runtime stream first. No reference
+ * counterpart: Goldy has no device-side waits. */
+int ab_runtime_set_wait_limit(ab_runtime* rt, uint32_t ms);
+int ab_runtime_wait_limit(ab_runtime* rt, uint32_t* ms);
 
 /* ---- tensors (goldy::Tensor::zeros / from_f32 / host take) ---------------- */
 int ab_tensor_zeros(ab_runtime* rt, int32_t dtype, int32_t rank, const uint32_t* dims,
@@ -374,9 +382,23 @@ typedef struct ab_comm ab_comm;
 #define AB_COMM_ID_BYTES 128
 /* A fresh communicator id (rank 0 makes it and shares it with the other ranks). */
 int ab_comm_unique_id(uint8_t* id);
+/* Joins the communicator of `world` ranks that `id` names. A rank that never joins ends the
+ * call on the others with AB_ERR_NCCL after timeout_ms (the rendezvous communicator is
+ * aborted with ncclCommAbort) instead of blocking it; ab_comm_create takes the timeout from
+ * AMMON_B200_COMM_TIMEOUT_MS, default 300000. */
+int ab_comm_create_timeout(ab_runtime* rt, const uint8_t* id, int32_t rank, int32_t world,
+                           uint32_t timeout_ms, ab_comm** out);
 int ab_comm_create(ab_runtime* rt, const uint8_t* id, int32_t rank, int32_t world,
                    ab_comm** out);
 int ab_comm_rank(const ab_comm* c, int32_t* rank, int32_t* world);
+/* Diagnostic of the all-reduce's bounded wait, on one GPU: runs the tensor-parallel
+ * all-reduce kernel over `world` (1..8) ranks whose partials (rank r: r + 1 + 0.25*(i % 7))
+ * and arrival words all sit in this GPU's memory. Rank 0 is this process; rank r > 0 has
+ * arrived when bit r of `ready` is set and never arrives otherwise. out (n floats, host)
+ * receives the rank-ordered sum; with a rank missing the kernel gives up after the
+ * runtime's wait limit and the call returns AB_ERR_DEVICE ("bounded wait timed out"). */
+int ab_comm_loopback_reduce(ab_runtime* rt, uint32_t world, uint32_t ready, uint32_t n,
+                            float* out);
 /* Aborts outstanding collectives (error paths); destroy still frees the handle. */
 int ab_comm_abort(ab_comm* c);
 int ab_comm_destroy(ab_comm* c);

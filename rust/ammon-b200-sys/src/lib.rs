@@ -99,6 +99,8 @@ extern "C" {
     pub fn ab_runtime_synchronize(rt: *mut ab_runtime) -> c_int;
     pub fn ab_runtime_stream(rt: *mut ab_runtime) -> *mut c_void;
     pub fn ab_runtime_sm_count(rt: *mut ab_runtime, out_: *mut i32) -> c_int;
+    pub fn ab_runtime_set_wait_limit(rt: *mut ab_runtime, ms: u32) -> c_int;
+    pub fn ab_runtime_wait_limit(rt: *mut ab_runtime, ms: *mut u32) -> c_int;
     pub fn ab_tensor_zeros(rt: *mut ab_runtime, dtype: i32, rank: i32, dims: *const u32, out_: *mut ab_tensor) -> c_int;
     pub fn ab_tensor_free(rt: *mut ab_runtime, t: *mut ab_tensor) -> c_int;
     pub fn ab_tensor_write(rt: *mut ab_runtime, t: ab_tensor, host: *const c_void, bytes: u64) -> c_int;
@@ -172,8 +174,10 @@ extern "C" {
     pub fn ab_llama_as_model(m: *mut ab_llama, out_: *mut ab_autoregressive_model) -> c_int;
     pub fn ab_llama_destroy(m: *mut ab_llama) -> c_int;
     pub fn ab_comm_unique_id(id: *mut u8) -> c_int;
+    pub fn ab_comm_create_timeout(rt: *mut ab_runtime, id: *const u8, rank: i32, world: i32, timeout_ms: u32, out_: *mut *mut ab_comm) -> c_int;
     pub fn ab_comm_create(rt: *mut ab_runtime, id: *const u8, rank: i32, world: i32, out_: *mut *mut ab_comm) -> c_int;
     pub fn ab_comm_rank(c: *const ab_comm, rank: *mut i32, world: *mut i32) -> c_int;
+    pub fn ab_comm_loopback_reduce(rt: *mut ab_runtime, world: u32, ready: u32, n: u32, out_: *mut f32) -> c_int;
     pub fn ab_comm_abort(c: *mut ab_comm) -> c_int;
     pub fn ab_comm_destroy(c: *mut ab_comm) -> c_int;
     pub fn ab_comm_last_error() -> *const c_char;

@@ -158,11 +158,16 @@ def test_fused_step_trace_records_every_barrier(rt):
 
 def test_fused_step_wait_limit_ends_a_stalled_barrier(rt, orc):
     """CTA 0 never arrives at the third grid barrier (test hook): every other CTA's wait there
-    runs out after 20 ms, the launch ends, the step raises DeviceError (bounded wait timed out)
-    and the next launches on the same device work."""
-    g = _model(rt, AMMON_B200_TEST_STALL_BARRIER=3, AMMON_B200_WAIT_MS=20)
-    with pytest.raises(ab.DeviceError, match="bounded wait timed out"):
-        g.step_batch([9], [0], logits=False)
+    runs out after the runtime's wait limit (20 ms here), the launch ends, the step raises
+    DeviceError (bounded wait timed out) and the next launches on the same device work."""
+    g = _model(rt, AMMON_B200_TEST_STALL_BARRIER=3)
+    old = rt.wait_limit_ms
+    rt.wait_limit_ms = 20
+    try:
+        with pytest.raises(ab.DeviceError, match="bounded wait timed out"):
+            g.step_batch([9], [0], logits=False)
+    finally:
+        rt.wait_limit_ms = old
     g.close()
     h = _model(rt)
     o = _oracle(orc)
