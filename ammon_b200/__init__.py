@@ -751,14 +751,14 @@ class LlamaModel:
         return s
 
     def step_trace(self):
-        """[barriers, 3, grid] %globaltimer ns of each CTA at each grid barrier of the last
-        persistent decode step (arrival, release, operand staged; AMMON_B200_STEP_TRACE set at
-        creation), or None."""
+        """[barriers, 4, grid] %globaltimer ns of each CTA at each grid barrier of the last
+        persistent decode step (arrival, release, operand staged, partial rows pushed at an
+        all-reduce site; AMMON_B200_STEP_TRACE set at creation), or None."""
         nb, ng = C.c_uint32(), C.c_uint32()
         _check(_abi.lib().ab_llama_step_trace(self._h, None, 0, C.byref(nb), C.byref(ng)))
         if nb.value == 0:
             return None
-        out = np.zeros((nb.value, 3, ng.value), np.uint64)
+        out = np.zeros((nb.value, 4, ng.value), np.uint64)
         _check(_abi.lib().ab_llama_step_trace(
             self._h, out.ctypes.data_as(C.POINTER(C.c_uint64)), out.size, C.byref(nb),
             C.byref(ng)))

@@ -106,30 +106,59 @@ struct PsParams {
     uint32_t* bar;     // [0] grid barrier counter, [1] exit counter, [2] abort word
     uint32_t* flags;
     uint32_t stall_barrier;  // test hook: CTA 0 never arrives at this barrier (0 = none)
-    uint64_t* trace;         // optional [barriers][grid] %globaltimer at each arrival
+    uint64_t* trace;         // optional [barriers][kTrCols][grid] %globaltimer (trace_at)
     // tensor parallelism (world > 1): every rank's exchange block as this rank addresses it
     // (layout kXb*), the second residual buffer (all-reduce sites alternate x and x2), this
-    // rank's launch count and the first vocabulary id of its classifier rows
+    // rank's counts (launches, all-reduce sites) and the first vocabulary id of its
+    // classifier rows
     uint32_t world, rank, vocab_off;
     uint32_t vocab_all;  // rows of the (replicated) embedding table: V times the ranks
     unsigned char* xb[kTpMaxWorld];
     float* x2;
-    unsigned long long* launch;
+    unsigned long long* launch;  // [0] launches, [1] all-reduce sites
 };
 
-// Exchange block of one rank: [0] all-reduce arrivals (u64), [8] argmax arrivals (u64),
-// [16] this rank's launch count (u64), [64] argmax candidates [world] x (f32 value, u32 id),
-// [256] partial projections [2 parities][world][d] f32. Counters only grow, kept with the
-// block for the communicator's life: a site's target is the launch count times the sites per
-// launch, plus the site, times the arrivals per site.
-constexpr uint32_t kXbAr = 0, kXbAm = 8, kXbLaunch = 16, kXbCand = 64, kXbPart = 256;
+// Exchange block of one rank: [16] this rank's launch count (u64), [24] all-reduce sites run
+// so far (u64), [64] argmax candidates [world] x two pairs (f32 value, u32 id), [256] partial
+// projections
+// [2 parities][world][d] of 8-byte pairs (f32 value, u32 site flag). A pair is written with
+// one 8-byte store, so a reader that sees the site's flag sees that site's value: the
+// all-reduce needs no fence or arrival counter (the flag-in-data scheme of low-latency
+// collectives). The counts only grow, kept with the block for the communicator's life
+// (models that share a communicator continue them): site k of a launch carries flag
+// S + k + 1 for the S sites run before it, its argmax candidates S + 2L + 1 (32 bits: unique
+// for 2^32 sites). A launch that ended early still advances both counts on every rank, so the
+// ranks' flags stay in step after an error.
+constexpr uint32_t kXbLaunch = 16, kXbSites = 24, kXbCand = 64, kXbPart = 256;
 
-__device__ __forceinline__ unsigned long long* xb_ctr(const PsParams& p, uint32_t r,
-                                                      uint32_t off) {
-    return reinterpret_cast<unsigned long long*>(p.xb[r] + off);
+static_assert(kXbSites == kXbLaunch + 8, "the counts word pair: launches, then sites");
+
+// rank `r`'s block as this rank addresses it: the pair slots of parity `par`, [world][d]; a
+// pair is one u64 (low half the f32 value's bits, high half the flag), so one scalar 8-byte
+// access moves both
+__device__ __forceinline__ unsigned long long* xb_pairs(const PsParams& p, uint32_t r,
+                                                        uint32_t par) {
+    return reinterpret_cast<unsigned long long*>(p.xb[r] + kXbPart) +
+           (size_t)par * p.world * p.d;
 }
-__device__ __forceinline__ float* xb_part(const PsParams& p, uint32_t r, uint32_t par) {
-    return reinterpret_cast<float*>(p.xb[r] + kXbPart) + (size_t)par * p.world * p.d;
+__device__ __forceinline__ unsigned long long mk_pair(float v, uint32_t flag) {
+    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)flag << 32);
+}
+__device__ __forceinline__ void st_pair(unsigned long long* dst, float v, uint32_t flag) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(mk_pair(v, flag))
+                 : "memory");
+}
+// two consecutive pairs in one 16-byte store (two 8-byte elements, each landing whole)
+__device__ __forceinline__ void st_pair2(unsigned long long* dst, float v0, float v1,
+                                         uint32_t flag) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(mk_pair(v0, flag)),
+                 "l"(mk_pair(v1, flag))
+                 : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_pair(const unsigned long long* src) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
+    return v;
 }
 
 // ---- shared-memory layout ------------------------------------------------------------------
@@ -315,38 +344,50 @@ __device__ void stage_norm(const PsParams& p, const PsSmem& s, const float* x, c
     norm_from_xf(p, s, gain);
 }
 
-// Tensor parallelism: x_new = x_old + the ranks' partial projections of site parity `par`,
-// summed in rank order (every CTA of every rank adds the same values in the same order, so the
-// replicated residual stays bit-identical); the whole x_new is left staged (f32) for the next
-// norm, and this CTA writes its slice of it to x_new for the site after.
-__device__ void tp_reduce_stage(const PsParams& p, const PsSmem& s, uint32_t par,
-                                const float* x_old, float* x_new) {
-    float4* xf = reinterpret_cast<float4*>(s.act + kPsXOff);
-    const float* part = xb_part(p, p.rank, par);
-    const uint32_t nv = p.d / 4;
-    const uint32_t i0 = (uint32_t)((uint64_t)p.d * blockIdx.x / gridDim.x);
-    const uint32_t i1 = (uint32_t)((uint64_t)p.d * (blockIdx.x + 1) / gridDim.x);
-    for (uint32_t v = threadIdx.x; v < nv; v += kPsConsumers * 32) {
-        float4 a = __ldcg(reinterpret_cast<const float4*>(x_old) + v);
-        float4 pr[kTpMaxWorld];
-#pragma unroll
-        for (uint32_t r = 0; r < kTpMaxWorld; r++)
-            if (r < p.world) pr[r] = __ldcg(reinterpret_cast<const float4*>(part + (size_t)r * p.d) + v);
-#pragma unroll
-        for (uint32_t r = 0; r < kTpMaxWorld; r++) {
-            if (r >= p.world) break;
-            a.x += pr[r].x;
-            a.y += pr[r].y;
-            a.z += pr[r].z;
-            a.w += pr[r].w;
+// Tensor parallelism, the all-reduce of one site: x_new = x_old + the ranks' partial rows,
+// summed in rank order (every rank adds the same values in the same order, so the replicated
+// residual stays bit-identical). Every rank splits a phase's rows over its CTAs the same way,
+// so CTA c produced rows [r0, r1) on every rank: it waits for exactly those rows' pairs from
+// every rank (the site's flag in each; one thread per pair, all polls in flight together),
+// sums them and writes x_new[r0, r1). A grid barrier after it publishes the whole x_new on
+// this rank. Bounded like every wait; false when this thread gave up.
+__device__ bool tp_site_reduce(const PsParams& p, const PsSmem& s, uint32_t par, uint32_t r0,
+                               uint32_t r1, uint32_t flag, const float* x_old, float* x_new) {
+    consumers_sync();  // every warp is done with the phase's operand in the activation stage
+    const uint32_t n = r1 - r0, total = n * p.world;
+    float* vals = reinterpret_cast<float*>(s.act);  // [world][n]
+    const unsigned long long* pairs = xb_pairs(p, p.rank, par);
+    bool ok = true;
+    for (uint32_t i = threadIdx.x; i < total && ok; i += kPsConsumers * 32) {
+        const uint32_t r = i / n, u = r0 + i % n;
+        const unsigned long long* src = pairs + (size_t)r * p.d + u;
+        unsigned long long v = ld_pair(src);
+        if ((uint32_t)(v >> 32) != flag) {
+            WaitClock clock;
+            uint32_t k = 0;
+            while ((uint32_t)((v = ld_pair(src)) >> 32) != flag) {
+                if ((++k & 15) == 0) {
+                    if (aborted(p)) {
+                        ok = false;
+                        break;
+                    }
+                    if (clock.expired(p.flags)) {
+                        raise_abort(p);
+                        ok = false;
+                        break;
+                    }
+                }
+            }
         }
-        xf[v] = a;
-        const float c[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (uint32_t e = 0; e < 4; e++)
-            if (4 * v + e >= i0 && 4 * v + e < i1) x_new[4 * v + e] = c[e];
+        vals[i] = __uint_as_float((uint32_t)v);
     }
     consumers_sync();
+    for (uint32_t i = threadIdx.x; i < n; i += kPsConsumers * 32) {
+        float a = __ldcg(x_old + r0 + i);
+        for (uint32_t r = 0; r < p.world; r++) a += vals[r * n + i];
+        x_new[r0 + i] = a;
+    }
+    return ok;
 }
 
 // xs = src[0 .. n) (bf16 produced earlier in this launch).
@@ -417,8 +458,10 @@ __device__ __forceinline__ PsBest first_max2(PsBest a, PsBest b) {
 }
 
 // Consumes this warp's chunks of one phase (chunk g goes to warp g % kPsSlots).
+// `flag`: the all-reduce site's flag (tensor parallelism, wo and w2 phases).
 __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind, uint32_t l,
-                              uint32_t& g, uint32_t pos, bool pos_ok, PsBest* best) {
+                              uint32_t& g, uint32_t pos, bool pos_ok, PsBest* best,
+                              uint32_t flag = 0) {
     const bool tp = p.world > 1;
     const uint32_t par = kind == kPhDown ? 1u : 0u;  // all-reduce site parity
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -462,7 +505,7 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
             if (lane == 0) {
                 if (tp) {  // this rank's partial row, into every rank's exchange block
                     for (uint32_t r = 0; r < p.world; r++)
-                        xb_part(p, r, par)[(size_t)p.rank * p.d + u] = acc[0];
+                        st_pair(xb_pairs(p, r, par) + (size_t)p.rank * p.d + u, acc[0], flag);
                 } else {
                     p.x[u] = xr.x + acc[0];
                 }
@@ -483,8 +526,7 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
         } else if (kind == kPhWo) {
             if (tp) {
                 for (uint32_t r = 0; r < p.world; r++)
-                    reinterpret_cast<float2*>(xb_part(p, r, par) + (size_t)p.rank * p.d)[unit] =
-                        make_float2(y0, y1);
+                    st_pair2(xb_pairs(p, r, par) + (size_t)p.rank * p.d + 2 * unit, y0, y1, flag);
             } else {
                 reinterpret_cast<float2*>(p.x)[unit] = make_float2(xr.x + y0, xr.y + y1);
             }
@@ -513,6 +555,13 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
     return true;
 }
 
+// ---- trace ---------------------------------------------------------------------------------
+// AMMON_B200_STEP_TRACE: [barriers][kTrCols][grid] %globaltimer nanoseconds per CTA and barrier.
+enum : uint32_t { kTrArrive = 0, kTrRelease = 1, kTrStaged = 2, kTrSignal = 3, kTrCols = 4 };
+__device__ __forceinline__ void trace_at(const PsParams& p, uint32_t barrier, uint32_t col) {
+    p.trace[((uint64_t)barrier * kTrCols + col) * gridDim.x + blockIdx.x] = global_timer_ns();
+}
+
 // ---- grid barrier --------------------------------------------------------------------------
 // All consumer threads call it; thread 0 arrives and waits for every CTA's arrival number
 // `epoch`. ok_in false (any warp) makes the whole CTA leave. Returns false when aborting.
@@ -525,7 +574,7 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
         uint32_t ok = s.misc[2] == 0;
         if (p.stall_barrier == epoch && blockIdx.x == 0) ok = 0;  // test hook: never arrives
         if (ok && p.trace)
-            p.trace[((uint64_t)(epoch - 1) * 3 + 0) * gridDim.x + blockIdx.x] = global_timer_ns();
+            trace_at(p, epoch - 1, kTrArrive);
         if (ok) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const uint32_t target = epoch * gridDim.x;
         if (ok && ld_acquire(p.bar) < target) {
@@ -547,71 +596,16 @@ __device__ bool grid_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch
         }
         s.misc[0] = ok;
         if (ok && p.trace)
-            p.trace[((uint64_t)(epoch - 1) * 3 + 1) * gridDim.x + blockIdx.x] = global_timer_ns();
+            trace_at(p, epoch - 1, kTrRelease);
     }
     consumers_sync();
     return s.misc[0] != 0;
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Tensor parallelism: the barrier of an all-reduce site over every CTA of every rank. Each
-// CTA, once its partial rows are in every rank's exchange block, adds one arrival to every
-// rank's counter (release, system scope); thread 0 then waits until this rank's counter
-// reaches `target` (acquire). Bounded like grid_barrier; a rank that gives up leaves the
-// others to run out of their own waits.
-__device__ bool tp_barrier(const PsParams& p, const PsSmem& s, uint32_t& epoch, bool ok_in,
-                           unsigned long long target) {
-    if (!ok_in) s.misc[2] = 1;
-    consumers_sync();
-    epoch++;
-    if (threadIdx.x == 0) {
-        uint32_t ok = s.misc[2] == 0;
-        if (p.stall_barrier == epoch && blockIdx.x == 0) ok = 0;  // test hook
-        if (ok && p.trace)
-            p.trace[((uint64_t)(epoch - 1) * 3 + 0) * gridDim.x + blockIdx.x] = global_timer_ns();
-        if (ok) {
-            __threadfence_system();
-            for (uint32_t r = 0; r < p.world; r++)
-                asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(xb_ctr(p, r, kXbAr))
-                             : "memory");
-            // the local grid-barrier counter counts this barrier too (its targets follow epoch)
-            asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-        }
-        const unsigned long long* mine = xb_ctr(p, p.rank, kXbAr);
-        if (ok && ld_acquire_sys64(mine) < target) {
-            WaitClock clock;
-            uint32_t n = 0;
-            while (ld_acquire_sys64(mine) < target) {
-                if ((++n & 15) == 0) {
-                    if (aborted(p)) {
-                        ok = 0;
-                        break;
-                    }
-                    if (clock.expired(p.flags)) {
-                        raise_abort(p);
-                        ok = 0;
-                        break;
-                    }
-                }
-            }
-        }
-        s.misc[0] = ok;
-        if (ok && p.trace)
-            p.trace[((uint64_t)(epoch - 1) * 3 + 1) * gridDim.x + blockIdx.x] = global_timer_ns();
-    }
-    consumers_sync();
-    return s.misc[0] != 0;
-}
 
 // Trace point: the CTA has staged the operand of the phase that ends at barrier epoch + 1.
 __device__ __forceinline__ void trace_staged(const PsParams& p, uint32_t epoch) {
-    if (p.trace && threadIdx.x == 0)
-        p.trace[((uint64_t)epoch * 3 + 2) * gridDim.x + blockIdx.x] = global_timer_ns();
+    if (p.trace && threadIdx.x == 0) trace_at(p, epoch, kTrStaged);
 }
 
 // ---- attention -----------------------------------------------------------------------------
@@ -929,14 +923,11 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
     ok = grid_barrier(p, s, epoch);
     const bool tp = p.world > 1;
     // tensor parallelism: all-reduce site k of this launch (wo of layer l is 2l, w2 is 2l + 1)
-    const unsigned long long launch = tp ? *p.launch : 0ull;
-    auto ar_target = [&](uint32_t k) {
-        return (launch * 2ull * p.L + k + 1) * (unsigned long long)p.world * gridDim.x;
-    };
+    const unsigned long long sites = tp ? p.launch[1] : 0ull;  // kXbSites follows kXbLaunch
+    auto site_flag = [&](uint32_t k) { return (uint32_t)(sites + k + 1); };
     for (uint32_t l = 0; l < p.L && ok; l++) {
         const PsLayer& ly = p.layers[l];
-        if (tp && l > 0) norm_from_xf(p, s, ly.rms_att);  // x staged by the last w2 site
-        else stage_norm(p, s, p.x, ly.rms_att);
+        stage_norm(p, s, p.x, ly.rms_att);
         trace_staged(p, epoch);
         // this CTA's attention item's first tile (rows before pos) lands during the QKV phase
         const bool staged = attn_prestage_any(p, s, l, npos);
@@ -949,11 +940,15 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
         stage_copy(s, p.o, p.qd);
         trace_staged(p, epoch);
         if (tp) {
-            ok = tp_barrier(p, s, epoch, consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best),
-                            ar_target(2 * l));
+            const uint32_t f = site_flag(2 * l);
+            bool mine = consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best, f);
+            uint32_t u0, u1;
+            cta_range(p.d / 2, &u0, &u1);
+            if (p.trace && threadIdx.x == 0) trace_at(p, epoch, kTrSignal);
+            mine = tp_site_reduce(p, s, 0, 2 * u0, 2 * u1, f, p.x, p.x2) && mine;
+            ok = grid_barrier(p, s, epoch, mine);
             if (!ok) break;
-            tp_reduce_stage(p, s, 0, p.x, p.x2);
-            norm_from_xf(p, s, ly.rms_ffn);
+            stage_norm(p, s, p.x2, ly.rms_ffn);
         } else {
             ok = grid_barrier(p, s, epoch, consume_phase(p, s, kPhWo, l, g, pos, pos_ok, &best));
             if (!ok) break;
@@ -966,9 +961,13 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
         stage_copy(s, p.h, p.F);
         trace_staged(p, epoch);
         if (tp) {
-            ok = tp_barrier(p, s, epoch, consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best),
-                            ar_target(2 * l + 1));
-            if (ok) tp_reduce_stage(p, s, 1, p.x2, p.x);
+            const uint32_t f = site_flag(2 * l + 1);
+            bool mine = consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best, f);
+            uint32_t u0, u1;
+            cta_range(p.d, &u0, &u1);
+            if (p.trace && threadIdx.x == 0) trace_at(p, epoch, kTrSignal);
+            mine = tp_site_reduce(p, s, 1, u0, u1, f, p.x2, p.x) && mine;
+            ok = grid_barrier(p, s, epoch, mine);
         } else {
             ok = grid_barrier(p, s, epoch,
                               consume_phase(p, s, kPhDown, l, g, pos, pos_ok, &best));
@@ -976,8 +975,7 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
     }
     cp_async_wait_all();  // an aborted layer may leave a prestaged tile in flight
     if (ok) {
-        if (tp && p.L > 0) norm_from_xf(p, s, p.rms_final);
-        else stage_norm(p, s, p.x, p.rms_final);
+        stage_norm(p, s, p.x, p.rms_final);
         if (!consume_phase(p, s, kPhCls, 0, g, pos, pos_ok, &best)) s.misc[2] = 1;
     }
     // the CTA's first maximum, then the last CTA keeps the first maximum of all CTAs
@@ -999,34 +997,35 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
                 a = first_max2(a, PsBest{__ldcg(p.cand_v + c), __ldcg(p.cand_i + c)});
             bool merged = true;
             if (tp) {
-                // every rank's best (value, id) into every rank's block, then the first maximum
-                // over the ranks in rank order: all ranks pick the same id
+                // every rank's best (value, id) into every rank's block as two flagged pairs
+                // (this launch's flag: one past its last all-reduce site), then the first
+                // maximum over the ranks in rank order: all ranks pick the same id
+                const uint32_t f = site_flag(2 * p.L);
                 for (uint32_t r = 0; r < p.world; r++) {
-                    float* c = reinterpret_cast<float*>(p.xb[r] + kXbCand) + 2 * p.rank;
-                    c[0] = a.v;
-                    reinterpret_cast<uint32_t*>(c)[1] = a.i;
-                }
-                __threadfence_system();
-                for (uint32_t r = 0; r < p.world; r++)
-                    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(
-                                     xb_ctr(p, r, kXbAm))
+                    unsigned long long* c =
+                        reinterpret_cast<unsigned long long*>(p.xb[r] + kXbCand) + 2 * p.rank;
+                    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(c),
+                                 "l"(mk_pair(a.v, f)),
+                                 "l"((unsigned long long)a.i | ((unsigned long long)f << 32))
                                  : "memory");
-                const unsigned long long want = (launch + 1) * p.world;
-                const unsigned long long* mine = xb_ctr(p, p.rank, kXbAm);
-                WaitClock clock;
-                while (ld_acquire_sys64(mine) < want) {
-                    if (clock.expired(p.flags)) {
-                        raise_abort(p);
-                        merged = false;
-                        break;
-                    }
                 }
+                const unsigned long long* cand =
+                    reinterpret_cast<const unsigned long long*>(p.xb[p.rank] + kXbCand);
                 a = PsBest{-INFINITY, 0xffffffffu};
-                const float* cand = reinterpret_cast<const float*>(p.xb[p.rank] + kXbCand);
-                for (uint32_t r = 0; merged && r < p.world; r++)
-                    a = first_max2(a, PsBest{__ldcv(cand + 2 * r),
-                                             __ldcv(reinterpret_cast<const unsigned int*>(cand) +
-                                                    2 * r + 1)});
+                for (uint32_t r = 0; merged && r < p.world; r++) {
+                    unsigned long long v = ld_pair(cand + 2 * r), i = ld_pair(cand + 2 * r + 1);
+                    WaitClock clock;
+                    while ((uint32_t)(v >> 32) != f || (uint32_t)(i >> 32) != f) {
+                        if (clock.expired(p.flags)) {
+                            raise_abort(p);
+                            merged = false;
+                            break;
+                        }
+                        v = ld_pair(cand + 2 * r);
+                        i = ld_pair(cand + 2 * r + 1);
+                    }
+                    a = first_max2(a, PsBest{__uint_as_float((uint32_t)v), (uint32_t)i});
+                }
             }
             const int32_t id = a.i == 0xffffffffu ? 0 : (int32_t)a.i;
             p.argmax[0] = id;
@@ -1050,7 +1049,10 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_step_kernel(const PsPara
         if (atomicAdd(p.bar + 1, 1u) == gridDim.x - 1) {
             if (ld_relaxed(p.bar + 2))
                 for (uint32_t k = 0; k <= p.KV; k++) p.tickets[k] = 0;
-            if (tp) *p.launch += 1;
+            if (tp) {
+                p.launch[0] += 1;
+                p.launch[1] += 2ull * p.L;
+            }
             p.bar[0] = 0;
             p.bar[1] = 0;
             p.bar[2] = 0;
@@ -1088,7 +1090,7 @@ static uint32_t env_stall_barrier() {
 }
 
 size_t fused_step_xblock_bytes(uint32_t world, uint32_t dim) {
-    return kXbPart + 2ull * world * dim * sizeof(float);
+    return kXbPart + 2ull * world * dim * sizeof(unsigned long long);
 }
 
 // Why the fused step cannot run this model ("" when it can).
@@ -1167,7 +1169,7 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     const size_t b_tk = al(4ull * (p.KV + 1));
     const size_t b_cand = al(8ull * f->grid);
     const size_t b_bar = 256;
-    const size_t b_trace = trace ? al(8ull * 3 * f->barriers * f->grid) : 0;
+    const size_t b_trace = trace ? al(8ull * kTrCols * f->barriers * f->grid) : 0;
     const size_t total =
         b_layers + b_q + b_o + b_h + b_x2 + b_part + b_ml + b_tk + b_cand + b_bar + b_trace;
     try {
@@ -1259,13 +1261,14 @@ void record_fused_step(ab_scheme* s, FusedStep* f, bool feedback) {
     });
 }
 
-// Per-barrier times of the last launch (AMMON_B200_STEP_TRACE set): [barriers][3][grid]
-// nanoseconds of %globaltimer -- arrival, release, and when the CTA had staged the operand of
-// the phase that ends at that barrier; false when tracing is off.
+// Per-barrier times of the last launch (AMMON_B200_STEP_TRACE set): [barriers][4][grid]
+// nanoseconds of %globaltimer -- arrival, release, when the CTA had staged the operand of the
+// phase that ends at that barrier, and (the barriers after an all-reduce site) when it had
+// pushed its partial rows and began to wait for the other ranks'; false when tracing is off.
 bool fused_step_trace(FusedStep* f, std::vector<uint64_t>* out, uint32_t* barriers,
                       uint32_t* grid) {
     if (!f || !f->p.trace) return false;
-    out->resize((size_t)3 * f->barriers * f->grid);
+    out->resize((size_t)kTrCols * f->barriers * f->grid);
     cuda_check(cudaMemcpy(out->data(), f->p.trace, out->size() * 8, cudaMemcpyDeviceToHost),
                "fused step trace");
     *barriers = f->barriers;

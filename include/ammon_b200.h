@@ -356,11 +356,13 @@ int ab_llama_generate_tokens(ab_llama* m, const int32_t* prompt, uint32_t prompt
                              int32_t* out_tokens, uint32_t cap, uint32_t* out_len,
                              double* tokens_per_second);
 /* Profiling aid with no reference counterpart: when the model runs its decode step as the
- * persistent single launch (batch 1, bf16, one GPU; AMMON_B200_STEP_TRACE set at model
- * creation), %globaltimer nanoseconds of each CTA at each grid barrier of the last step,
- * [barriers][3][grid]: its arrival, its release, and when it had staged the operand of the
- * phase that ends at that barrier (0 where no phase stages one); the first
- * min(cap, 3 * barriers * grid) values. *barriers and *grid are 0 when no trace is kept. */
+ * persistent single launch (batch 1, bf16; AMMON_B200_STEP_TRACE set at model creation),
+ * %globaltimer nanoseconds of each CTA at each grid barrier of the last step,
+ * [barriers][4][grid]: its arrival, its release, when it had staged the operand of the phase
+ * that ends at that barrier (0 where no phase stages one), and at the barrier after a
+ * tensor-parallel all-reduce site when it had pushed its partial rows to every rank and began
+ * to wait for the other ranks' (0 at other barriers); the first min(cap, 4 * barriers * grid)
+ * values. *barriers and *grid are 0 when no trace is kept. */
 int ab_llama_step_trace(ab_llama* m, uint64_t* out, uint32_t cap, uint32_t* barriers,
                         uint32_t* grid);
 /* The model's step scheme (recorded on first use), for profiling. */

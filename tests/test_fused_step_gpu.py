@@ -147,7 +147,8 @@ def test_fused_step_trace_records_every_barrier(rt):
     g = _model(rt, AMMON_B200_STEP_TRACE=1)
     g.step_batch([5], [0], logits=False)
     tr = g.step_trace()
-    assert tr is not None and tr.shape[:2] == (1 + 5 * CFG["layers"], 3)
+    assert tr is not None and tr.shape[:2] == (1 + 5 * CFG["layers"], 4)
+    assert np.all(tr[:, 3] == 0)  # one GPU: no all-reduce barriers
     arrive, release = tr[:, 0].astype(np.int64), tr[:, 1].astype(np.int64)
     assert np.all(arrive > 0) and np.all(release >= arrive)
     # every CTA leaves a barrier after the last CTA arrived at it
