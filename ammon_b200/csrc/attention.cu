@@ -822,318 +822,9 @@ __global__ void __launch_bounds__(kAttnThreads)
                              kvh, b, tid);
 }
 
-// ---- prefill attention: rows of one sequence over one shared cache --------------------------
-// When the rows of a launch share one cache (cache_rows == 0: the positions of one prompt),
-// every row reads the same K/V prefix. A CTA then takes 64 query rows -- QP = 64 / G
-// consecutive batch rows times the G query heads of kv head blockIdx.y -- so each staged
-// K/V tile serves 64 queries instead of G (flash attention in the FA2 register layout on
-// mma.sync m16n8k16): per warp, S (16 queries x 64 positions) = Q.K^T with Q as bf16 high +
-// low A fragments, the online softmax per query row with the causal limit of each row (its
-// own position), and O (16 x HD) += P.V with P as bf16 high + low A fragments taken straight
-// from the S accumulators. No split partials: each CTA writes its rows' outputs.
-constexpr uint32_t kPfRows = 64;  // query rows per CTA (16 per warp)
-
-__device__ __forceinline__ void store_pair(float* d, float a, float b) {
-    *reinterpret_cast<float2*>(d) = make_float2(a, b);
-}
-__device__ __forceinline__ void store_pair(bf16* d, float a, float b) {
-    *reinterpret_cast<__nv_bfloat162*>(d) = __floats2bfloat162_rn(a, b);
-}
-constexpr uint32_t kPfMinBatch = 16;  // fewer shared-cache rows take the split decode kernel
-
-template <int HD>
-struct AttnPfLayout {
-    static constexpr uint32_t kRowBytes = HD * 2;
-    static constexpr uint32_t kStage = 2 * kAttnTile * kRowBytes;  // K tile | V tile
-    static constexpr uint32_t kStages = HD == 128 ? 3 : 4;
-    static size_t smem() { return (size_t)kStages * kStage + 1024; }
-};
-
-// Two groups of four warps take alternate K/V tiles for the same 64 query rows (twice the
-// warps in flight over the same CTA count) and merge their (max, sum, O) at the end.
-constexpr uint32_t kPfGroups = 2;
-constexpr uint32_t kPfThreads = 128 * kPfGroups;
-
-template <typename OT, int G, int HD>
-__global__ void __launch_bounds__(kPfThreads)
-    attn_prefill_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
-                            const __grid_constant__ CUtensorMap vmap) {
-    using LY = AttnPfLayout<HD>;
-    constexpr uint32_t S = LY::kStages;
-    constexpr uint32_t NBOX = LY::kRowBytes / 128;
-    constexpr int KS = HD / 16;  // k-steps of Q.K^T
-    constexpr int NT = HD / 8;   // n-tiles of P.V
-    constexpr uint32_t QP = kPfRows / G;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[S];
-    __shared__ __align__(8) uint64_t empty_bar[S];
-    __shared__ int sm_fail;
-    __shared__ uint32_t sm_end;
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-
-    const uint32_t kvh = blockIdx.y, b0 = blockIdx.x * QP;
-    const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-    const uint32_t grp = warp / 4, wq = warp % 4;  // tile parity group, query row block
-    const uint32_t g = lane / 4, t = lane % 4;
-
-    pdl_wait();
-    // this thread's query rows 16 * wq + g (+ 8): the last position each may see (-1: none)
-    int32_t lim[2];
-    const float* qrow[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint32_t r = wq * 16 + g + 8 * h;
-        const uint32_t b = b0 + r / G;
-        lim[h] = -1;
-        qrow[h] = nullptr;
-        if (b < p.batch) {
-            const uint32_t pos = p.step[b].position;
-            if (pos < p.seq) {
-                lim[h] = (int32_t)pos;
-                qrow[h] = p.q + ((uint64_t)b * p.heads + (uint64_t)kvh * G + r % G) * HD;
-            }
-        }
-    }
-    auto issue = [&](uint32_t i) {
-        const uint32_t s = i % S;
-        const uint32_t bar = smem_u32(&full_bar[s]);
-        unsigned char* kst = smem + (size_t)s * LY::kStage;
-        unsigned char* vst = kst + LY::kStage / 2;
-        const int32_t y = (int32_t)(i * kAttnTile);
-        // whole tiles: rows past the block's last position are masked below (cache rows,
-        // or the zero fill past seq)
-        mbar_arrive_expect_tx(bar, LY::kStage);
-#pragma unroll
-        for (uint32_t j = 0; j < NBOX; j++) {
-            const int32_t x = (int32_t)(kvh * HD + j * 64);
-            tma_load_2d(smem_u32(kst + j * kAttnTile * 128), &kmap, x, y, bar);
-            tma_load_2d(smem_u32(vst + j * kAttnTile * 128), &vmap, x, y, bar);
-        }
-    };
-    uint32_t issued = 0;  // meaningful in thread 0
-    if (tid == 0) {
-        uint32_t e = 0;
-        for (uint32_t j = 0; j < QP && b0 + j < p.batch; j++) {
-            const uint32_t pos = p.step[b0 + j].position;
-            if (pos < p.seq) e = max(e, pos + 1);
-        }
-        sm_end = e;
-        for (uint32_t s = 0; s < S; s++) {
-            mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), 4);  // the four warps of the consuming group
-        }
-        fence_barrier_init();
-        sm_fail = 0;
-        const uint32_t nt0 = (e + kAttnTile - 1) / kAttnTile;
-        for (; issued < nt0 && issued < S; issued++) issue(issued);
-    }
-    // Q fragments (rows g / g + 8, k = head dims), pre-scaled, bf16 high + low parts
-    uint32_t qh[KS][4], ql[KS][4];
-    {
-        const float qscale = 1.0f / sqrtf((float)HD);
-#pragma unroll
-        for (int ks = 0; ks < KS; ks++) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-#pragma unroll
-                for (int kh = 0; kh < 2; kh++) {
-                    const uint32_t d = ks * 16 + 2 * t + 8 * kh;
-                    float a = 0.0f, c = 0.0f;
-                    if (qrow[h]) {
-                        a = qrow[h][d] * qscale;
-                        c = qrow[h][d + 1] * qscale;
-                    }
-                    split_bf16x2(a, c, &qh[ks][h + 2 * kh], &ql[ks][h + 2 * kh]);
-                }
-            }
-        }
-    }
-    __syncthreads();
-    const uint32_t ntiles = (sm_end + kAttnTile - 1) / kAttnTile;
-    // the warp's last visible position: tiles past it hold nothing for this warp
-    int32_t wmax = max(lim[0], lim[1]);
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
-
-    float o[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
-    const uint32_t mi = lane / 8, r8 = lane % 8;
-    for (uint32_t i = grp; i < ntiles; i += kPfGroups) {
-        // thread 0 keeps the ring S tiles ahead of its own group: tile j reuses the stage of
-        // tile j - S, released by whichever group consumed it (earlier tiles only, so every
-        // wait ends)
-        if (tid == 0) {
-            while (issued < ntiles && issued < i + S) {
-                const uint32_t r = issued - S;
-                if (!mbar_wait_bounded(smem_u32(&empty_bar[r % S]), (r / S) & 1, p.flags)) {
-                    sm_fail = 1;
-                    break;
-                }
-                issue(issued++);
-            }
-        }
-        __syncwarp();
-        if (__any_sync(0xffffffffu, *(volatile int*)&sm_fail != 0)) break;
-        const uint32_t s = i % S;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full_bar[s]), (i / S) & 1, p.flags))) {
-            sm_fail = 1;
-            break;
-        }
-        const uint32_t t0 = i * kAttnTile;
-        const uint32_t kst = smem_u32(smem + (size_t)s * LY::kStage);
-        const uint32_t vst = kst + LY::kStage / 2;
-        if (wmax >= (int32_t)t0) {
-            // S = Q.K^T: n-tile nt holds positions t0 + 8 nt + (2t, 2t + 1)
-            float sc[8][4];
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
-#pragma unroll
-            for (int ks = 0; ks < KS; ks++) {
-#pragma unroll
-                for (int np = 0; np < 4; np++) {
-                    const uint32_t pos = np * 16 + (mi >= 2 ? 8 : 0) + r8;
-                    const uint32_t dim = ks * 16 + (mi & 1) * 8;
-                    uint32_t kb[4];
-                    ldsm_x4(kst + swizzle_off<128>((dim / 64) * kAttnTile * 128 + pos * 128 +
-                                                   (dim % 64) * 2),
-                            kb);
-                    mma_16816(sc[2 * np], qh[ks], kb[0], kb[1]);
-                    mma_16816(sc[2 * np], ql[ks], kb[0], kb[1]);
-                    mma_16816(sc[2 * np + 1], qh[ks], kb[2], kb[3]);
-                    mma_16816(sc[2 * np + 1], ql[ks], kb[2], kb[3]);
-                }
-            }
-            // causal limits, row maxima over the quad's 64 positions
-            float tmax[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++) {
-                const int32_t pos = (int32_t)(t0 + nt * 8 + 2 * t);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int h = e / 2;
-                    if (pos + (e & 1) > lim[h]) sc[nt][e] = -INFINITY;
-                    tmax[h] = fmaxf(tmax[h], sc[nt][e]);
-                }
-            }
-            float alpha[2];
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
-                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
-                const float nm = fmaxf(mrow[h], tmax[h]);
-                // a row with nothing visible yet keeps m = -inf and weight 0
-                alpha[h] = nm == -INFINITY ? 1.0f : expf(mrow[h] - nm);
-                mrow[h] = nm;
-            }
-            float rs[2] = {0.0f, 0.0f};
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++) {
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int h = e / 2;
-                    const float v = mrow[h] == -INFINITY ? 0.0f : expf(sc[nt][e] - mrow[h]);
-                    sc[nt][e] = v;
-                    rs[h] += v;
-                }
-            }
-            lrow[0] = lrow[0] * alpha[0] + rs[0];
-            lrow[1] = lrow[1] * alpha[1] + rs[1];
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-                o[n][0] *= alpha[0];
-                o[n][1] *= alpha[0];
-                o[n][2] *= alpha[1];
-                o[n][3] *= alpha[1];
-            }
-            // O += P.V, 16 positions per k-step: the S accumulators of n-tiles 2kk, 2kk + 1
-            // are the A fragment of P
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                uint32_t ph[4], pl[4];
-                split_bf16x2(sc[2 * kk][0], sc[2 * kk][1], &ph[0], &pl[0]);
-                split_bf16x2(sc[2 * kk][2], sc[2 * kk][3], &ph[1], &pl[1]);
-                split_bf16x2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], &ph[2], &pl[2]);
-                split_bf16x2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], &ph[3], &pl[3]);
-#pragma unroll
-                for (int np = 0; np < NT / 2; np++) {
-                    const uint32_t pos = kk * 16 + (mi & 1) * 8 + r8;
-                    const uint32_t dim = np * 16 + (mi >= 2 ? 8 : 0);
-                    uint32_t vb[4];
-                    ldsm_x4_t(vst + swizzle_off<128>((dim / 64) * kAttnTile * 128 + pos * 128 +
-                                                     (dim % 64) * 2),
-                              vb);
-                    mma_16816(o[2 * np], ph, vb[0], vb[1]);
-                    mma_16816(o[2 * np], pl, vb[0], vb[1]);
-                    mma_16816(o[2 * np + 1], ph, vb[2], vb[3]);
-                    mma_16816(o[2 * np + 1], pl, vb[2], vb[3]);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
-    }
-    __syncthreads();
-    if (sm_fail) {
-        // a bounded wait ran out: flag it, let the copies in flight land, and stop
-        if (tid == 0) {
-            atomicOr(p.flags, kFlagWaitTimeout);
-            for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
-                mbar_wait_bounded(smem_u32(&full_bar[j % S]), (j / S) & 1, p.flags);
-        }
-        __syncthreads();
-        pdl_trigger();
-        return;
-    }
-    pdl_trigger();
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 1);
-        lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 2);
-    }
-    // group 1 hands its (m, l, O) to group 0 through the (now idle) stage memory
-    float* xo = (float*)smem;                     // [4 warps][NT * 4][32 lanes]
-    float* xml = xo + 4 * NT * 4 * 32;            // [4 warps][4][32 lanes]: m0, m1, l0, l1
-    if (grp == 1) {
-#pragma unroll
-        for (int n = 0; n < NT; n++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) xo[((wq * NT + n) * 4 + e) * 32 + lane] = o[n][e];
-        xml[(wq * 4 + 0) * 32 + lane] = mrow[0];
-        xml[(wq * 4 + 1) * 32 + lane] = mrow[1];
-        xml[(wq * 4 + 2) * 32 + lane] = lrow[0];
-        xml[(wq * 4 + 3) * 32 + lane] = lrow[1];
-    }
-    __syncthreads();
-    if (grp != 0) return;
-    float w0[2], w1[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const float m1 = xml[(wq * 4 + h) * 32 + lane];
-        const float l1 = xml[(wq * 4 + 2 + h) * 32 + lane];
-        const float m = fmaxf(mrow[h], m1);
-        w0[h] = mrow[h] == -INFINITY ? 0.0f : expf(mrow[h] - m);
-        w1[h] = m1 == -INFINITY ? 0.0f : expf(m1 - m);
-        lrow[h] = lrow[h] * w0[h] + l1 * w1[h];
-    }
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        if (!qrow[h] || lrow[h] <= 0.0f) continue;
-        const uint32_t r = wq * 16 + g + 8 * h;
-        const uint32_t b = b0 + r / G;
-        const float inv = 1.0f / lrow[h];
-        OT* dst = (OT*)p.out + ((uint64_t)b * p.heads + (uint64_t)kvh * G + r % G) * HD;
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-            const uint32_t d = n * 8 + 2 * t;
-            const float a0 = o[n][2 * h] * w0[h] + xo[((wq * NT + n) * 4 + 2 * h) * 32 + lane] * w1[h];
-            const float a1 =
-                o[n][2 * h + 1] * w0[h] + xo[((wq * NT + n) * 4 + 2 * h + 1) * 32 + lane] * w1[h];
-            store_pair(dst + d, a0 * inv, a1 * inv);
-        }
-    }
-}
+// Rows of one sequence over one shared cache (a prefill pass) take the tcgen05 prompt kernel
+// (attention_prompt_tc.cu) from this many rows on; fewer take the split decode kernel.
+constexpr uint32_t kPfMinBatch = 16;
 
 // ---- plain-load kernel (head sizes the TMA boxes cannot tile) --------------------------------
 template <typename KT, typename OT, int G>
@@ -1321,33 +1012,11 @@ static void add_attn(ab_scheme* s, const char* label, const AttnParams& p) {
     const uint32_t rowbytes = p.head * esz;
     dim3 grid(p.nsplit, p.kv_heads, p.batch);
     const int swz = rowbytes % 128 == 0 ? 128 : rowbytes % 64 == 0 ? 64 : 0;
-    if (esz == 2 && (p.head == 128 || p.head == 64) && p.cache_rows == 0 &&
-        p.batch >= kPfMinBatch) {
-        // the rows share one cache (a prompt's positions): 64 queries per staged K/V tile
-        CUtensorMap kmap, vmap;
-        const uint64_t inner = (uint64_t)p.kv_heads * p.head;
-        encode_tmap_2d(&kmap, AB_BF16, p.kcache, inner, p.seq, inner * 2, 64, kAttnTile, 128);
-        encode_tmap_2d(&vmap, AB_BF16, p.vcache, inner, p.seq, inner * 2, 64, kAttnTile, 128);
-        const uint32_t qp = kPfRows / G;
-        const dim3 pgrid((p.batch + qp - 1) / qp, p.kv_heads);
-        const size_t smem = p.head == 128 ? AttnPfLayout<128>::smem() : AttnPfLayout<64>::smem();
-        if (p.head == 128) {
-            auto kern = attn_prefill_mma_kernel<OT, G, 128>;
-            s->add(label, [=](cudaStream_t st) {
-                cudaError_t e = set_smem((const void*)kern, smem);
-                if (e != cudaSuccess) return e;
-                return launch(st, pgrid, dim3(kPfThreads), smem, true, kern, p, kmap, vmap);
-            });
-        } else {
-            auto kern = attn_prefill_mma_kernel<OT, G, 64>;
-            s->add(label, [=](cudaStream_t st) {
-                cudaError_t e = set_smem((const void*)kern, smem);
-                if (e != cudaSuccess) return e;
-                return launch(st, pgrid, dim3(kPfThreads), smem, true, kern, p, kmap, vmap);
-            });
-        }
+    // the rows share one cache (a prompt's positions): 128 queries per staged K/V tile on the
+    // 5th-generation tensor cores (attention_prompt_tc.cu)
+    if (esz == 2 && p.cache_rows == 0 && p.batch >= kPfMinBatch &&
+        record_prompt_attention_tc(s, label, p))
         return;
-    }
     if (esz == 2 && (p.head == 128 || p.head == 64)) {
         // bf16 K/V: both products on the tensor cores
         CUtensorMap kmap, vmap;

@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "ops.h"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace ab {
@@ -40,85 +41,6 @@ constexpr int kTcBK = 64;  // bf16 elements per k-block: one 128-byte swizzled r
 constexpr int kTcMaxStages = 8;
 constexpr int kTfBK = 32;          // fp32 elements per k-block: one 128-byte swizzled row
 constexpr int kTfThreads = 192;    // producer warp, MMA warp, 4 split/epilogue warps
-
-// ---- tcgen05 wrappers -------------------------------------------------------------------------
-__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
-                 "r"(cols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// D[tmem] (+)= A[smem desc] x B[smem desc]^T, both K-major.
-__device__ __forceinline__ void tc_mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                            uint32_t accumulate) {
-    const uint32_t m = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m)
-        : "memory");
-}
-// D[tmem] (+)= A x B^T on the tf32 pipe (fp32 operands in shared memory, read as tf32).
-__device__ __forceinline__ void tc_mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                            uint32_t accumulate) {
-    const uint32_t m = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m)
-        : "memory");
-}
-// Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     bar)
-                 : "memory");
-}
-// 16 consecutive f32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes
-// apart (stride byte offset), leading byte offset unused (1), descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)(1024 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
-    return d;
-}
-
-// Instruction descriptor of kind::f16: f32 accumulate, bf16 A and B, both K-major.
-__host__ __device__ constexpr uint32_t tc_idesc_bf16(uint32_t M, uint32_t N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
-}
-
-// Instruction descriptor of kind::tf32: f32 accumulate, tf32 A and B, both K-major.
-__host__ __device__ constexpr uint32_t tc_idesc_tf32(uint32_t M, uint32_t N) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
-}
 
 // High part of the exact split v = hi + lo: v with its 13 low mantissa bits cleared (a
 // tf32 value). lo = v - hi is exact in fp32 and carries the cleared bits.

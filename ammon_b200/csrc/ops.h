@@ -238,6 +238,9 @@ uint32_t attention_max_splits(uint32_t max_groups, uint32_t seq, int sm_count,
                               uint32_t max_splits);
 bool attention_fusable(uint32_t heads, uint32_t kv_heads, uint32_t head, int32_t kv_dtype);
 void record_attention(ab_scheme* s, const char* label, AttnParams p);
+// Prompt attention of a pass whose rows share one bf16 cache (cache_rows == 0), head 64 or
+// 128, on the tcgen05 tensor cores (attention_prompt_tc.cu); false when it does not apply.
+bool record_prompt_attention_tc(ab_scheme* s, const char* label, const AttnParams& p);
 
 // ---- persistent decode step (step_fused.cu) ----------------------------------------------
 // What the single-launch batch-1 decode step reads and writes (device pointers; per-layer

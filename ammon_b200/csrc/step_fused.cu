@@ -87,6 +87,7 @@ struct PsParams {
     const bf16* rms_final;
     uint32_t d, qd, kvd, hd, H, KV, F, V, seq;
     uint32_t upc_qkv, upc_wo, upc_gu, upc_cls;  // units (row pairs) per chunk
+    uint32_t upc_down;                          // w2 rows per chunk
     float theta, eps;
     Step* step;
     float* x;         // [d] residual stream
@@ -260,7 +261,7 @@ __device__ __forceinline__ PsGeom ps_geom(const PsParams& p, uint32_t kind) {
         case kPhQkv: return {(p.qd + 2 * p.kvd) / 2, 2, p.upc_qkv, p.d};
         case kPhWo: return {p.d / 2, 2, p.upc_wo, p.qd};
         case kPhGateUp: return {p.F, 2, p.upc_gu, p.d};
-        case kPhDown: return {p.d, 1, 1, p.F};
+        case kPhDown: return {p.d, 1, p.upc_down, p.F};
         default: return {p.V / 2, 2, p.upc_cls, p.d};
     }
 }
@@ -398,52 +399,62 @@ __device__ void stage_copy(const PsSmem& s, const bf16* src, uint32_t n) {
 }
 
 // ---- consumers: one chunk ------------------------------------------------------------------
+// R rows (row-major, nv 16-byte vectors each) against the staged vector: every lane takes
+// vectors lane, lane + 32, ... with U of them (times R rows) in flight per iteration and two
+// accumulator chains per row and in-flight vector; sums[r] gets row r's lane partial.
+template <uint32_t R, uint32_t U>
+__device__ __forceinline__ void dots_rows(const uint4* w, const uint4* xv, uint32_t nv,
+                                          float* sums) {
+    const uint32_t lane = threadIdx.x % 32;
+    float a0[R][U], a1[R][U];
+#pragma unroll
+    for (uint32_t r = 0; r < R; r++)
+#pragma unroll
+        for (uint32_t u = 0; u < U; u++) a0[r][u] = a1[r][u] = 0.0f;
+    uint32_t j = lane;
+    for (; j + 32 * (U - 1) < nv; j += 32 * U) {
+        uint4 xa[U], wa[R][U];
+#pragma unroll
+        for (uint32_t u = 0; u < U; u++) {
+            xa[u] = xv[j + 32 * u];
+#pragma unroll
+            for (uint32_t r = 0; r < R; r++) wa[r][u] = w[r * nv + j + 32 * u];
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < U; u++)
+#pragma unroll
+            for (uint32_t r = 0; r < R; r++) dot_bf16x8_2(wa[r][u], xa[u], a0[r][u], a1[r][u]);
+    }
+    for (; j < nv; j += 32) {
+        const uint4 x = xv[j];
+#pragma unroll
+        for (uint32_t r = 0; r < R; r++) dot_bf16x8_2(w[r * nv + j], x, a0[r][0], a1[r][0]);
+    }
+#pragma unroll
+    for (uint32_t r = 0; r < R; r++) {
+        float t = 0.0f;
+#pragma unroll
+        for (uint32_t u = 0; u < U; u++) t += a0[r][u] + a1[r][u];
+        sums[r] = t;
+    }
+}
+
 // Dot products of the chunk's rows (row-major, K elements each, back to back in the slot) with
 // the staged activation; every lane ends with every row's sum.
 __device__ __forceinline__ void chunk_dots(const unsigned char* slot, const unsigned char* act,
                                            uint32_t rows, uint32_t K, float acc[kPsMaxRows]) {
-    const uint32_t lane = threadIdx.x % 32, nv = K / 8;
+    const uint32_t nv = K / 8;
     const uint4* w = reinterpret_cast<const uint4*>(slot);
     const uint4* xv = reinterpret_cast<const uint4*>(act);
-    // two accumulator chains per row (even and odd elements): twice the independent FMAs
-    float a0[kPsMaxRows], a1[kPsMaxRows];
+    float part[kPsMaxRows];
 #pragma unroll
-    for (uint32_t r = 0; r < kPsMaxRows; r++) a0[r] = a1[r] = 0.0f;
-    if (rows == kPsMaxRows) {
-        for (uint32_t j = lane; j < nv; j += 32) {
-            const uint4 x = xv[j];
+    for (uint32_t r = 0; r < kPsMaxRows; r++) part[r] = 0.0f;
+    if (rows == 4) dots_rows<4, 2>(w, xv, nv, part);
+    else if (rows == 2) dots_rows<2, 2>(w, xv, nv, part);
+    else if (rows == 1) dots_rows<1, 4>(w, xv, nv, part);
+    else dots_rows<3, 1>(w, xv, nv, part);
 #pragma unroll
-            for (uint32_t r = 0; r < kPsMaxRows; r++) dot_bf16x8_2(w[r * nv + j], x, a0[r], a1[r]);
-        }
-    } else if (rows == 1) {
-        // one long row (a w2 row): four vectors in flight per lane, four accumulator chains
-        uint32_t j = lane;
-        for (; j + 96 < nv; j += 128) {
-            uint4 xa[4], wa[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                xa[k] = xv[j + 32 * k];
-                wa[k] = w[j + 32 * k];
-            }
-            dot_bf16x8_2(wa[0], xa[0], a0[0], a1[0]);
-            dot_bf16x8_2(wa[1], xa[1], a0[1], a1[1]);
-            dot_bf16x8_2(wa[2], xa[2], a0[2], a1[2]);
-            dot_bf16x8_2(wa[3], xa[3], a0[3], a1[3]);
-        }
-        for (; j < nv; j += 32) dot_bf16x8_2(w[j], xv[j], a0[0], a1[0]);
-        a0[0] += a0[1] + a0[2] + a0[3];
-        a1[0] += a1[1] + a1[2] + a1[3];
-        a0[1] = a0[2] = a0[3] = a1[1] = a1[2] = a1[3] = 0.0f;
-    } else {
-        for (uint32_t j = lane; j < nv; j += 32) {
-            const uint4 x = xv[j];
-#pragma unroll
-            for (uint32_t r = 0; r < kPsMaxRows; r++)
-                if (r < rows) dot_bf16x8_2(w[r * nv + j], x, a0[r], a1[r]);
-        }
-    }
-#pragma unroll
-    for (uint32_t r = 0; r < kPsMaxRows; r++) acc[r] = warp_sum(a0[r] + a1[r]);
+    for (uint32_t r = 0; r < kPsMaxRows; r++) acc[r] = warp_sum(part[r]);
 }
 
 struct PsBest {
@@ -478,7 +489,7 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
         float2 xr = make_float2(0.0f, 0.0f);
         if (!tp && kind == kPhWo && lane < n)
             xr = __ldcg(reinterpret_cast<const float2*>(p.x) + u + lane);
-        if (!tp && kind == kPhDown && lane == 0) xr.x = __ldcg(p.x + u);
+        if (!tp && kind == kPhDown && lane < n) xr.x = __ldcg(p.x + u + lane);
         // every lane waits; the warp agrees on one outcome before the full-mask shuffles below
         const bool landed = ps_wait(p, smem_u32(&s.full[slot]), (g / kPsSlots) & 1);
         if (!__all_sync(0xffffffffu, landed)) return false;
@@ -501,18 +512,20 @@ __device__ bool consume_phase(const PsParams& p, const PsSmem& s, uint32_t kind,
             }
             continue;
         }
-        if (kind == kPhDown) {
-            if (lane == 0) {
-                if (tp) {  // this rank's partial row, into every rank's exchange block
-                    for (uint32_t r = 0; r < p.world; r++)
-                        st_pair(xb_pairs(p, r, par) + (size_t)p.rank * p.d + u, acc[0], flag);
-                } else {
-                    p.x[u] = xr.x + acc[0];
-                }
+        if (lane >= n) continue;
+        if (kind == kPhDown) {  // lane i: w2 row u + i
+            float y = acc[0];
+#pragma unroll
+            for (uint32_t r = 1; r < kPsMaxRows; r++)
+                if (r == lane) y = acc[r];
+            if (tp) {  // this rank's partial row, into every rank's exchange block
+                for (uint32_t r = 0; r < p.world; r++)
+                    st_pair(xb_pairs(p, r, par) + (size_t)p.rank * p.d + u + lane, y, flag);
+            } else {
+                p.x[u + lane] = xr.x + y;
             }
             continue;
         }
-        if (lane >= n) continue;
         float y0 = acc[0], y1 = acc[1];
 #pragma unroll
         for (uint32_t i = 1; i < kPsMaxRows / 2; i++)
@@ -1139,6 +1152,8 @@ FusedStep* fused_step_create(Runtime* rt, const FusedStepModel& m) {
     p.upc_wo = upc(p.qd);
     p.upc_gu = upc(p.d);
     p.upc_cls = upc(p.d);
+    // w2 rows per chunk (tensor-parallel shards have short rows: several fill a slot)
+    p.upc_down = std::max(1u, std::min(kPsMaxRows, kPsSlotBytes / (2u * p.F)));
     p.embed = (const bf16*)m.embed;
     p.wcls = (const bf16*)m.wcls;
     p.rms_final = (const bf16*)m.rms_final;
