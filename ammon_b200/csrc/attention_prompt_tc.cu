@@ -16,8 +16,8 @@
 //    the row's causal limit, keep the running max and sum, write P to shared memory as the A
 //    operand of the next P.V, and rescale O in TMEM (tcgen05.ld/st) only when the row's max
 //    grew by more than kPtRescale since the reference it was last scaled to (exact either way:
-//    P and the sum use the same reference); at the end they read O, divide by the sum and
-//    store the row.
+//    P and the sum use the same reference; scores in base 2, exp2f); at the end they read O,
+//    divide by the sum and store the row.
 // Q is fp32 and P carries values up to e^kPtRescale, so both go to the tensor core as bf16
 // high + low pairs (two MMAs each), keeping the scores and the weighted sums near fp32
 // precision; K and V are the bf16 cache itself.
@@ -39,7 +39,11 @@ constexpr uint32_t kPtRows = 128;      // query rows per CTA (TMEM lanes)
 constexpr uint32_t kPtTile = 64;       // positions per K/V tile
 constexpr uint32_t kPtThreads = 224;   // softmax warps 0-3, K and V TMA warps 4 and 6, MMA 5
 constexpr uint32_t kPtTmemCols = 256;  // S buffers at columns 0 and 64, O from column 128
-constexpr float kPtRescale = 8.0f;     // O is rescaled when a row's max grows by more
+// Scores are kept in base 2 (Q is pre-scaled by log2(e) / sqrt(head)), so P = 2^(s - m) is
+// e^(score - max) exactly as the softmax defines it; O is rescaled when a row's max grows by
+// more than kPtRescale (in base-2 units: P stays below 2^kPtRescale).
+constexpr float kPtLog2e = 1.4426950408889634f;
+constexpr float kPtRescale = 11.5f;
 
 // K and V tiles stream through separate rings: a K tile is free once its scores are computed,
 // long before the P.V that frees its V tile, so the next K tiles never wait behind a softmax.
@@ -158,7 +162,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             }
         }
         // Q (pre-scaled) as the K-major A operand, bf16 high and low parts
-        const float qs = 1.0f / sqrtf((float)HD);
+        const float qs = kPtLog2e / sqrtf((float)HD);
 #pragma unroll
         for (uint32_t kb = 0; kb < NBOX; kb++) {
 #pragma unroll
@@ -299,28 +303,34 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&s_free[i % 2]));
             const int32_t t0 = (int32_t)(i * kPtTile);
-            float mx = -INFINITY;
+            // only a tile that reaches past the row's position needs the causal mask
+            if (t0 + (int32_t)kPtTile - 1 > lim) {
 #pragma unroll
-            for (uint32_t j = 0; j < kPtTile; j++) {
-                if (t0 + (int32_t)j > lim) sv[j] = -INFINITY;
-                mx = fmaxf(mx, sv[j]);
+                for (uint32_t j = 0; j < kPtTile; j++)
+                    if (t0 + (int32_t)j > lim) sv[j] = -INFINITY;
             }
+            float mx = sv[0];
+#pragma unroll
+            for (uint32_t j = 1; j < kPtTile; j++) mx = fmaxf(mx, sv[j]);
             float alpha = 1.0f;
             bool rescale = false;
             if (mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + kPtRescale)) {
                 if (m_ref != -INFINITY) {
-                    alpha = expf(m_ref - mx);
+                    alpha = exp2f(m_ref - mx);
                     rescale = true;
                 }
                 m_ref = mx;
             }
             float sum = 0.0f;
+            if (m_ref == -INFINITY) {  // nothing visible yet: P = 0
 #pragma unroll
-            for (uint32_t j = 0; j < kPtTile; j++) {
-                const float e = (m_ref == -INFINITY || sv[j] == -INFINITY) ? 0.0f
-                                                                           : expf(sv[j] - m_ref);
-                sv[j] = e;
-                sum += e;
+                for (uint32_t j = 0; j < kPtTile; j++) sv[j] = 0.0f;
+            } else {
+#pragma unroll
+                for (uint32_t j = 0; j < kPtTile; j++) {
+                    sv[j] = exp2f(sv[j] - m_ref);  // a masked score (-inf) gives 0
+                    sum += sv[j];
+                }
             }
             l = l * alpha + sum;
             // this P buffer is free once P.V of tile i - 2 has finished
