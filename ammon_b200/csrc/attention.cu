@@ -1227,6 +1227,8 @@ extern "C" int ab_kernel_attention_decode(ab_scheme* s, ab_tensor q, ab_tensor k
                                                  s->rt->sm_count);
         uint64_t floats = 0, tickets = 0;
         attention_scratch_size(p.batch, p.heads, p.head, p.nsplit, &floats, &tickets);
+        // room for the prompt kernel's two halves too (rows over one shared cache)
+        floats = std::max<uint64_t>(floats, (uint64_t)p.batch * p.heads * 2 * (p.head + 2));
         tickets = (uint64_t)p.batch * p.kv_heads;
         s->rt->activate();
         void* part = nullptr;
@@ -1244,6 +1246,7 @@ extern "C" int ab_kernel_attention_decode(ab_scheme* s, ab_tensor q, ab_tensor k
         p.part_o = (float*)part;
         p.part_ml = (float*)part + (uint64_t)p.batch * p.heads * p.nsplit * p.head;
         p.counters = (uint32_t*)counters;
+        p.part_cap = floats;
         p.flags = s->rt->flags;
         record_attention(s, "attn_decode", p);
     });

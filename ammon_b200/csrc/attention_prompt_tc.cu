@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     __shared__ __align__(8) uint64_t k_full[S], k_empty[S], v_full[S], v_empty[S];
     __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], done_bar;
     __shared__ uint32_t sm_tmem, sm_end;
-    __shared__ int sm_fail;
+    __shared__ int sm_fail, sm_last;
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -191,7 +191,13 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm_tmem;
-    const uint32_t ntiles = (sm_end + kPtTile - 1) / kPtTile;
+    // gridDim.z CTAs (1 or 2) split the row block's tiles: this one takes [t_lo, t_lo + ntiles)
+    const uint32_t halves = gridDim.z, nt_all = (sm_end + kPtTile - 1) / kPtTile;
+    const uint32_t h_tiles = (nt_all + halves - 1) / halves;
+    const uint32_t t_lo = min(nt_all, blockIdx.z * h_tiles);
+    const uint32_t ntiles = min(nt_all, t_lo + h_tiles) - t_lo;
+    float m_ref = -INFINITY, l = 0.0f;        // softmax rows: running max (base 2) and sum
+    const uint32_t lane_base = (warp * 32u) << 16;
 
     if (warp == 4 || warp == 6) {
         // ---- TMA: warp 4 streams the K tiles, warp 6 the V tiles (64 positions each) ----
@@ -216,7 +222,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 for (uint32_t j = 0; j < NBOX; j++) {
                     // whole tiles: rows past seq read the zero fill, rows past a query's
                     // position are masked by its causal limit
-                    const int32_t x = (int32_t)(kvh * HD + j * 64), y = (int32_t)(i * kPtTile);
+                    const int32_t x = (int32_t)(kvh * HD + j * 64);
+                    const int32_t y = (int32_t)((t_lo + i) * kPtTile);
                     tma_load_2d(ring + s * LY::kTile + j * kPtTile * 128, map, x, y, bar);
                 }
                 issued++;
@@ -286,8 +293,6 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         if (lane == 0) tc_commit(smem_u32(&done_bar));  // every MMA this thread issued
     } else {
         // ---- softmax: thread = query row = TMEM lane ----
-        const uint32_t lane_base = (warp * 32u) << 16;
-        float m_ref = -INFINITY, l = 0.0f;
         bool ok = true;
         for (uint32_t i = 0; i < ntiles; i++) {
             // waits are per thread; the warp agrees on one outcome before its collective
@@ -302,7 +307,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 tmem_ld16(tmem + lane_base + (i % 2) * kPtTile + 16 * c, sv + 16 * c);
             tc_fence_before();
             mbar_arrive(smem_u32(&s_free[i % 2]));
-            const int32_t t0 = (int32_t)(i * kPtTile);
+            const int32_t t0 = (int32_t)((t_lo + i) * kPtTile);
             // only a tile that reaches past the row's position needs the causal mask
             if (t0 + (int32_t)kPtTile - 1 > lim) {
 #pragma unroll
@@ -375,21 +380,95 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             const uint32_t last = ntiles - 1;
             ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done[last % 2]),
                                                             (last / 2) & 1, p.flags));
-            if (ok) {
-                tc_fence_after();
-                const float inv = (lim >= 0 && l > 0.0f) ? 1.0f / l : 0.0f;
-                OT* dst = (OT*)p.out + orow * HD;
+            if (ok) tc_fence_after();
+        }
+        if (ok && halves == 1 && ntiles > 0) {
+            const float inv = (lim >= 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+            OT* dst = (OT*)p.out + orow * HD;
 #pragma unroll
-                for (uint32_t c = 0; c < HD / 16; c++) {
-                    float o[16];
-                    tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
-                    if (lim >= 0) pt_store16<OT>(dst + 16 * c, o, inv);
-                }
+            for (uint32_t c = 0; c < HD / 16; c++) {
+                float o[16];
+                tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
+                if (lim >= 0) pt_store16<OT>(dst + 16 * c, o, inv);
             }
+        } else if (ok && halves > 1) {
+            // this half's partial (O relative to its reference m_ref, m_ref, l) for the merge
+            float* po = p.part_o + (orow * halves + blockIdx.z) * HD;
+            float* pm = p.part_o + (uint64_t)p.batch * p.heads * halves * HD +
+                        (orow * halves + blockIdx.z) * 2;
+#pragma unroll
+            for (uint32_t c = 0; c < HD / 16; c++) {
+                float o[16];
+                if (ntiles > 0) {
+                    tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 16; k++) o[k] = 0.0f;
+                }
+                if (lim >= 0) pt_store16<float>(po + 16 * c, o, 1.0f);
+            }
+            if (lim >= 0) {
+                pm[0] = m_ref;
+                pm[1] = l;
+            }
+            __threadfence();
         }
         if (!ok) sm_fail = 1;
     }
     __syncthreads();
+    if (halves > 1) {
+        // the second CTA of the row block to finish merges both halves
+        if (tid == 0) {
+            int last = 0;
+            if (!sm_fail) {
+                __threadfence();
+                last = atomicAdd(p.counters + blockIdx.x * p.kv_heads + kvh, 1u) == halves - 1;
+            }
+            sm_last = last;
+        }
+        __syncthreads();
+        if (sm_last && warp < 4) {
+            __threadfence();
+            const uint32_t other = blockIdx.z ^ 1;
+            const float* po = p.part_o + (orow * halves + other) * HD;
+            const float* pm = p.part_o + (uint64_t)p.batch * p.heads * halves * HD +
+                              (orow * halves + other) * 2;
+            float m2 = -INFINITY, l2 = 0.0f;
+            if (lim >= 0) {
+                m2 = __ldcg(pm);
+                l2 = __ldcg(pm + 1);
+            }
+            const float m = fmaxf(m_ref, m2);
+            const float w1 = m_ref == -INFINITY ? 0.0f : exp2f(m_ref - m);
+            const float w2 = m2 == -INFINITY ? 0.0f : exp2f(m2 - m);
+            const float lt = l * w1 + l2 * w2;
+            const float inv = (lim >= 0 && lt > 0.0f) ? 1.0f / lt : 0.0f;
+            OT* dst = (OT*)p.out + orow * HD;
+#pragma unroll
+            for (uint32_t c = 0; c < HD / 16; c++) {
+                float o[16];
+                if (ntiles > 0) {
+                    tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 16; k++) o[k] = 0.0f;
+                }
+                if (lim >= 0) {
+#pragma unroll
+                    for (int k = 0; k < 16; k += 4) {
+                        const float4 b = __ldcg(reinterpret_cast<const float4*>(po + 16 * c + k));
+                        o[k] = o[k] * w1 + b.x * w2;
+                        o[k + 1] = o[k + 1] * w1 + b.y * w2;
+                        o[k + 2] = o[k + 2] * w1 + b.z * w2;
+                        o[k + 3] = o[k + 3] * w1 + b.w * w2;
+                    }
+                    pt_store16<OT>(dst + 16 * c, o, inv);
+                }
+            }
+        }
+        if (sm_last && tid == 0) p.counters[blockIdx.x * p.kv_heads + kvh] = 0;
+        __syncthreads();
+    }
     if (warp == 0) {
         if (sm_fail && lane == 0) atomicOr(p.flags, kFlagWaitTimeout);
         // every MMA has completed before the TMEM goes back
@@ -410,7 +489,11 @@ void pt_add(ab_scheme* s, const char* label, const AttnParams& p, const CUtensor
     auto kern = attn_prompt_tc_kernel<OT, G, HD>;
     const size_t smem = AttnPtLayout<HD>::smem();
     const uint32_t qp = kPtRows / G;
-    const dim3 grid((p.batch + qp - 1) / qp, p.kv_heads);
+    // two CTAs per row block (each half of the positions, merged by the second to finish)
+    // when the block's split scratch can hold the halves' partials
+    const uint64_t need = (uint64_t)p.batch * p.heads * 2 * (HD + 2);
+    const uint32_t halves = (p.part_o && p.counters && p.part_cap >= need) ? 2 : 1;
+    const dim3 grid((p.batch + qp - 1) / qp, p.kv_heads, halves);
     s->add(label, [=](cudaStream_t st) {
         cudaError_t e = pt_set_smem((const void*)kern, smem);
         if (e != cudaSuccess) return e;

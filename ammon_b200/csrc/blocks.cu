@@ -27,6 +27,7 @@ struct ab_attention_block {
     uint32_t hidden, heads, head, seq, max_batch;
     float theta;
     uint32_t nsplit_max;
+    uint64_t part_floats = 0;  // floats of `part`
     float* q = nullptr;         // [max_batch, heads * head] rotated queries
     void* attn_out = nullptr;   // [max_batch, heads * head] (f32 or bf16)
     float* part = nullptr;      // split partials
@@ -104,6 +105,7 @@ ab_attention_block* attention_block_new(ab_runtime* rt, uint32_t hidden, uint32_
         b->q = (float*)device_alloc(rt, max_batch * qd * 4);
         b->attn_out = device_alloc(rt, max_batch * qd * 4);
         b->part = (float*)device_alloc(rt, floats * 4);
+        b->part_floats = floats;
         b->counters = (uint32_t*)device_alloc(rt, counters * 4);
         if (tp) b->tp_y = (float*)device_alloc(rt, (size_t)max_batch * hidden * 4);
         alloc_tc_scratch(rt, &b->tc, max_batch, (uint32_t)std::max<uint64_t>(qd, hidden),
@@ -388,6 +390,7 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
         attention_scratch_size(batch, heads, head, nsplit, &floats, &counters);
         a.part_o = blk->part;
         a.part_ml = blk->part + (uint64_t)batch * heads * nsplit * head;
+        a.part_cap = blk->part_floats;
         a.counters = blk->counters;
         a.step = st;
         a.flags = flags;

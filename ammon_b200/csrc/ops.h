@@ -223,6 +223,7 @@ struct AttnParams {
     uint32_t min_chunk;  // fewest positions per split (a multiple of 64; 0 = 64)
     float* part_o;   // [B, KV, nsplit, g, hd]
     float* part_ml;  // [B, KV, nsplit, g, 2]
+    uint64_t part_cap;  // floats available from part_o on (0: unknown, no other layout used)
     uint32_t* counters;  // [B, KV], zero between launches
     const Step* step;
     uint32_t* flags;
