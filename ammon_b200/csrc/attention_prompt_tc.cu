@@ -37,7 +37,8 @@ namespace {
 
 constexpr uint32_t kPtRows = 128;      // query rows per CTA (TMEM lanes)
 constexpr uint32_t kPtTile = 64;       // positions per K/V tile
-constexpr uint32_t kPtThreads = 224;   // softmax warps 0-3, K and V TMA warps 4 and 6, MMA 5
+constexpr uint32_t kPtSoftmax = 256;   // softmax threads: two per row (warps 0-7)
+constexpr uint32_t kPtThreads = 352;   // + the K TMA warp 8, the MMA warp 9, the V TMA warp 10
 constexpr uint32_t kPtTmemCols = 256;  // S buffers at columns 0 and 64, O from column 128
 // Scores are kept in base 2 (Q is pre-scaled by log2(e) / sqrt(head)), so P = 2^(s - m) is
 // e^(score - max) exactly as the softmax defines it; O is rescaled when a row's max grows by
@@ -52,12 +53,16 @@ struct AttnPtLayout {
     static constexpr uint32_t kQBytes = kPtRows * HD * 2;        // Q hi, then Q lo
     static constexpr uint32_t kPBytes = kPtRows * kPtTile * 2;   // P hi, then P lo (16 KB)
     static constexpr uint32_t kTile = kPtTile * HD * 2;          // one K or V tile
-    static constexpr uint32_t kStages = HD == 128 ? 3 : 4;       // per ring
+    // a K tile is needed one tile ahead of its V tile and freed a softmax earlier: V gets the
+    // deeper ring
+    static constexpr uint32_t kKStages = HD == 128 ? 2 : 4;
+    static constexpr uint32_t kVStages = HD == 128 ? 3 : 4;
     static constexpr uint32_t kQOff = 0;
     static constexpr uint32_t kPOff = 2 * kQBytes;               // [2 buffers][hi, lo]
     static constexpr uint32_t kKOff = kPOff + 4 * kPBytes;
-    static constexpr uint32_t kVOff = kKOff + kStages * kTile;
-    static constexpr size_t smem() { return (size_t)kVOff + kStages * kTile + 1024; }
+    static constexpr uint32_t kVOff = kKOff + kKStages * kTile;
+    static constexpr uint32_t kRedOff = kVOff + kVStages * kTile;   // [6][128] f32
+    static constexpr size_t smem() { return (size_t)kRedOff + 6 * kPtRows * 4 + 1024; }
 };
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a K-major 128-byte-swizzled operand block
@@ -80,6 +85,19 @@ __device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t a, uint32_t 
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
                  "r"(d)
                  : "memory");
+}
+
+// Named barrier 1 of the 256 softmax threads that also ANDs a predicate over them: every
+// softmax thread takes the same barriers, and a failed wait anywhere stops all of them together.
+__device__ __forceinline__ bool softmax_sync_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kPtSoftmax)
+        : "memory");
+    return r != 0;
 }
 
 template <typename OT>
@@ -108,11 +126,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     attn_prompt_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap vmap) {
     using LY = AttnPtLayout<HD>;
-    constexpr uint32_t S = LY::kStages;
+    constexpr uint32_t SK = LY::kKStages, SV = LY::kVStages;
     constexpr uint32_t NBOX = HD / 64;     // 64-dimension boxes of a K or V row
     constexpr uint32_t QP = kPtRows / G;   // batch rows per CTA
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t k_full[S], k_empty[S], v_full[S], v_empty[S];
+    __shared__ __align__(8) uint64_t k_full[SK], k_empty[SK], v_full[SV], v_empty[SV];
     __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], done_bar;
     __shared__ uint32_t sm_tmem, sm_end;
     __shared__ int sm_fail, sm_last;
@@ -129,16 +147,18 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             if (pos < p.seq) e = max(e, pos + 1);
         }
         sm_end = e;
-        for (uint32_t i = 0; i < S; i++) {
+        for (uint32_t i = 0; i < SK; i++) {
             mbar_init(smem_u32(&k_full[i]), 1);
             mbar_init(smem_u32(&k_empty[i]), 1);
+        }
+        for (uint32_t i = 0; i < SV; i++) {
             mbar_init(smem_u32(&v_full[i]), 1);
             mbar_init(smem_u32(&v_empty[i]), 1);
         }
         for (uint32_t i = 0; i < 2; i++) {
             mbar_init(smem_u32(&s_full[i]), 1);
-            mbar_init(smem_u32(&s_free[i]), kPtRows);
-            mbar_init(smem_u32(&p_full[i]), kPtRows);
+            mbar_init(smem_u32(&s_free[i]), kPtSoftmax);
+            mbar_init(smem_u32(&p_full[i]), kPtSoftmax);
             mbar_init(smem_u32(&pv_done[i]), 1);
         }
         mbar_init(smem_u32(&done_bar), 1);
@@ -150,17 +170,19 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     // row r = tid (warps 0-3): batch row b0 + r / G, query head kvh * G + r % G
     int32_t lim = -1;  // last visible position (-1: no query)
     uint64_t orow = 0;
-    if (tid < kPtRows) {
-        const uint32_t b = b0 + tid / G;
-        const float* q = nullptr;
+    const float* q = nullptr;
+    if (tid < kPtSoftmax) {  // both softmax threads of a row need its limit and output row
+        const uint32_t r = tid % kPtRows, b = b0 + r / G;
         if (b < p.batch) {
             const uint32_t pos = p.step[b].position;
             if (pos < p.seq) {
                 lim = (int32_t)pos;
-                orow = (uint64_t)b * p.heads + (uint64_t)kvh * G + tid % G;
+                orow = (uint64_t)b * p.heads + (uint64_t)kvh * G + r % G;
                 q = p.q + orow * HD;
             }
         }
+    }
+    if (tid < kPtRows) {
         // Q (pre-scaled) as the K-major A operand, bf16 high and low parts
         const float qs = kPtLog2e / sqrtf((float)HD);
 #pragma unroll
@@ -199,10 +221,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     float m_ref = -INFINITY, l = 0.0f;        // softmax rows: running max (base 2) and sum
     const uint32_t lane_base = (warp * 32u) << 16;
 
-    if (warp == 4 || warp == 6) {
-        // ---- TMA: warp 4 streams the K tiles, warp 6 the V tiles (64 positions each) ----
+    if (warp == 8 || warp == 10) {
+        // ---- TMA: warp 8 streams the K tiles, warp 10 the V tiles (64 positions each) ----
         if (lane == 0) {
-            const bool kside = warp == 4;
+            const bool kside = warp == 8;
+            const uint32_t S = kside ? SK : SV;
             uint64_t* full = kside ? k_full : v_full;
             uint64_t* empty = kside ? k_empty : v_empty;
             const CUtensorMap* map = kside ? &kmap : &vmap;
@@ -232,15 +255,15 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (uint32_t j = issued > S ? issued - S : 0; j < issued; j++)
                 mbar_wait_bounded(smem_u32(&full[j % S]), (j / S) & 1, p.flags);
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ---- MMA: S(i + 1) = Q.K^T ahead of O += P(i).V ----
         if (lane == 0 && ntiles > 0) {
             const uint32_t idesc_s = tc_idesc_bf16(kPtRows, kPtTile);
             const uint32_t idesc_o = tc_idesc_bf16(kPtRows, HD) | kIdescBMajorMN;
             const uint32_t qhi = sbase + LY::kQOff, qlo = qhi + LY::kQBytes;
             auto issue_s = [&](uint32_t i) {
-                const uint32_t s = i % S;
-                if (!mbar_wait_bounded(smem_u32(&k_full[s]), (i / S) & 1, p.flags)) return false;
+                const uint32_t s = i % SK;
+                if (!mbar_wait_bounded(smem_u32(&k_full[s]), (i / SK) & 1, p.flags)) return false;
                 // the softmax warps have read this S buffer's previous tile
                 if (i >= 2 &&
                     !mbar_wait_bounded(smem_u32(&s_free[i % 2]), ((i - 2) / 2) & 1, p.flags))
@@ -269,14 +292,14 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                     ok = false;
                     break;
                 }
-                if (!mbar_wait_bounded(smem_u32(&v_full[i % S]), (i / S) & 1, p.flags) ||
+                if (!mbar_wait_bounded(smem_u32(&v_full[i % SV]), (i / SV) & 1, p.flags) ||
                     !mbar_wait_bounded(smem_u32(&p_full[i % 2]), (i / 2) & 1, p.flags)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t pb = sbase + LY::kPOff + (i % 2) * 2 * LY::kPBytes;
-                const uint32_t vst = sbase + LY::kVOff + (i % S) * LY::kTile;
+                const uint32_t vst = sbase + LY::kVOff + (i % SV) * LY::kTile;
                 const uint64_t ph = sw128_desc(pb), pl = sw128_desc(pb + LY::kPBytes);
 #pragma unroll
                 for (uint32_t k = 0; k < kPtTile / 16; k++) {
@@ -286,37 +309,47 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                     tc_mma_bf16(tmem + 128, pl + 2 * k, dv, idesc_o, 1);
                 }
                 tc_commit(smem_u32(&pv_done[i % 2]));
-                tc_commit(smem_u32(&v_empty[i % S]));
+                tc_commit(smem_u32(&v_empty[i % SV]));
             }
             if (!ok) sm_fail = 1;
         }
         if (lane == 0) tc_commit(smem_u32(&done_bar));  // every MMA this thread issued
-    } else {
-        // ---- softmax: thread = query row = TMEM lane ----
-        bool ok = true;
+    } else if (warp < 8) {
+        // ---- softmax: two threads per query row (TMEM lane = row); half 0 (warps 0-3) owns
+        // score columns 0-31 and O columns [0, HD/2), half 1 (warps 4-7) the rest ----
+        const uint32_t row = tid % kPtRows, hf = tid / kPtRows;
+        float* red = reinterpret_cast<float*>(smem + LY::kRedOff);  // [2 tiles][2 halves][128]
+        bool ok = true, failed = false;
+        float lh = 0.0f;  // this half's part of the row sum
         for (uint32_t i = 0; i < ntiles; i++) {
-            // waits are per thread; the warp agrees on one outcome before its collective
-            // tcgen05 loads and stores
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&s_full[i % 2]), (i / 2) & 1,
-                                                            p.flags));
-            if (!ok) break;
+            // every wait happens before the tile's barrier, which ANDs the outcomes: the
+            // softmax threads leave together (and the warps stay converged for tcgen05.ld/st)
+            bool w = mbar_wait_bounded(smem_u32(&s_full[i % 2]), (i / 2) & 1, p.flags);
+            // this tile's P buffer is free once P.V of tile i - 2 finished
+            if (i >= 2)
+                w = mbar_wait_bounded(smem_u32(&pv_done[i % 2]), ((i - 2) / 2) & 1, p.flags) &&
+                    w;
             tc_fence_after();
-            float sv[kPtTile];
+            float sv[kPtTile / 2];
 #pragma unroll
-            for (uint32_t c = 0; c < kPtTile / 16; c++)
-                tmem_ld16(tmem + lane_base + (i % 2) * kPtTile + 16 * c, sv + 16 * c);
+            for (uint32_t c = 0; c < kPtTile / 32; c++)
+                tmem_ld16(tmem + lane_base + (i % 2) * kPtTile + hf * 32 + 16 * c, sv + 16 * c);
             tc_fence_before();
             mbar_arrive(smem_u32(&s_free[i % 2]));
-            const int32_t t0 = (int32_t)((t_lo + i) * kPtTile);
+            const int32_t t0 = (int32_t)((t_lo + i) * kPtTile + hf * 32);
             // only a tile that reaches past the row's position needs the causal mask
-            if (t0 + (int32_t)kPtTile - 1 > lim) {
+            if (t0 + (int32_t)(kPtTile / 2) - 1 > lim) {
 #pragma unroll
-                for (uint32_t j = 0; j < kPtTile; j++)
+                for (uint32_t j = 0; j < kPtTile / 2; j++)
                     if (t0 + (int32_t)j > lim) sv[j] = -INFINITY;
             }
-            float mx = sv[0];
+            float pmx = sv[0];
 #pragma unroll
-            for (uint32_t j = 1; j < kPtTile; j++) mx = fmaxf(mx, sv[j]);
+            for (uint32_t j = 1; j < kPtTile / 2; j++) pmx = fmaxf(pmx, sv[j]);
+            red[((i & 1) * 2 + hf) * kPtRows + row] = pmx;
+            ok = softmax_sync_and(w && !failed);
+            if (!ok) break;
+            const float mx = fmaxf(pmx, red[((i & 1) * 2 + (hf ^ 1)) * kPtRows + row]);
             float alpha = 1.0f;
             bool rescale = false;
             if (mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + kPtRescale)) {
@@ -329,64 +362,71 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             float sum = 0.0f;
             if (m_ref == -INFINITY) {  // nothing visible yet: P = 0
 #pragma unroll
-                for (uint32_t j = 0; j < kPtTile; j++) sv[j] = 0.0f;
+                for (uint32_t j = 0; j < kPtTile / 2; j++) sv[j] = 0.0f;
             } else {
 #pragma unroll
-                for (uint32_t j = 0; j < kPtTile; j++) {
+                for (uint32_t j = 0; j < kPtTile / 2; j++) {
                     sv[j] = exp2f(sv[j] - m_ref);  // a masked score (-inf) gives 0
                     sum += sv[j];
                 }
             }
-            l = l * alpha + sum;
-            // this P buffer is free once P.V of tile i - 2 has finished
-            if (i >= 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done[i % 2]),
-                                                                ((i - 2) / 2) & 1, p.flags));
-                if (!ok) break;
-            }
-            if (__any_sync(0xffffffffu, rescale)) {
-                // O holds every earlier tile's P.V before it is scaled (alpha = 1 for rows that
-                // keep their reference)
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done[(i - 1) % 2]),
-                                                                ((i - 1) / 2) & 1, p.flags));
-                if (!ok) break;
+            lh = lh * alpha + sum;
+            // O holds every earlier tile's P.V before it is scaled: the rare tile that rescales
+            // waits for P.V of tile i - 1 (a warp whose wait runs out skips the scaling and
+            // fails the launch at the next barrier, so no softmax thread is left behind)
+            bool scale = __any_sync(0xffffffffu, rescale);
+            if (scale && i >= 1) {
+                scale = __all_sync(0xffffffffu,
+                                   mbar_wait_bounded(smem_u32(&pv_done[(i - 1) % 2]),
+                                                     ((i - 1) / 2) & 1, p.flags));
+                failed |= !scale;
                 tc_fence_after();
+            }
+            if (scale) {
+                // this half's O columns (alpha = 1 for rows that keep their reference)
 #pragma unroll
-                for (uint32_t c = 0; c < HD / 16; c++) {
+                for (uint32_t c = 0; c < HD / 32; c++) {
                     float o[16];
-                    tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
+                    const uint32_t col = 128 + hf * (HD / 2) + 16 * c;
+                    tmem_ld16(tmem + lane_base + col, o);
 #pragma unroll
                     for (int k = 0; k < 16; k++) o[k] *= alpha;
-                    tmem_st16(tmem + lane_base + 128 + 16 * c, o);
+                    tmem_st16(tmem + lane_base + col, o);
                 }
                 tmem_wait_st();
             }
-            // P (bf16 high and low parts) as the K-major A operand of the next P.V
+            // this half's P columns (bf16 high and low parts) as the K-major A operand
             const uint32_t pb = sbase + LY::kPOff + (i % 2) * 2 * LY::kPBytes;
 #pragma unroll
-            for (uint32_t c = 0; c < kPtTile / 8; c++) {
+            for (uint32_t c = 0; c < kPtTile / 16; c++) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int k = 0; k < 4; k++)
                     pt_split(sv[8 * c + 2 * k], sv[8 * c + 2 * k + 1], &hi[k], &lo[k]);
-                st_shared16(pb + sw_row_chunk(tid, c), hi[0], hi[1], hi[2], hi[3]);
-                st_shared16(pb + LY::kPBytes + sw_row_chunk(tid, c), lo[0], lo[1], lo[2], lo[3]);
+                const uint32_t off = sw_row_chunk(row, hf * (kPtTile / 16) + c);
+                st_shared16(pb + off, hi[0], hi[1], hi[2], hi[3]);
+                st_shared16(pb + LY::kPBytes + off, lo[0], lo[1], lo[2], lo[3]);
             }
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(smem_u32(&p_full[i % 2]));
         }
+        // the row sum from both halves; the last tile's P.V
+        bool w = true;
         if (ok && ntiles > 0) {
             const uint32_t last = ntiles - 1;
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done[last % 2]),
-                                                            (last / 2) & 1, p.flags));
-            if (ok) tc_fence_after();
+            w = mbar_wait_bounded(smem_u32(&pv_done[last % 2]), (last / 2) & 1, p.flags);
         }
+        red[(4 + hf) * kPtRows + row] = lh;
+        ok = softmax_sync_and(ok && w && !failed);
+        l = red[4 * kPtRows + row] + red[5 * kPtRows + row];
+        if (ok) tc_fence_after();
+        const uint32_t c0 = hf * (HD / 32);  // this half's 16-column chunks of O
         if (ok && halves == 1 && ntiles > 0) {
             const float inv = (lim >= 0 && l > 0.0f) ? 1.0f / l : 0.0f;
             OT* dst = (OT*)p.out + orow * HD;
 #pragma unroll
-            for (uint32_t c = 0; c < HD / 16; c++) {
+            for (uint32_t c = c0; c < c0 + HD / 32; c++) {
                 float o[16];
                 tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
                 if (lim >= 0) pt_store16<OT>(dst + 16 * c, o, inv);
@@ -397,7 +437,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             float* pm = p.part_o + (uint64_t)p.batch * p.heads * halves * HD +
                         (orow * halves + blockIdx.z) * 2;
 #pragma unroll
-            for (uint32_t c = 0; c < HD / 16; c++) {
+            for (uint32_t c = c0; c < c0 + HD / 32; c++) {
                 float o[16];
                 if (ntiles > 0) {
                     tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
@@ -407,7 +447,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 }
                 if (lim >= 0) pt_store16<float>(po + 16 * c, o, 1.0f);
             }
-            if (lim >= 0) {
+            if (lim >= 0 && hf == 0) {
                 pm[0] = m_ref;
                 pm[1] = l;
             }
@@ -427,7 +467,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             sm_last = last;
         }
         __syncthreads();
-        if (sm_last && warp < 4) {
+        if (sm_last && warp < 8) {
             __threadfence();
             const uint32_t other = blockIdx.z ^ 1;
             const float* po = p.part_o + (orow * halves + other) * HD;
@@ -444,8 +484,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             const float lt = l * w1 + l2 * w2;
             const float inv = (lim >= 0 && lt > 0.0f) ? 1.0f / lt : 0.0f;
             OT* dst = (OT*)p.out + orow * HD;
+            const uint32_t c0 = (tid / kPtRows) * (HD / 32);  // this half's chunks of O
 #pragma unroll
-            for (uint32_t c = 0; c < HD / 16; c++) {
+            for (uint32_t c = c0; c < c0 + HD / 32; c++) {
                 float o[16];
                 if (ntiles > 0) {
                     tmem_ld16(tmem + lane_base + 128 + 16 * c, o);
