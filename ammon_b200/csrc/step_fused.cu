@@ -17,11 +17,16 @@
 // Layout of the work:
 //  - Every GEMV phase splits its output rows (row pairs; (w1, w3) row pairs for gate/up) into
 //    one balanced contiguous range per CTA. A CTA's rows stream as chunks of up to 32 KB
-//    (four 4096-element bf16 rows, or one 14336-element w2 row) by cp.async.bulk row copies
-//    into ring slot g % 6; consumer warp w takes every chunk with g % 6 == w, computes its
-//    rows' dot products from shared memory (weights and the staged bf16 activation) and
-//    applies the epilogue of the phase: RoPE + K/V append (QKV), residual add (wo, w2),
-//    SwiGLU (gate/up), logits + running first maximum (classifier).
+//    (four 4096-element bf16 rows, one 14336-element w2 row, or up to four of the shorter w2
+//    rows of a tensor-parallel shard) by cp.async.bulk row copies into ring slot g % 6;
+//    consumer warp w takes every chunk with g % 6 == w, computes its rows' dot products from
+//    shared memory (weights and the staged bf16 activation) and applies the epilogue of the
+//    phase: RoPE + K/V append (QKV), residual add (wo, w2), SwiGLU (gate/up), logits + running
+//    first maximum (classifier).
+//  - Tensor parallelism (world > 1): the same kernel on every rank over its shards; wo and w2
+//    push their partial rows into every rank's exchange block as flag-carrying pairs, and CTA
+//    c sums, for the rows it produced (the same rows on every rank), the ranks' partials in
+//    rank order (tp_site_reduce) before a grid barrier publishes the new residual.
 //  - Attention (between QKV and wo) is flash-decoding over positions 0..pos: items of
 //    (kv head, block of 32-position tiles) sized to one wave of CTAs (see ps_attention).
 //  - Staging (the normalised activation, the attention output, the SwiGLU output, K/V tiles)
