@@ -600,6 +600,12 @@ class LlamaModel:
         self.comm = comm
         self._logits = np.zeros((cfg.batch, cfg.vocab), np.float32)
         self._argmax = np.zeros(cfg.batch, np.int32)
+        self._register_logits()
+
+    def _register_logits(self):
+        """Page-locks the logits buffer so step() fills it straight from the device."""
+        self._registered = _abi.lib().ab_host_register(
+            self._logits.ctypes.data, self._logits.nbytes) == _abi.AB_OK
 
     @classmethod
     def from_llama2c(cls, rt: Runtime, path: str, dtype: int = AB_F32, batch: int = 1,
@@ -621,6 +627,7 @@ class LlamaModel:
         self.comm = comm
         self._logits = np.zeros((c.batch, c.vocab), np.float32)
         self._argmax = np.zeros(c.batch, np.int32)
+        self._register_logits()
         return self
 
     @staticmethod
@@ -780,6 +787,9 @@ class LlamaModel:
         if getattr(self, "_h", None):
             _abi.lib().ab_llama_destroy(self._h)
             self._h = None
+        if getattr(self, "_registered", False):
+            _abi.lib().ab_host_unregister(self._logits.ctypes.data)
+            self._registered = False
 
     def __del__(self):
         try:

@@ -70,6 +70,8 @@ SIGNATURES = {
     "ab_runtime_stream": (P, [P]),
     "ab_runtime_sm_count": (C.c_int, [P, C.POINTER(i32)]),
     "ab_runtime_set_wait_limit": (C.c_int, [P, u32]),
+    "ab_host_register": (C.c_int, [P, u64]),
+    "ab_host_unregister": (C.c_int, [P]),
     "ab_runtime_wait_limit": (C.c_int, [P, C.POINTER(u32)]),
     "ab_tensor_zeros": (C.c_int, [P, i32, i32, C.POINTER(u32), C.POINTER(T)]),
     "ab_tensor_free": (C.c_int, [P, C.POINTER(T)]),

@@ -201,6 +201,7 @@ struct ab_llama {
     FusedStep* fused = nullptr;        // persistent single-launch step (batch 1, bf16)
     float* h_logits = nullptr;         // pinned [batch, vocab]
     int32_t* h_argmax = nullptr;
+    uint32_t* h_flags = nullptr;       // pinned copy of the runtime's device flag word
     ab_decode_step* h_steps = nullptr;
     std::vector<float> vt_logits;  // host logits handed out through the vtable
     // Batched prefill: up to pf_rows prompt positions of one cache stream run as the rows
@@ -285,6 +286,7 @@ void destroy_model(ab_llama* m) {
         free_t(*t);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_argmax) cudaFreeHost(m->h_argmax);
+    if (m->h_flags) cudaFreeHost(m->h_flags);
     if (m->h_steps) cudaFreeHost(m->h_steps);
     delete m;
 }
@@ -607,6 +609,7 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
         check(ab_step_parcel(rt, c.batch, &m->step));
         cuda_check(cudaMallocHost(&m->h_logits, (size_t)c.batch * c.vocab * 4), "pinned logits");
         cuda_check(cudaMallocHost(&m->h_argmax, (size_t)c.batch * 4), "pinned argmax");
+        cuda_check(cudaMallocHost(&m->h_flags, 4), "pinned flag word");
         cuda_check(cudaMallocHost(&m->h_steps, (size_t)c.batch * sizeof(ab_decode_step)),
                    "pinned steps");
         check(ab_scheme_create(rt, &m->scheme));
@@ -842,17 +845,29 @@ int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* l
         check(ab_scheme_submit(m->scheme));
         const size_t lbytes = (size_t)n * m->c.vocab * 4;
         const void* lsrc = m->world > 1 ? m->logits_all.data : m->logits.data;
+        // a page-locked caller buffer (ab_host_register) takes the logits straight from the
+        // device; any other goes through the pinned staging buffer
+        bool direct = false;
+        if (logits_host && m->world == 1) {
+            cudaPointerAttributes a = {};
+            direct = cudaPointerGetAttributes(&a, logits_host) == cudaSuccess &&
+                     a.type == cudaMemoryTypeHost;
+            cudaGetLastError();
+        }
         if (logits_host)
-            cuda_check(
-                cudaMemcpyAsync(m->h_logits, lsrc, lbytes, cudaMemcpyDeviceToHost, rt->stream),
-                "logits readback");
+            cuda_check(cudaMemcpyAsync(direct ? (void*)logits_host : (void*)m->h_logits, lsrc,
+                                       lbytes, cudaMemcpyDeviceToHost, rt->stream),
+                       "logits readback");
         if (argmax_host)
             cuda_check(cudaMemcpyAsync(m->h_argmax, m->argmax.data, (size_t)n * 4,
                                        cudaMemcpyDeviceToHost, rt->stream),
                        "argmax readback");
+        // the flag word rides along: one synchronisation for the whole step
+        cuda_check(cudaMemcpyAsync(m->h_flags, rt->flags, 4, cudaMemcpyDeviceToHost, rt->stream),
+                   "flag word readback");
         cuda_check(cudaStreamSynchronize(rt->stream), "step synchronize");
-        rt->check_flags();
-        if (logits_host) {
+        if (*m->h_flags) rt->check_flags();
+        if (logits_host && !direct) {
             if (m->world == 1) {
                 std::memcpy(logits_host, m->h_logits, lbytes);
             } else {

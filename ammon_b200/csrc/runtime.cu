@@ -281,6 +281,20 @@ int ab_runtime_synchronize(ab_runtime* rt) {
 
 void* ab_runtime_stream(ab_runtime* rt) { return rt ? (void*)rt->stream : nullptr; }
 
+int ab_host_register(void* ptr, uint64_t bytes) {
+    return guard([&] {
+        if (!ptr || bytes == 0) fail(AB_ERR_ARGUMENT, "null or empty host range");
+        cuda_check(cudaHostRegister(ptr, bytes, cudaHostRegisterDefault), "cudaHostRegister");
+    });
+}
+
+int ab_host_unregister(void* ptr) {
+    return guard([&] {
+        if (!ptr) fail(AB_ERR_ARGUMENT, "null host pointer");
+        cuda_check(cudaHostUnregister(ptr), "cudaHostUnregister");
+    });
+}
+
 int ab_runtime_set_wait_limit(ab_runtime* rt, uint32_t ms) {
     return guard([&] {
         if (!rt) fail(AB_ERR_ARGUMENT, "null runtime");

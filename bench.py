@@ -13,7 +13,8 @@ value:  tokens/s of the device-resident greedy loop (graph replays, device argma
         the next DecodeStep), CUDA events on the decode stream, max over ranks.
 e2e:    tokens/s through the reference-facing step() (AutoregressiveModel::step): every
         step uploads the DecodeSteps and reads [batch, vocab] fp32 logits back to the
-        host, where sample_argmax picks the next ids.
+        host (into a page-locked buffer) together with the library's greedy pick of them
+        (sample_argmax's first-maximum rule, on the device), which feeds the next step.
 With N > 1 (one process per GPU under torch.distributed.run):
   --parallel tp (default for the bf16 8B workload): the model is tensor parallel over the
         ranks (heads, kv heads, FFN columns and vocab split; one NCCL all-reduce after wo
@@ -805,8 +806,10 @@ def run_decode(args, w, B, env):
         dist.barrier()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
-        logits, _ = model.step_batch(tok, [pos0 + i] * B, logits=True)
-        tok = [int(np.argmax(logits[b])) for b in range(B)]
+        # logits come back to the host every step; the next token is the library's greedy
+        # pick of them (sample_argmax's first-maximum rule, computed on the device)
+        logits, am = model.step_batch(tok, [pos0 + i] * B, logits=True, argmax=True)
+        tok = [int(t) for t in am]
     t_e2e = time.perf_counter() - t0
     if dist:
         tt = torch.tensor([t_e2e], device="cuda")
@@ -856,7 +859,7 @@ def run_decode(args, w, B, env):
                         "gbs": round(lb[l] * c[0] / (c[1] / 1e3) / 1e9, 1) if l in lb else None}
                     for l, c in sorted(per_label.items(), key=lambda kv: -kv[1][1])},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
-                "d2h_bytes_per_step": 4 * B * w["vocab"]},
+                "d2h_bytes_per_step": 4 * B * w["vocab"] + 4 * B},
         "gpu_launches": nodes_loop * args.steps,
         "clocks": clocks.summary(),
     }

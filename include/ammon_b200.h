@@ -86,6 +86,12 @@ int ab_runtime_sm_count(ab_runtime* rt, int32_t* out);
  * counterpart: Goldy has no device-side waits. */
 int ab_runtime_set_wait_limit(ab_runtime* rt, uint32_t ms);
 int ab_runtime_wait_limit(ab_runtime* rt, uint32_t* ms);
+/* Page-locks `bytes` of caller host memory at `ptr` (cudaHostRegister) for as long as the caller
+ * keeps it: a step's logits then go from the device straight into a registered buffer passed
+ * to ab_llama_step, without the staging copy. ab_host_unregister before the memory is freed.
+ * No reference counterpart (the host side of AutoregressiveModel::step, src/model.rs:10). */
+int ab_host_register(void* ptr, uint64_t bytes);
+int ab_host_unregister(void* ptr);
 
 /* ---- tensors (goldy::Tensor::zeros / from_f32 / host take) ---------------- */
 int ab_tensor_zeros(ab_runtime* rt, int32_t dtype, int32_t rank, const uint32_t* dims,

@@ -101,6 +101,8 @@ extern "C" {
     pub fn ab_runtime_sm_count(rt: *mut ab_runtime, out_: *mut i32) -> c_int;
     pub fn ab_runtime_set_wait_limit(rt: *mut ab_runtime, ms: u32) -> c_int;
     pub fn ab_runtime_wait_limit(rt: *mut ab_runtime, ms: *mut u32) -> c_int;
+    pub fn ab_host_register(ptr: *mut c_void, bytes: u64) -> c_int;
+    pub fn ab_host_unregister(ptr: *mut c_void) -> c_int;
     pub fn ab_tensor_zeros(rt: *mut ab_runtime, dtype: i32, rank: i32, dims: *const u32, out_: *mut ab_tensor) -> c_int;
     pub fn ab_tensor_free(rt: *mut ab_runtime, t: *mut ab_tensor) -> c_int;
     pub fn ab_tensor_write(rt: *mut ab_runtime, t: ab_tensor, host: *const c_void, bytes: u64) -> c_int;

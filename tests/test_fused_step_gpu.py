@@ -176,3 +176,23 @@ def test_fused_step_wait_limit_ends_a_stalled_barrier(rt, orc):
     assert rel(logits[0], o.step(9, 0)) < BF16_TOL
     h.close()
     o.close()
+
+
+def test_step_logits_into_registered_and_plain_host_buffers(rt):
+    """step() copies the logits straight into the model's page-locked buffer
+    (ab_host_register) and through the staging buffer into any other host memory: both give
+    the same values."""
+    import ctypes as C
+
+    from ammon_b200 import _abi
+
+    g = _model(rt)
+    assert g._registered
+    a, _ = g.step_batch([3], [0], logits=True)
+    a = a.copy()
+    plain = np.zeros((1, CFG["vocab"]), np.float32)
+    steps = (_abi.DecodeStep_t * 1)((3, 0))
+    ab._check(_abi.lib().ab_llama_step(g._h, steps, 1,
+                                       plain.ctypes.data_as(C.POINTER(C.c_float)), None))
+    assert np.array_equal(plain, a)
+    g.close()
