@@ -134,7 +134,9 @@ static void allgather_host(ab_comm* c, const void* mine, void* all, size_t bytes
 
 bool comm_peers_setup(ab_comm* c, size_t max_elems) {
     if (c->peers) {
-        if (max_elems > c->max_elems) fail(AB_ERR_ARGUMENT, "peer buffers set up smaller");
+        if (max_elems > c->max_elems)
+            fail(AB_ERR_ARGUMENT, "peer buffers were set up for a narrower model on this "
+                                  "communicator");
         return true;
     }
     if (c->world < 2 || c->world > (int)kTpMaxWorld) return false;

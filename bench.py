@@ -23,6 +23,11 @@ With N > 1 (one process per GPU under torch.distributed.run):
   --parallel replicas (default for the fp32 workloads): every rank decodes its own batch
         of independent streams with no collective; value is the sum over ranks
         ("scaling": "weak").
+The default line also carries `batch64` (the same 8B decode at batch 64) and `configs`, the
+other BASELINE.json configurations, each with its own metric, unit, roofline and CPU
+baseline: the tiny fp32 decode, the 110M fp32 decode of 256 streams (split data-parallel
+over the ranks at N > 1, the only sub-record run there), and at N = 1 the split-attention,
+per-op and prefill microbenchmarks (`--workload attention|ops|prefill` run them alone).
 """
 from __future__ import annotations
 
@@ -399,8 +404,8 @@ def run_ops_micro(args):
         cpu = {"value": (rows * dim * 8 + dim * 4) / dt_s / 1e9, "unit": "GB/s", "cores": 1,
                "kind": "port", "sample": "oracle rmsnorm, 64 rows x 4096 f32, 50 repetitions"}
     line = _micro_line("ops", cases, peak, peak_kind, clocks.summary(), cpu)
-    print(json.dumps(line), flush=True)
     rt.close()
+    return line
 
 
 def run_attention_micro(args):
@@ -474,10 +479,10 @@ def run_attention_micro(args):
                                          "counted at 2 bytes per element"}
     line = _micro_line("attention", cases, peak, peak_kind, clocks.summary(), cpu,
                        {"parity": {"max_rel_err_vs_float64": worst, "tolerance": 1e-4}})
-    print(json.dumps(line), flush=True)
     kbuf.free()
     vbuf.free()
     rt.close()
+    return line
 
 
 def prefill_flops(w, P):
@@ -544,7 +549,7 @@ def run_prefill_micro(args):
                           "launches": launches}), flush=True)
         g.close()
         rt.close()
-        return
+        return None
     # the reference's way on the same kernels: one decode step per prompt token
     loop_n = 32
     rt.synchronize()
@@ -624,7 +629,7 @@ def run_prefill_micro(args):
             "kind": "port", "sample": "the reference feeds a prompt one decode step per token: "
                                       "full tokens (every layer, the full classifier) of the "
                                       f"oracle port at positions {pos}"}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def decode_config(w, B, first, last, world, mode):
@@ -673,6 +678,80 @@ def stream_assignment(w, batch, parallel, world, rank):
         per = batch // world
         return per, rank * per, True
     return batch, 0 if tp else rank * batch, False
+
+
+def cpu_decode_baseline(w, B, positions):
+    """cpu_baseline of a decode sub-record: full tokens of the oracle port (every layer, the
+    full classifier) at `positions`, the streams of a batch decoded one after another, so
+    the port's tokens/s is one over its mean token time whatever the batch."""
+    m, threads = cpu_port_model(w, max(positions) + 1)
+    S = cpu_streams_sampled(w, B)
+    times = []
+    for pos in positions:
+        times += cpu_token_times(m, [pos] * S)
+    m.close()
+    return {"value": 1.0 / statistics.mean(times), "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": f"full tokens (every layer, the full classifier) of the oracle port at "
+                      f"positions {positions}, {S} stream(s) each; the port decodes the "
+                      f"{B} streams of a step one after another"}
+
+
+# The other BASELINE.json configurations ride in the default line's `configs` object, each
+# with its own metric and unit: the tiny fp32 decode (128 tokens) and the 110M fp32 decode
+# of 256 streams (256 tokens; split data-parallel over the ranks at N > 1, no collective),
+# and at N = 1 the split-attention, per-op and prefill microbenchmarks.
+SUB_DECODES = (("tiny-llama-f32", 128), ("llama-110m-f32", 256))
+SUB_KEEP = ("value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scaling", "dtype",
+            "config", "step_bytes", "step_gbs", "step_frac", "roofline", "kernels", "e2e",
+            "gpu_launches", "clocks")
+
+
+def configs_wanted(args, w):
+    return batch64_wanted(args, w) and not args.no_configs
+
+
+def run_sub_decode(args, name, steps, env):
+    w = dict(WORKLOADS[name])
+    rank, world = env["rank"], env["world"]
+    per, sbase, split = stream_assignment(w, 0, "replicas", world, rank)
+    sub_args = argparse.Namespace(**vars(args))
+    sub_args.steps, sub_args.warmup, sub_args.e2e_steps = steps, 8, 0
+    env2 = dict(env, tp=False, split_streams=split, sbase=sbase, batch=per, comm=None)
+    line = run_decode(sub_args, w, per, env2, name=name)
+    sub = {"metric": "decode tokens/sec", **{k: line[k] for k in SUB_KEEP}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        first, last = timed_positions(w, sub_args)
+        sub["cpu_baseline"] = cpu_decode_baseline(w, per, [first, (first + last) // 2, last])
+    return sub
+
+
+def run_other_configs(args, env):
+    """The `configs` object of the default line. A sub-record that fails carries its error
+    instead of failing the headline line."""
+    out = {}
+    world = env["world"]
+    for name, steps in SUB_DECODES:
+        if world > 1 and not WORKLOADS[name].get("split_streams"):
+            continue  # one stream: nothing to partition over the ranks
+        try:
+            out[name] = run_sub_decode(args, name, steps, env)
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    if world > 1:
+        return out
+    for key, fn, steps in (("split-attention", run_attention_micro, 0),
+                           ("ops", run_ops_micro, 0), ("prefill", run_prefill_micro, 5)):
+        a = argparse.Namespace(**vars(args))
+        a.steps, a.warmup, a.layers, a.seq, a.no_parity = steps, 3, 0, 0, False
+        try:
+            sub = fn(a)
+            for k in ("n_gpus", "higher_is_better", "scaling", "vs_baseline", "data"):
+                sub.pop(k, None)
+            out[key] = sub
+        except Exception as e:  # noqa: BLE001
+            out[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    return out
 
 
 def batch64_wanted(args, w):
@@ -728,10 +807,10 @@ def run_reference(args, w, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def run_decode(args, w, B, env):
+def run_decode(args, w, B, env, name=None):
     """One decode line of the GPU arm at batch B (per rank): the device greedy loop timed
     between CUDA events (max over ranks), e2e through step(), per-kernel times and the
-    roofline of the dominant kernel."""
+    roofline of the dominant kernel. `name`: the workload's key (default: --workload)."""
     import numpy as np
     import torch
 
@@ -853,7 +932,8 @@ def run_decode(args, w, B, env):
                      "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,
                      "bytes_per_launch": lb.get(dom), "launch_ms": t_launch * 1e3,
-                     "traffic": profile_traffic(dom, args.workload + suffix, lb.get(dom))},
+                     "traffic": profile_traffic(dom, (name or args.workload) + suffix,
+                                                lb.get(dom))},
         "kernels": {l: {"launches": c[0], "ms": round(c[1], 4),
                         "share": round(c[1] / total_ms, 4),
                         "gbs": round(lb[l] * c[0] / (c[1] / 1e3) / 1e9, 1) if l in lb else None}
@@ -885,6 +965,9 @@ def main():
                          "streams are split over the ranks)")
     ap.add_argument("--no-batch64", action="store_true",
                     help="the default 8B line without its batch-64 sub-record")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="the default 8B line without its `configs` object (the other "
+                         "workloads and the kernel microbenchmarks)")
     ap.add_argument("--impl", default="ammon", choices=["ammon", "reference"])
     ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
                     help="N > 1: tensor parallel (8B default) or independent replicas")
@@ -906,8 +989,10 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "kernel microbenchmarks "
                               "report the oracle's CPU rate as cpu_baseline in the main arm"}))
             return
-        {"ops": run_ops_micro, "attention": run_attention_micro,
-         "prefill": run_prefill_micro}[args.workload](args)
+        line = {"ops": run_ops_micro, "attention": run_attention_micro,
+                "prefill": run_prefill_micro}[args.workload](args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
         return
     w = dict(WORKLOADS[args.workload])
     if args.layers:
@@ -967,6 +1052,8 @@ def main():
         line["batch64"] = {k: sub[k] for k in (
             "value", "unit", "ms_per_step", "config", "step_bytes", "step_gbs", "step_frac",
             "roofline", "kernels", "e2e", "gpu_launches", "clocks")}
+    if configs_wanted(args, w):
+        line["configs"] = run_other_configs(args, env)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         first, last = timed_positions(w, args)
         cpos = [first, (first + last) // 2, last]

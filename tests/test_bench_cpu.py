@@ -59,3 +59,24 @@ def test_reference_arm_prints_one_line():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "tokens/s"
     assert d["cpu_baseline"]["kind"] == "port" and d["e2e"]["value"] == d["value"]
+
+
+def test_sub_decodes_fit_their_contexts():
+    # the `configs` decodes of the default line: prompt, 8 warm-up steps, the timed steps and
+    # the e2e steps (min(steps, 64)) all stay inside each workload's KV cache
+    for name, steps in bench.SUB_DECODES:
+        w = bench.WORKLOADS[name]
+        need = w["prompt"] - 1 + 8 + steps + min(steps, 64) + 1
+        assert need <= w["seq"], (name, need)
+    # the 110M streams split over every rank count of the scaling run
+    w = bench.WORKLOADS["llama-110m-f32"]
+    for world in (1, 2, 4, 8):
+        per, first, split = bench.stream_assignment(w, 0, "replicas", world, world - 1)
+        assert per * world == 256 and first == 256 - per and split == (world > 1)
+
+
+def test_cpu_decode_baseline_on_the_tiny_workload():
+    w = bench.WORKLOADS["tiny-llama-f32"]
+    base = bench.cpu_decode_baseline(w, 1, [10, 20])
+    assert base["value"] > 0 and base["unit"] == "tokens/s" and base["kind"] == "port"
+    assert base["cores"] >= 1 and "[10, 20]" in base["sample"]

@@ -22,7 +22,7 @@ def _free_port():
 
 
 def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=False,
-            fused=None):
+            fused=None, first_batch=None):
     import datetime
 
     import torch
@@ -47,6 +47,15 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
             uid.copy_(torch.frombuffer(bytearray(ab.Comm.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         comm = ab.Comm(rt, bytes(uid.cpu().numpy().tobytes()), rank, world)
+        if first_batch is not None:
+            # an earlier model of another batch on the same communicator (as bench.py's
+            # batch-1 line before its batch-64 record): it sets up the peer slots first
+            first = ab.LlamaModel(rt, ab.LlamaConfig(**cfg_d, batch=first_batch,
+                                                     rope_theta=500000.0,
+                                                     dtype=ab.BF16 if bf16 else ab.F32), comm)
+            first.init_synthetic(17, 0.02)
+            first.step_batch([TOKENS[0]] * first_batch, [0] * first_batch, logits=False)
+            first.close()
         cfg = ab.LlamaConfig(**cfg_d, batch=batch, rope_theta=500000.0,
                              dtype=ab.BF16 if bf16 else ab.F32)
         if ckpt:  # every rank loads its own shard of one llama2.c file
@@ -97,7 +106,8 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
         dist.destroy_process_group()
 
 
-def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False, fused=None):
+def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False, fused=None,
+         first_batch=None):
     import torch
     import torch.multiprocessing as mp
 
@@ -107,7 +117,7 @@ def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False, fused=None):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg, ckpt,
-                                                    prefill, fused))
+                                                    prefill, fused, first_batch))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -185,4 +195,12 @@ def test_tensor_parallel_persistent_step_matches_oracle(world):
     graph = _run(True, 1, world, cfg, fused=False)
     for rank, worst, same, agree in graph:
         assert worst < 2e-2, (world, rank, worst)
+        assert same and agree
+
+
+def test_tensor_parallel_models_of_two_batches_share_a_communicator():
+    # a batch-1 model (peer all-reduce slots) then a batch-6 model (NCCL all-reduce) on one
+    # communicator: the second one is created and matches the oracle
+    for rank, worst, same, agree in _run(True, 6, first_batch=1):
+        assert worst < 2e-2, (rank, worst)
         assert same and agree
