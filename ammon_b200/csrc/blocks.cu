@@ -419,7 +419,7 @@ int ab_attention_block_record(ab_attention_block* blk, ab_scheme* s, ab_tensor x
                 // slots at GEMV batches, else through NCCL
                 o2.out = blk->tp_y;
                 o2.addend = comm_rank(blk->tp) == 0 ? (const float*)x.data : nullptr;
-                if (comm_has_peers(blk->tp) && batch <= kGemvMaxBatch) {
+                if (comm_has_peers(blk->tp) && batch <= kTpPeerMaxRows) {
                     const TpPush tgt = comm_push_target(blk->tp);
                     o2.out = tgt.out;
                     record_gemv(s, "attn_wo_partial", o2, wdt, batch, kProNone, kEpiStore);
@@ -523,7 +523,7 @@ int ab_swiglu_block_record(ab_swiglu_block* blk, ab_scheme* s, ab_tensor x,
             if (blk->tp) {
                 d.out = blk->tp_y;
                 d.addend = comm_rank(blk->tp) == 0 ? (const float*)x.data : nullptr;
-                if (comm_has_peers(blk->tp) && batch <= kGemvMaxBatch) {
+                if (comm_has_peers(blk->tp) && batch <= kTpPeerMaxRows) {
                     const TpPush tgt = comm_push_target(blk->tp);
                     d.out = tgt.out;
                     record_gemv(s, "ffn_down_partial", d, wdt, batch, kProNone, kEpiStore);

@@ -372,7 +372,9 @@ void record_tp_reduce(ab_scheme* s, const char* label, ab_comm* c, const TpPush&
     const uint64_t* ep = c->epoch;
     const uint32_t site = push.site, world = (uint32_t)c->world;
     uint32_t* err = c->rt->flags;
-    const unsigned grid = std::max(1u, std::min(32u, (n + 1023) / 1024));
+    // one float4 of every rank per thread: all of a batched step's peer loads in flight at
+    // once (up to 64 rows x 4096 = 256 CTAs); a batch-1 row takes 4 CTAs
+    const unsigned grid = std::max(1u, std::min(512u, (n + 1023) / 1024));
     s->add(label, [=](cudaStream_t st) {
         return launch(st, dim3(grid), dim3(256), 0, true, tp_reduce_kernel, srcs, flags, ep, site,
                       world, x, n, err);
@@ -578,7 +580,9 @@ int ab_comm_loopback_reduce(ab_runtime* rt, uint32_t world, uint32_t ready, uint
             srcs.src[r] = slots + (size_t)r * n;
             srcs.flag[r] = r == 0 ? arrivals : sinks + r;
         }
-        const unsigned grid = std::max(1u, std::min(32u, (n + 1023) / 1024));
+        // one float4 of every rank per thread: all of a batched step's peer loads in flight at
+    // once (up to 64 rows x 4096 = 256 CTAs); a batch-1 row takes 4 CTAs
+    const unsigned grid = std::max(1u, std::min(512u, (n + 1023) / 1024));
         cudaError_t e = cudaMemset(d, 0, bytes);
         if (e == cudaSuccess) e = cudaMemcpy(d, head.data(), head.size() * 8, cudaMemcpyHostToDevice);
         if (e == cudaSuccess)

@@ -586,12 +586,12 @@ ab_llama* create_model(ab_runtime* rt, const ab_llama_config* cfg, ab_comm* comm
             m->w3.push_back(alloc_t(rt, dt, {m->hidden_l, c.dim}));
         }
         check(ab_kvcache_create(rt, c.layers, c.seq, m->kv_l, c.head_dim, dt, c.batch, &m->cache));
-        // NVLink peer slots for the per-block row all-reduce. That path carries at most the
-        // GEMV's batch rows (batched steps and wider prefill passes take NCCL), so the slots
-        // depend on the width alone and every model of this width on the communicator shares
-        // them (collective; falls back to NCCL on every rank when a peer cannot be opened)
+        // NVLink peer slots for the per-block row all-reduce. That path carries at most
+        // kTpPeerMaxRows rows (wider steps and prefill passes take NCCL), so the slots depend
+        // on the width alone and every model of this width on the communicator shares them
+        // (collective; falls back to NCCL on every rank when a peer cannot be opened)
         if (comm && world > 1)
-            comm_peers_setup(comm, (size_t)kGemvMaxBatch * c.dim);
+            comm_peers_setup(comm, (size_t)kTpPeerMaxRows * c.dim);
         m->attn = attention_block_new(rt, c.dim, m->heads_l, c.head_dim, c.seq, c.batch,
                                       c.rope_theta, comm);
         m->ffn = swiglu_block_new(rt, c.dim, m->hidden_l, c.batch, comm);

@@ -90,6 +90,9 @@ struct GemvParams {
 // Largest batch the GEMV serves in one launch; above it the weights go to the tensor-core
 // GEMM (gemm_tc.cu): bf16 on the f16 pipe, fp32 as 3xTF32 on the tf32 pipe.
 constexpr uint32_t kGemvMaxBatch = 4;
+// Rows (batch rows or prefill-pass rows) up to which a tensor-parallel block sums the ranks'
+// partial projections with the NVLink peer all-reduce (tp_reduce); wider steps use NCCL.
+constexpr uint32_t kTpPeerMaxRows = 64;
 
 // Parameters of one tensor-core GEMM launch (gemm_tc.cu).
 struct GemmTcParams {

@@ -17,8 +17,9 @@ e2e:    tokens/s through the reference-facing step() (AutoregressiveModel::step)
         (sample_argmax's first-maximum rule, on the device), which feeds the next step.
 With N > 1 (one process per GPU under torch.distributed.run):
   --parallel tp (default for the bf16 8B workload): the model is tensor parallel over the
-        ranks (heads, kv heads, FFN columns and vocab split; one NCCL all-reduce after wo
-        and one after w2 per layer, captured in the step graph); all ranks decode the same
+        ranks (heads, kv heads, FFN columns and vocab split; one all-reduce after wo and one
+        after w2 per layer over NVLink: inside the persistent step at batch 1, the peer
+        all-reduce kernel up to 64 rows, NCCL beyond); all ranks decode the same
         batch, so value is that batch's tokens/s ("scaling": "strong").
   --parallel replicas (default for the fp32 workloads): every rank decodes its own batch
         of independent streams with no collective; value is the sum over ranks

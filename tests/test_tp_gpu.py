@@ -1,5 +1,6 @@
-"""Tensor parallelism on real GPUs: two ranks (one process per GPU) decode through NCCL
-all-reduces captured in the step graph, and every rank's logits and greedy ids match the
+"""Tensor parallelism on real GPUs: two ranks (one process per GPU) decode through the
+NVLink peer all-reduce (steps of up to 64 rows) or NCCL's (forced, or wider steps) captured
+in the step graph, and every rank's logits and greedy ids match the
 CPU oracle's single-device model. Needs two visible GPUs (skipped otherwise)."""
 import os
 import socket
@@ -22,7 +23,7 @@ def _free_port():
 
 
 def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=False,
-            fused=None, first_batch=None):
+            fused=None, first_batch=None, env=None):
     import datetime
 
     import torch
@@ -33,6 +34,7 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
 
     cfg_d = cfg or CFG
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(env or {})
     if fused is not None:
         os.environ["AMMON_B200_FUSED_STEP"] = "1" if fused else "0"
     torch.cuda.set_device(rank)
@@ -68,8 +70,8 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
         if fused is not None:
             same &= ("decode_step" in model.scheme().node_labels()) == fused
         if prefill:
-            # the prompt in one pass of 6 rows (NCCL all-reduce), then in passes of 2 (peer
-            # all-reduce) over the same positions; then decode continues from the cache
+            # the prompt in one pass of 6 rows, then in passes of 2 over the same positions
+            # (row all-reduces over the NVLink peer slots); then decode continues from the cache
             for want_pos, tok in enumerate(TOKENS):
                 want = ref.step(tok, want_pos)
             for rows in (0, 2):
@@ -107,7 +109,7 @@ def _worker(rank, world, port, bf16, batch, out, cfg=None, ckpt=None, prefill=Fa
 
 
 def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False, fused=None,
-         first_batch=None):
+         first_batch=None, env=None):
     import torch
     import torch.multiprocessing as mp
 
@@ -117,7 +119,7 @@ def _run(bf16, batch, world=2, cfg=None, ckpt=None, prefill=False, fused=None,
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, bf16, batch, q, cfg, ckpt,
-                                                    prefill, fused, first_batch))
+                                                    prefill, fused, first_batch, env))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -136,8 +138,11 @@ def test_tensor_parallel_fp32_matches_oracle():
         assert same and agree
 
 
-def test_tensor_parallel_bf16_batched_matches_oracle():
-    for rank, worst, same, agree in _run(True, 6):
+@pytest.mark.parametrize("nccl", [False, True])
+def test_tensor_parallel_bf16_batched_matches_oracle(nccl):
+    # batch 6: the NVLink peer all-reduce (up to 64 rows), or NCCL's when forced
+    env = {"AMMON_B200_TP_NCCL": "1"} if nccl else None
+    for rank, worst, same, agree in _run(True, 6, env=env):
         assert worst < 2e-2, (rank, worst)
         assert same and agree
 
@@ -145,7 +150,7 @@ def test_tensor_parallel_bf16_batched_matches_oracle():
 @pytest.mark.parametrize("world", [4, 8])
 def test_tensor_parallel_wide_matches_oracle(world):
     """Four or eight ranks (one kv head per rank at eight): the peer all-reduce with more
-    sources, at batch 1 (NVLink peer slots) and batch 6 (NCCL)."""
+    sources, at batch 1 and batch 6 (NVLink peer slots)."""
     for rank, worst, same, agree in _run(False, 1, world, CFG8):
         assert worst < 1e-5, (world, rank, worst)
         assert same and agree
@@ -168,8 +173,8 @@ def test_tensor_parallel_llama2c_shards_match_oracle(tmp_path):
 
 
 def test_tensor_parallel_prefill_matches_oracle():
-    """Sharded prefill passes (row all-reduces through NCCL at 6 rows, over the NVLink peer
-    slots at 2) leave every rank with the oracle's last-token logits and a cache the decode
+    """Sharded prefill passes (row all-reduces over the NVLink peer slots at 6 and at 2
+    rows) leave every rank with the oracle's last-token logits and a cache the decode
     continues from."""
     for rank, worst, same, _ in _run(False, 1, prefill=True):
         assert worst < 1e-5, (rank, worst)
@@ -199,8 +204,8 @@ def test_tensor_parallel_persistent_step_matches_oracle(world):
 
 
 def test_tensor_parallel_models_of_two_batches_share_a_communicator():
-    # a batch-1 model (peer all-reduce slots) then a batch-6 model (NCCL all-reduce) on one
-    # communicator: the second one is created and matches the oracle
+    # a batch-1 model then a batch-6 model on one communicator (the peer slots the first one
+    # set up serve both): the second one is created and matches the oracle
     for rank, worst, same, agree in _run(True, 6, first_batch=1):
         assert worst < 2e-2, (rank, worst)
         assert same and agree
