@@ -762,26 +762,39 @@ def batch64_wanted(args, w):
             and not args.no_batch64)
 
 
+# Tokens the reference arm times per batch: the work of a token depends on its position only,
+# so an evenly spaced sample of the timed positions stands for all of them and the arm ends in
+# well under a minute (an 8B token takes ~0.4 s on 16 host threads) while the GPUs wait.
+REF_SAMPLES = 12
+
+
+def reference_positions(first, last, steps):
+    """Evenly spaced sample (at most REF_SAMPLES, both ends included) of first..last."""
+    n = max(1, min(steps, REF_SAMPLES))
+    return sorted({first + (last - first) * i // max(n - 1, 1) for i in range(n)})
+
+
 def run_reference(args, w, rank, world):
     """The reference arm: the oracle port of the reference's per-token kernels on the host
-    cores, full tokens (every layer and the full classifier) at the positions the GPU arm
-    times, streams decoded one after another."""
+    cores, full tokens (every layer and the full classifier) at a sample of the positions the
+    GPU arm times, streams decoded one after another."""
     if rank != 0:
         return
     first, last = timed_positions(w, args)
-    positions = list(range(first - args.warmup, last + 1))
+    positions = reference_positions(first, last, args.steps)
     m, threads = cpu_port_model(w, last + 1)
     mode = parallel_mode(w, args, world)
+    cpu_token_times(m, [first - 1])  # untimed warm-up token
 
     def arm(B):
         S = cpu_streams_sampled(w, B)
         steps = []
         for pos in positions:
             steps.append(sum(cpu_token_times(m, [pos] * S)) * B / S)
-        timed = steps[args.warmup:]
-        step_s = statistics.mean(timed)
+        step_s = statistics.mean(steps)
         value = B / step_s
-        sample = (f"full tokens of the oracle port at positions {first}..{last}, "
+        sample = (f"full tokens of the oracle port at {len(positions)} positions evenly "
+                  f"spaced over {first}..{last}, "
                   + ("one stream per step" if S == 1 else f"{S} streams per step")
                   + (f", scaled to the batch's {B} streams (decoded one after another)"
                      if S < B else ""))

@@ -80,3 +80,12 @@ def test_cpu_decode_baseline_on_the_tiny_workload():
     base = bench.cpu_decode_baseline(w, 1, [10, 20])
     assert base["value"] > 0 and base["unit"] == "tokens/s" and base["kind"] == "port"
     assert base["cores"] >= 1 and "[10, 20]" in base["sample"]
+
+
+def test_reference_positions_sample_the_timed_range():
+    # the default 8B run: positions 135..390, twelve tokens timed, both ends included
+    p = bench.reference_positions(135, 390, 256)
+    assert len(p) == bench.REF_SAMPLES and p[0] == 135 and p[-1] == 390
+    assert p == sorted(set(p)) and all(135 <= x <= 390 for x in p)
+    assert bench.reference_positions(10, 11, 2) == [10, 11]
+    assert bench.reference_positions(7, 7, 1) == [7]
