@@ -112,6 +112,10 @@ enum DeviceFlag : uint32_t {
 // "device reported: ..." text for a non-zero flag word.
 std::string device_flag_message(uint32_t flags);
 
+// Whether [p, p + bytes) lies inside one host range page-locked through ab_host_register (and
+// not yet unregistered): only such a range takes a device copy without the staging buffer.
+bool host_range_registered(const void* p, size_t bytes);
+
 // ---- schemes -------------------------------------------------------------------------
 using LaunchFn = std::function<cudaError_t(cudaStream_t)>;
 

@@ -846,16 +846,12 @@ int ab_llama_step(ab_llama* m, const ab_decode_step* steps, uint32_t n, float* l
         check(ab_scheme_submit(m->scheme));
         const size_t lbytes = (size_t)n * m->c.vocab * 4;
         const void* lsrc = m->world > 1 ? m->logits_all.data : m->logits.data;
-        // a page-locked caller buffer (ab_host_register) takes the logits straight from the
-        // device (under tensor parallelism too at batch 1, where the gathered [rank][vocab
-        // slice] rows are already [vocab]); any other goes through the pinned staging buffer
-        bool direct = false;
-        if (logits_host && (m->world == 1 || n == 1)) {
-            cudaPointerAttributes a = {};
-            direct = cudaPointerGetAttributes(&a, logits_host) == cudaSuccess &&
-                     a.type == cudaMemoryTypeHost;
-            cudaGetLastError();
-        }
+        // a caller buffer page-locked through ab_host_register over the whole copy takes the
+        // logits straight from the device (under tensor parallelism too at batch 1, where the
+        // gathered [rank][vocab slice] rows are already [vocab]); any other goes through the
+        // pinned staging buffer
+        const bool direct = logits_host && (m->world == 1 || n == 1) &&
+                            host_range_registered(logits_host, lbytes);
         if (logits_host)
             cuda_check(cudaMemcpyAsync(direct ? (void*)logits_host : (void*)m->h_logits, lsrc,
                                        lbytes, cudaMemcpyDeviceToHost, rt->stream),

@@ -8,7 +8,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <sstream>
+#include <vector>
 
 #include <cudaTypedefs.h>
 
@@ -216,6 +218,19 @@ void fill_normal_region(Runtime* rt, ab_tensor t, uint64_t seed, uint64_t stream
     cuda_check(cudaGetLastError(), "fill_normal_region launch");
 }
 
+// Host ranges page-locked by ab_host_register: (start, bytes), in registration order.
+static std::mutex g_host_ranges_mu;
+static std::vector<std::pair<uintptr_t, size_t>> g_host_ranges;
+
+bool host_range_registered(const void* p, size_t bytes) {
+    const uintptr_t a = (uintptr_t)p;
+    std::lock_guard<std::mutex> lock(g_host_ranges_mu);
+    for (const auto& r : g_host_ranges)
+        if (a >= r.first && a - r.first <= r.second && bytes <= r.second - (a - r.first))
+            return true;
+    return false;
+}
+
 }  // namespace ab
 
 using namespace ab;
@@ -285,12 +300,23 @@ int ab_host_register(void* ptr, uint64_t bytes) {
     return guard([&] {
         if (!ptr || bytes == 0) fail(AB_ERR_ARGUMENT, "null or empty host range");
         cuda_check(cudaHostRegister(ptr, bytes, cudaHostRegisterDefault), "cudaHostRegister");
+        std::lock_guard<std::mutex> lock(g_host_ranges_mu);
+        g_host_ranges.emplace_back((uintptr_t)ptr, (size_t)bytes);
     });
 }
 
 int ab_host_unregister(void* ptr) {
     return guard([&] {
         if (!ptr) fail(AB_ERR_ARGUMENT, "null host pointer");
+        {
+            // forget the range first: no later step copies into memory about to be unlocked
+            std::lock_guard<std::mutex> lock(g_host_ranges_mu);
+            for (size_t i = 0; i < g_host_ranges.size(); i++)
+                if (g_host_ranges[i].first == (uintptr_t)ptr) {
+                    g_host_ranges.erase(g_host_ranges.begin() + (long)i);
+                    break;
+                }
+        }
         cuda_check(cudaHostUnregister(ptr), "cudaHostUnregister");
     });
 }

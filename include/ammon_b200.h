@@ -87,9 +87,12 @@ int ab_runtime_sm_count(ab_runtime* rt, int32_t* out);
 int ab_runtime_set_wait_limit(ab_runtime* rt, uint32_t ms);
 int ab_runtime_wait_limit(ab_runtime* rt, uint32_t* ms);
 /* Page-locks `bytes` of caller host memory at `ptr` (cudaHostRegister) for as long as the caller
- * keeps it: a step's logits then go from the device straight into a registered buffer passed
- * to ab_llama_step, without the staging copy. ab_host_unregister before the memory is freed.
- * No reference counterpart (the host side of AutoregressiveModel::step, src/model.rs:10). */
+ * keeps it: when the whole logits copy of a step ([n, vocab] floats) lies inside one range
+ * registered here, ab_llama_step copies the logits from the device straight into it, without
+ * the staging copy; any other buffer still works through the staging copy.
+ * ab_host_unregister(ptr), with the `ptr` given to ab_host_register, before the memory is
+ * freed. No reference counterpart (the host side of AutoregressiveModel::step,
+ * src/model.rs:10). */
 int ab_host_register(void* ptr, uint64_t bytes);
 int ab_host_unregister(void* ptr);
 

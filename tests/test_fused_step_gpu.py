@@ -180,8 +180,8 @@ def test_fused_step_wait_limit_ends_a_stalled_barrier(rt, orc):
 
 def test_step_logits_into_registered_and_plain_host_buffers(rt):
     """step() copies the logits straight into the model's page-locked buffer
-    (ab_host_register) and through the staging buffer into any other host memory: both give
-    the same values."""
+    (ab_host_register) and through the staging buffer into any other host memory, including
+    memory registered over less than the copy: all give the same values."""
     import ctypes as C
 
     from ammon_b200 import _abi
@@ -195,4 +195,14 @@ def test_step_logits_into_registered_and_plain_host_buffers(rt):
     ab._check(_abi.lib().ab_llama_step(g._h, steps, 1,
                                        plain.ctypes.data_as(C.POINTER(C.c_float)), None))
     assert np.array_equal(plain, a)
+    # a buffer page-locked over its first half only: the copy does not fit the registered
+    # range, so it takes the staging buffer and still fills every logit
+    half = np.zeros((1, CFG["vocab"]), np.float32)
+    ab._check(_abi.lib().ab_host_register(half.ctypes.data, half.nbytes // 2))
+    try:
+        ab._check(_abi.lib().ab_llama_step(g._h, steps, 1,
+                                           half.ctypes.data_as(C.POINTER(C.c_float)), None))
+    finally:
+        ab._check(_abi.lib().ab_host_unregister(half.ctypes.data))
+    assert np.array_equal(half, a)
     g.close()
