@@ -89,3 +89,32 @@ def test_reference_positions_sample_the_timed_range():
     assert p == sorted(set(p)) and all(135 <= x <= 390 for x in p)
     assert bench.reference_positions(10, 11, 2) == [10, 11]
     assert bench.reference_positions(7, 7, 1) == [7]
+
+
+def test_other_configs_selection_and_errors(monkeypatch):
+    # stand-ins for the GPU runners: which sub-records run at N = 1 and N > 1, and a failing
+    # one reported in place instead of failing the line
+    import argparse
+
+    calls = []
+
+    def fake_decode(args, name, steps, env):
+        calls.append((name, steps, env["world"]))
+        if name == "tiny-llama-f32":
+            raise RuntimeError("boom")
+        return {"value": 1.0}
+
+    monkeypatch.setattr(bench, "run_sub_decode", fake_decode)
+    for fn in ("run_attention_micro", "run_ops_micro", "run_prefill_micro"):
+        monkeypatch.setattr(bench, fn, lambda a, fn=fn: {"value": 2.0, "n_gpus": 1,
+                                                          "steps": a.steps, "fn": fn})
+    args = argparse.Namespace(steps=256, warmup=8, layers=0, seq=0, no_parity=False,
+                              no_cpu_baseline=True, prompt_len=2048)
+    out = bench.run_other_configs(args, {"world": 1})
+    assert out["tiny-llama-f32"]["error"].startswith("RuntimeError: boom")
+    assert out["llama-110m-f32"] == {"value": 1.0}
+    assert out["prefill"]["steps"] == 5 and "n_gpus" not in out["prefill"]
+    assert set(out) == {"tiny-llama-f32", "llama-110m-f32", "split-attention", "ops", "prefill"}
+    calls.clear()
+    out = bench.run_other_configs(args, {"world": 4})
+    assert set(out) == {"llama-110m-f32"} and calls == [("llama-110m-f32", 256, 4)]
