@@ -638,6 +638,125 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const GemmTcParams
     }
 }
 
+// A residual k-split fold and the RMSNorm of the rows it updates, in one launch: the norm that
+// stages the next projection's operand reads the residual stream the fold just wrote, so
+// instead of a fold kernel and a norm kernel, one CTA per row b of x (1) folds the partials of
+// its row in split order and adds them to x (the arithmetic of
+// splitk_epilogue_kernel<kEpiResidual>), keeping the new row in shared memory, then (2) takes
+// its RMSNorm exactly as rmsnorm_rows_bf16_kernel / split_rows_tf32_kernel do (256 lanes, the
+// same order of sums), writing the bf16 operand or its exact tf32 halves.
+// Requirements (checked when recording): dim % 4 == 0, dim <= kFoldNormMaxDim, x rows of
+// stride dim, the fold's rows cover [0, dim).
+constexpr uint32_t kFoldNormThreads = 1024;
+constexpr uint32_t kFoldNormMaxDim = 8192;  // the row staged in shared memory (32 KB)
+
+template <typename WT, bool TF32>
+__global__ void __launch_bounds__(kFoldNormThreads)
+    splitk_residual_norm_kernel(const float* __restrict__ ws, uint32_t tiles, uint32_t bn,
+                                uint32_t ksplit, float* __restrict__ x, uint32_t dim,
+                                const WT* __restrict__ w, float eps, bf16* __restrict__ out,
+                                float* __restrict__ hi, float* __restrict__ lo) {
+    // the GEMM lets this kernel launch before its epilogue stored the partials: wait for it
+    pdl_wait();
+    __shared__ __align__(16) float xs[kFoldNormMaxDim];
+    __shared__ float red[8];
+    const uint32_t b = blockIdx.x;
+    float* xr = x + (uint64_t)b * dim;
+    const size_t stride = (size_t)tiles * bn * kTcBM;
+    // (1) thread -> 4 consecutive rows of one tile: a float4 of every split, summed in order
+    for (uint32_t k = threadIdx.x * 4; k < dim; k += kFoldNormThreads * 4) {
+        const uint32_t tile = k / kTcBM, r = k % kTcBM;
+        const float* base = ws + ((size_t)tile * bn + b) * kTcBM + r;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t sp = 0;
+        for (; sp + 4 <= ksplit; sp += 4) {  // four loads in flight, added in split order
+            const float4 a = __ldcg((const float4*)(base + sp * stride));
+            const float4 c = __ldcg((const float4*)(base + (sp + 1) * stride));
+            const float4 d = __ldcg((const float4*)(base + (sp + 2) * stride));
+            const float4 e = __ldcg((const float4*)(base + (sp + 3) * stride));
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+            acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
+            acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+            acc.x += e.x; acc.y += e.y; acc.z += e.z; acc.w += e.w;
+        }
+        for (; sp < ksplit; sp++) {
+            const float4 a = __ldcg((const float4*)(base + sp * stride));
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+        }
+        const float4 xo = *(const float4*)(xr + k);
+        const float4 xn = make_float4(xo.x + acc.x, xo.y + acc.y, xo.z + acc.z, xo.w + acc.w);
+        *(float4*)(xr + k) = xn;
+        *(float4*)(xs + k) = xn;
+    }
+    __syncthreads();
+    // (2) ss over the 256 lanes k = t, t + 256, ... then the eight warps in order
+    if (threadIdx.x < 256) {
+        float ss = 0.0f;
+        for (uint32_t k = threadIdx.x; k < dim; k += 256) ss = fmaf(xs[k], xs[k], ss);
+        ss = warp_sum(ss);
+        if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+    }
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += red[i];
+    const float scale = 1.0f / sqrtf(t / (float)dim + eps);
+    for (uint32_t k = threadIdx.x; k < dim; k += kFoldNormThreads) {
+        const float v = to_f32(w[k]) * (scale * xs[k]);
+        if (TF32) {
+            const float h = tf32_hi(v);
+            hi[(uint64_t)b * dim + k] = h;
+            lo[(uint64_t)b * dim + k] = v - h;
+        } else {
+            out[(uint64_t)b * dim + k] = __float2bfloat16_rn(v);
+        }
+    }
+    pdl_trigger();
+}
+
+// Fusion of a norm into the residual fold recorded just before it (AMMON_B200_FOLD_NORM=0
+// keeps them apart; read at each record, so one process can record either form).
+static bool fold_norm_enabled() {
+    const char* e = std::getenv("AMMON_B200_FOLD_NORM");
+    return !(e && e[0] == '0');
+}
+
+// The scheme's last node when it is a residual fold of exactly these rows of x (the rows the
+// norm about to be recorded reads), else null.
+static Node* fusable_fold(ab_scheme* s, const float* x, uint32_t x_stride, uint32_t rows,
+                          uint32_t dim) {
+    if (!fold_norm_enabled() || s->nodes.empty()) return nullptr;
+    Node& n = s->nodes.back();
+    const FoldInfo& f = n.fold;
+    if (f.x != x || f.x_stride != dim || x_stride != dim || f.nb != rows || f.n_rows != dim ||
+        (uint64_t)f.tiles * kTcBM < dim || dim % 4 || dim > kFoldNormMaxDim || f.ksplit < 2)
+        return nullptr;
+    return &n;
+}
+
+// Replaces the fold node's launch with the fused fold + norm (bf16 operand, or tf32 halves).
+template <typename WT>
+static void fuse_fold_norm(ab_scheme* s, Node* n, const char* label, const WT* w, float eps,
+                           uint32_t dim, bf16* out, float* hi, float* lo) {
+    const FoldInfo f = n->fold;
+    const bool tf32 = out == nullptr;
+    if (tf32)
+        n->launch = [=](cudaStream_t st) {
+            return launch(st, dim3(f.nb), dim3(kFoldNormThreads), 0, true,
+                          splitk_residual_norm_kernel<WT, true>, f.ws, f.tiles, f.bn, f.ksplit,
+                          f.x, dim, w, eps, (bf16*)nullptr, hi, lo);
+        };
+    else
+        n->launch = [=](cudaStream_t st) {
+            return launch(st, dim3(f.nb), dim3(kFoldNormThreads), 0, true,
+                          splitk_residual_norm_kernel<WT, false>, f.ws, f.tiles, f.bn, f.ksplit,
+                          f.x, dim, w, eps, out, (float*)nullptr, (float*)nullptr);
+        };
+    n->label += std::string("+") + label;
+    n->fold = FoldInfo{};
+    s->dirty = true;
+}
+
 GemmTcPlan gemm_tc_plan(uint32_t rows, uint32_t K, uint32_t batch, int sms, bool interleave,
                         bool f32) {
     GemmTcPlan pl = {};
@@ -766,9 +885,20 @@ static void add_gemm_tc(ab_scheme* s, const char* label, const GemmTcParams& p,
     if (p.ksplit > 1) {
         auto fold = splitk_epilogue_kernel<EPI>;
         dim3 fgrid(p.tiles, (p.bn + 7) / 8);
-        s->add((std::string(label) + "_splitk").c_str(), [=](cudaStream_t st) {
+        FoldInfo info;
+        if (EPI == kEpiResidual) {
+            info.ws = p.ws;
+            info.x = (float*)p.out;
+            info.tiles = p.tiles;
+            info.bn = p.bn;
+            info.ksplit = p.ksplit;
+            info.nb = p.nb;
+            info.n_rows = p.n_rows;
+            info.x_stride = p.out_stride;
+        }
+        s->add_fold((std::string(label) + "_splitk").c_str(), [=](cudaStream_t st) {
             return launch(st, fgrid, dim3(256), 0, true, fold, p);
-        });
+        }, info);
     }
 }
 
@@ -819,6 +949,15 @@ void record_gemm_tc(ab_scheme* s, const char* label, GemmTcParams p, int32_t wdt
 void record_split_rows_tf32(ab_scheme* s, const char* label, const float* x, uint32_t x_stride,
                             const void* norm_w, int32_t w_dtype, float* hi, float* lo,
                             uint32_t rows, uint32_t dim, float eps) {
+    if (norm_w) {
+        if (Node* n = fusable_fold(s, x, x_stride, rows, dim)) {
+            if (w_dtype == AB_F32)
+                fuse_fold_norm(s, n, label, (const float*)norm_w, eps, dim, nullptr, hi, lo);
+            else
+                fuse_fold_norm(s, n, label, (const bf16*)norm_w, eps, dim, nullptr, hi, lo);
+            return;
+        }
+    }
     if (!norm_w) {
         s->add(label, [=](cudaStream_t st) {
             return launch(st, dim3(rows), dim3(256), 0, true,
@@ -843,6 +982,13 @@ void record_split_rows_tf32(ab_scheme* s, const char* label, const float* x, uin
 void record_rmsnorm_rows_bf16(ab_scheme* s, const char* label, const float* x, const void* w,
                               int32_t w_dtype, void* out, uint32_t rows, uint32_t dim, float eps) {
     bf16* o = (bf16*)out;
+    if (Node* n = fusable_fold(s, x, dim, rows, dim)) {
+        if (w_dtype == AB_F32)
+            fuse_fold_norm(s, n, label, (const float*)w, eps, dim, o, nullptr, nullptr);
+        else
+            fuse_fold_norm(s, n, label, (const bf16*)w, eps, dim, o, nullptr, nullptr);
+        return;
+    }
     if (w_dtype == AB_F32) {
         const float* wp = (const float*)w;
         s->add(label, [=](cudaStream_t st) {

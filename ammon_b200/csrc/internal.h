@@ -119,9 +119,19 @@ bool host_range_registered(const void* p, size_t bytes);
 // ---- schemes -------------------------------------------------------------------------
 using LaunchFn = std::function<cudaError_t(cudaStream_t)>;
 
+// A recorded residual k-split fold: x[col * x_stride + r] += the sum over splits of
+// ws[split][tile][col][128] (rows r < n_rows, columns col < nb). Kept with its node so that an
+// RMSNorm of the same rows recorded right after it runs inside the fold (gemm_tc.cu).
+struct FoldInfo {
+    const float* ws = nullptr;
+    float* x = nullptr;  // null: the node is not such a fold
+    uint32_t tiles = 0, bn = 0, ksplit = 0, nb = 0, n_rows = 0, x_stride = 0;
+};
+
 struct Node {
     std::string label;
     LaunchFn launch;
+    FoldInfo fold;
 };
 
 struct Scheme {
@@ -137,7 +147,11 @@ struct Scheme {
     // (kernel entry points that need scratch of their own, e.g. ab_kernel_attention_decode)
     std::vector<void*> owned;
     void add(const char* label, LaunchFn fn) {
-        nodes.push_back(Node{label, std::move(fn)});
+        nodes.push_back(Node{label, std::move(fn), FoldInfo{}});
+        dirty = true;
+    }
+    void add_fold(const char* label, LaunchFn fn, const FoldInfo& fold) {
+        nodes.push_back(Node{label, std::move(fn), fold});
         dirty = true;
     }
     void release_graph();
