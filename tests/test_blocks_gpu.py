@@ -214,7 +214,9 @@ def test_batched_bf16_model_on_tensor_cores(rt, orc, batch):
             assert rel(logits[b], want) < BF16_TOL, (batch, pos, b, rel(logits[b], want))
         assert all(am[b] == int(np.argmax(logits[b])) for b in range(batch))
     labels = g.scheme().node_labels()
-    assert "attn_qkv_rope_norm" in labels and "ffn_gate_up_swiglu_norm" in labels
+    # the operand norms: standalone after the embedding, else inside the residual fold before
+    assert "attn_qkv_rope_norm" in labels
+    assert any(l.endswith("ffn_gate_up_swiglu_norm") for l in labels), labels
 
 
 @pytest.mark.parametrize("batch", [5, 32, 256])
@@ -241,7 +243,7 @@ def test_batched_fp32_model_on_tensor_cores(rt, orc, batch):
         assert all(am[b] == int(np.argmax(logits[b])) for b in range(batch))
     labels = g.scheme().node_labels()
     assert "attn_qkv_rope_split" in labels and "attn_wo_residual_split" in labels
-    assert "final_norm_classifier_split" in labels
+    assert any(l.endswith("final_norm_classifier_split") for l in labels), labels
 
 
 def test_device_greedy_loop_matches_host_loop(rt, orc):

@@ -146,7 +146,9 @@ def test_llama3_8b_shape_batch64_tensor_cores(rt, orc, oracle_8b):
     streams = [0, 1, 31, 63]
     _seed_caches(g, o, B, streams, seed=32)
     labels = g.scheme().node_labels()
-    assert "ffn_down_residual_splitk" in labels and "attn_qkv_rope_splitk" in labels, labels
+    # the w2 folds carry the next operand norm (the next layer's, then the classifier's)
+    assert any(l.startswith("ffn_down_residual_splitk") for l in labels), labels
+    assert "attn_qkv_rope_splitk" in labels, labels
     rng = np.random.default_rng(64)
     tokens = [int(t) for t in rng.integers(0, L8B["vocab"], B)]
     positions = [600 + b for b in range(B)]
